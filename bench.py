@@ -1,0 +1,342 @@
+"""
+Benchmark of Image-GS's rasterization training step on B200: forward + L1 backward steps/s and Gaussian-pixel evaluations/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3_1080p] [--impl ours|reference]
+
+A step (default workload: 1920x1080 RGB target, 20,000 Gaussians, 16x16 tiles, top-10) is projection -> prefix sum -> tile binning ->
+top-K forward -> L1 loss and gradient -> top-K backward -> projection backward, replayed from one CUDA graph with inputs resident in HBM
+(`value`). With N GPUs (torchrun, one process per GPU, NCCL for the barrier and the max over ranks) every rank renders its own independent
+image (weak scaling, no data-path communication). `e2e` runs the same step through the drop-in gsplat API with autograd, copying the
+Gaussian parameters host->device from pinned memory and reading the loss back every step. The L2 cache is flushed (a 256 MB write)
+between timed steps, outside the per-step CUDA-event intervals.
+
+`--impl reference` times the CPU restatement of the reference's path (the reference has no CPU implementation of its own) on the host's
+cores, on rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "image-gs_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from igs_b200 import workloads  # noqa: E402
+
+METRIC = "fwd+bwd raster steps/s at 1080p/20k (also Gaussian-pixel evals/s, % of HBM roofline)"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() in ("active", "1"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus and world > 1:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cpu_step_rate(wl, inp, min_seconds=10.0, max_steps=5):
+    """Steps/s of the CPU oracle (all host threads) over whole steps of the workload: (rate, threads, steps)."""
+    sys.path.insert(0, ROOT)
+    from oracle import cpu
+
+    threads = len(os.sched_getaffinity(0))
+    cpu.set_threads(threads)
+    args = [inp[k].numpy() for k in ("means", "scales", "rotations", "features", "target")]
+    cpu.train_step(*args, wl.height, wl.width)  # warm-up
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < max_steps and (steps == 0 or time.perf_counter() - t0 < min_seconds):
+        cpu.train_step(*args, wl.height, wl.width)
+        steps += 1
+    return steps / (time.perf_counter() - t0), threads, steps
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    inp = workloads.make_inputs(wl)
+    sys.path.insert(0, ROOT)
+    from oracle import cpu
+
+    threads = len(os.sched_getaffinity(0))
+    cpu.set_threads(threads)
+    a = [inp[k].numpy() for k in ("means", "scales", "rotations", "features", "target")]
+    for _ in range(args.warmup):
+        cpu.train_step(*a, wl.height, wl.width)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu.train_step(*a, wl.height, wl.width)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps / total
+    sample = f"{args.steps} whole {wl.width}x{wl.height} steps (N={wl.num_gaussians}) of the C restatement, {threads} threads, {cpu_model()}"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded sinusoid target, random Gaussians)",
+        "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels},
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU implementation of this path; this is the oracle's C restatement of its kernels",
+    }))
+
+
+def time_graph(graph, reps, flush):
+    """Mean ms of `reps` replays, each bracketed by CUDA events, with an L2 flush between replays."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    for i in range(reps):
+        flush.zero_()
+        starts[i].record()
+        graph.replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / reps
+
+
+def run_ours(args, wl):
+    from igs_b200 import pipeline
+
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    inp = workloads.make_inputs(wl, image_index=rank)
+    d = {k: v.to(device) for k, v in inp.items()}
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"])
+    graph = step.capture()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    num_isect = int(step.num_intersects.item())
+    if num_isect > step.capacity:
+        raise SystemExit(f"intersections {num_isect} exceed the capacity {step.capacity}")
+    evals = step.gaussian_pixel_evals()
+
+    barrier = (lambda: torch.distributed.barrier()) if world > 1 else (lambda: None)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            graph.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = torch.tensor([sum(ms)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+    ms_per_step = total_ms / args.steps
+    value = world * args.steps / (total_ms / 1e3)
+
+    # per-stage breakdown and the dominant kernel's roofline (graphs of single stages, same flush discipline)
+    stage_ms = {}
+    for s in pipeline.RasterStep.STAGES:
+        g = step.capture([s])
+        stage_ms[s.strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
+        del g
+    hbm_peak, peak_kind = peaks()
+    p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
+    fwd_bytes = p * (4 * c + 4 * k) + num_isect * 4 + n * 4 * (5 + c)
+    bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
+    dominant = max(("forward", "backward"), key=lambda s: stage_ms[s])
+    dom_ms = stage_ms[dominant]
+    dom_bytes = fwd_bytes if dominant == "forward" else bwd_bytes
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    step_bytes = (p * (8 * c + 8 * k) + n * 4 * (5 + 7 + 2 * (5 + c) + (5 + c) + 5 + 5) + num_isect * 4 * 5 + wl.num_tiles * 16)
+    loss_bytes = 12 * c * p
+
+    # end to end through the drop-in gsplat API (autograd), host -> device parameters and device -> host loss every step
+    e2e = run_e2e(args, wl, inp, device, step.capacity, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, threads, steps = cpu_step_rate(wl, inp)
+        cpu = {"value": rate, "unit": "steps/s", "cores": threads, "kind": "port",
+               "sample": f"{steps} whole {wl.width}x{wl.height} steps of the C restatement on {threads} threads ({cpu_model()})"}
+
+    if rank == 0:
+        clk = clocks.summary()
+        out = {
+            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded sinusoid target, random Gaussians; one independent image per GPU)",
+            "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
+                       "tile": 16, "top_k": 10, "intersections": num_isect, "capacity": step.capacity, "parallelism": f"dp{world} (independent images)",
+                       "l2": "flushed between timed steps (256 MB write outside the event intervals)", "graph": "one CUDA graph per step"},
+            "gaussian_pixel_evals_per_step": evals, "gaussian_pixel_evals_per_s": evals * value,
+            "stages_ms": stage_ms,
+            "roofline": {"bound": "hbm", "kernel": f"raster_{dominant}", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": dom_bytes,
+                         "kernel_ms": dom_ms},
+            "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
+                              "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
+                              "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
+            "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps, "clocks": clk,
+        }
+        print(json.dumps(out))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(args, wl, inp, device, capacity, world):
+    import torch.nn.functional as F
+
+    import gsplat
+
+    host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
+    target = inp["target"].to(device)
+    dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    tb = wl.tile_bounds
+
+    def one():
+        for k in dev:
+            dev[k].copy_(host[k], non_blocking=True)
+        means, scales, rots, feats = [dev[k].requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+        xys, radii, conics, hits = gsplat.project_gaussians_2d_scale_rot(means, scales, rots, wl.height, wl.width, tb)
+        img = gsplat.rasterize_gaussians_sum(xys, radii, conics, hits, feats, wl.height, wl.width, topk_norm=True, capacity=capacity)
+        img = img.permute(2, 0, 1).contiguous()
+        loss = F.l1_loss(img, target)
+        loss.backward()
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        for k in dev:
+            dev[k] = dev[k].detach()
+        return loss_host
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        one()
+        torch.cuda.current_stream().synchronize()  # the loss is read on the host every step
+        float(loss_host)
+    end.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    value = world * args.steps / (float(t.item()) / 1e3)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    return {"value": value, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+            "api": "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + F.l1_loss + backward"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="cfg3_1080p")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    wl = workloads.get_workload(args.workload)
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

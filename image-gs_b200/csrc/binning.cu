@@ -1,0 +1,262 @@
+// Tile binning: the inclusive prefix sum of the tiles hit per Gaussian (compute_cumulative_intersects, gsplat/gsplat/utils.py:96-115) and
+// the Gaussian IDs of every tile intersection sorted by tile (sort_intersects_by_tile, gsplat/gsplat/cuda/csrc/bindings.cu:106-167).
+//
+// The reference maps each intersection slot to its Gaussian by binary search, radix-sorts 32-bit tile keys with CUB (stable, so within a
+// tile the Gaussians are in increasing ID order) and finds the tile ranges in a third pass. Here the same order comes from a counting sort
+// on the tile grid, which needs no key buffer and no sort passes over all intersections:
+//   1. count:   one thread per Gaussian adds 1 to each tile of its footprint (only slots below the capacity, as the reference drops the
+//               intersections beyond it in Gaussian-major order),
+//   2. scan:    one CTA turns the per-tile counts into the tile ranges [start, end) (empty tiles (0, 0)) and per-tile write cursors,
+//   3. scatter: one thread per Gaussian claims a position in each of its tiles with an atomic cursor,
+//   4. order:   one warp per tile ranks its few entries (IDs are unique within a tile), restoring increasing Gaussian ID, and zero-fills the
+//               padding slots after the last intersection, as the reference's padding entries (key num_tiles, value 0) sort last.
+// Integer-only and deterministic; outputs are bit-identical to the reference for inputs whose tile counts come from the projection.
+#include "igs_common.cuh"
+
+namespace {
+
+using igs::kTile;
+
+constexpr int kScanThreads = 1024;
+
+// Tile rectangle of a pixel center and integer radius, as the projection computes it (helpers.cuh:11-43 of the reference)
+__device__ __forceinline__ void tile_rect(float cx, float cy, float radius, unsigned tiles_x, unsigned tiles_y, unsigned &x0, unsigned &y0,
+                                          unsigned &x1, unsigned &y1) {
+    const float tcx = cx / (float)kTile, tcy = cy / (float)kTile;
+    const float trx = radius / (float)kTile, try_ = radius / (float)kTile;
+    x0 = min((unsigned)max(0, (int)(tcx - trx)), tiles_x);
+    x1 = min((unsigned)max(0, (int)(tcx + trx + 1)), tiles_x);
+    y0 = min((unsigned)max(0, (int)(tcy - try_)), tiles_y);
+    y1 = min((unsigned)max(0, (int)(tcy + try_ + 1)), tiles_y);
+}
+
+// Inclusive block-wide scan of one value per thread (blockDim.x == kScanThreads); returns the inclusive prefix, *total gets the sum
+__device__ __forceinline__ int block_inclusive_scan(int v, int *warp_sums, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_sums[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (kScanThreads / 32) ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += n;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int result = v + (warp > 0 ? warp_sums[warp - 1] : 0);
+    *total = warp_sums[kScanThreads / 32 - 1];
+    __syncthreads();
+    return result;
+}
+
+// Inclusive int32 prefix sum (wrapping, as torch.cumsum in int32) by one CTA: thread t scans a contiguous run of per_thread elements
+__global__ void __launch_bounds__(kScanThreads) cumsum_kernel(const int n, const int *__restrict__ in, int *__restrict__ out,
+                                                              int *__restrict__ total_out) {
+    __shared__ int warp_sums[32];
+    const int per_thread = (n + kScanThreads - 1) / kScanThreads;
+    const int begin = min(n, (int)threadIdx.x * per_thread), end = min(n, begin + per_thread);
+    unsigned run = 0;
+    for (int i = begin; i < end; ++i) run += (unsigned)__ldg(&in[i]);
+    int total;
+    const int inclusive = block_inclusive_scan((int)run, warp_sums, &total);
+    unsigned acc = (unsigned)inclusive - run;
+    for (int i = begin; i < end; ++i) {
+        acc += (unsigned)__ldg(&in[i]);
+        out[i] = (int)acc;
+    }
+    if (threadIdx.x == 0 && total_out) *total_out = total;
+}
+
+// Slots of Gaussian g that fit below the capacity (the reference maps slot idx < min(capacity, total) only)
+__device__ __forceinline__ int kept_slots(const int *__restrict__ cum, int g, int capacity) {
+    const int base = g > 0 ? __ldg(&cum[g - 1]) : 0;
+    const int count = __ldg(&cum[g]) - base;
+    return max(0, min(count, capacity - base));
+}
+
+// Tile key of slot `local` of a Gaussian's footprint: row-major position in its tile rectangle (forward.cu:102-103 of the reference)
+__device__ __forceinline__ unsigned slot_tile(int local, unsigned x0, unsigned y0, unsigned width, unsigned tiles_x) {
+    return (y0 + (unsigned)local / width) * tiles_x + x0 + (unsigned)local % width;
+}
+
+__global__ void __launch_bounds__(256) count_kernel(const int n, const int capacity, const float2 *__restrict__ xys,
+                                                    const int *__restrict__ radii, const int *__restrict__ cum, const unsigned tiles_x,
+                                                    const unsigned tiles_y, int *__restrict__ tile_count) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const int kept = kept_slots(cum, g, capacity);
+    if (kept == 0) return;
+    const float2 xy = __ldg(&xys[g]);
+    unsigned x0, y0, x1, y1;
+    tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
+    const unsigned width = x1 - x0, num_tiles = tiles_x * tiles_y;
+    if (width == 0) return;
+    for (int local = 0; local < kept; ++local) {
+        const unsigned tile = slot_tile(local, x0, y0, width, tiles_x);
+        if (tile < num_tiles) atomicAdd(&tile_count[tile], 1);
+    }
+}
+
+// Exclusive scan of the tile counts by one CTA: tile_bins[t] = (start, end), (0, 0) for empty tiles; the counts become write cursors
+__global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const int num_tiles, int *__restrict__ tile_count,
+                                                                 int2 *__restrict__ tile_bins, int *__restrict__ total_out) {
+    __shared__ int warp_sums[32];
+    const int per_thread = (num_tiles + kScanThreads - 1) / kScanThreads;
+    const int begin = min(num_tiles, (int)threadIdx.x * per_thread), end = min(num_tiles, begin + per_thread);
+    int run = 0;
+    for (int t = begin; t < end; ++t) run += tile_count[t];
+    int total;
+    const int inclusive = block_inclusive_scan(run, warp_sums, &total);
+    int start = inclusive - run;
+    for (int t = begin; t < end; ++t) {
+        const int count = tile_count[t];
+        tile_bins[t] = count > 0 ? make_int2(start, start + count) : make_int2(0, 0);
+        tile_count[t] = start;
+        start += count;
+    }
+    if (threadIdx.x == 0) *total_out = total;
+}
+
+__global__ void __launch_bounds__(256) scatter_kernel(const int n, const int capacity, const float2 *__restrict__ xys,
+                                                      const int *__restrict__ radii, const int *__restrict__ cum, const unsigned tiles_x,
+                                                      const unsigned tiles_y, int *__restrict__ tile_cursor, int *__restrict__ unsorted) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const int kept = kept_slots(cum, g, capacity);
+    if (kept == 0) return;
+    const float2 xy = __ldg(&xys[g]);
+    unsigned x0, y0, x1, y1;
+    tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
+    const unsigned width = x1 - x0, num_tiles = tiles_x * tiles_y;
+    if (width == 0) return;
+    for (int local = 0; local < kept; ++local) {
+        const unsigned tile = slot_tile(local, x0, y0, width, tiles_x);
+        if (tile < num_tiles) unsorted[atomicAdd(&tile_cursor[tile], 1)] = g;
+    }
+}
+
+constexpr int kOrderWarps = 8;
+constexpr int kOrderStage = 1024;  // entries per warp staged in shared memory
+
+// One warp per tile: each entry's final position is the number of smaller IDs in its tile (IDs are unique within a tile). Lists up to 32
+// entries stay in registers, up to kOrderStage in shared memory, longer ones are ranked from global memory. Also zero-fills the padding
+// slots [total, capacity).
+__global__ void __launch_bounds__(kOrderWarps * 32) order_kernel(const int num_tiles, const int capacity, const int2 *__restrict__ tile_bins,
+                                                                 const int *__restrict__ unsorted, const int *__restrict__ total_in,
+                                                                 int *__restrict__ sorted) {
+    __shared__ int stage[kOrderWarps][kOrderStage];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tile = blockIdx.x * kOrderWarps + warp;
+
+    // padding after the last intersection
+    const int total = min(*total_in, capacity);
+    for (int i = total + blockIdx.x * blockDim.x + threadIdx.x; i < capacity; i += gridDim.x * blockDim.x) sorted[i] = 0;
+
+    if (tile >= num_tiles) return;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+    if (len <= 0) return;
+    const int *src = unsorted + range.x;
+    int *dst = sorted + range.x;
+    if (len <= 32) {
+        const int v = lane < len ? src[lane] : INT_MAX;
+        int rank = 0;
+        for (int j = 0; j < len; ++j) rank += __shfl_sync(0xffffffffu, v, j) < v;
+        if (lane < len) dst[rank] = v;
+    } else if (len <= kOrderStage) {
+        int *buf = stage[warp];
+        for (int j = lane; j < len; j += 32) buf[j] = src[j];
+        __syncwarp();
+        for (int e = lane; e < len; e += 32) {
+            const int v = buf[e];
+            int rank = 0;
+            for (int j = 0; j < len; ++j) rank += buf[j] < v;
+            dst[rank] = v;
+        }
+    } else {
+        for (int e = lane; e < len; e += 32) {
+            const int v = src[e];
+            int rank = 0;
+            for (int j = 0; j < len; ++j) rank += __ldg(&src[j]) < v;
+            dst[rank] = v;
+        }
+    }
+}
+
+size_t sort_workspace_bytes(int capacity, int num_tiles) {
+    // tile counts / cursors, the intersection total, and the unsorted IDs, each 256-byte aligned
+    auto round = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    return round(sizeof(int) * (size_t)num_tiles) + round(sizeof(int)) + round(sizeof(int) * (size_t)(capacity > 0 ? capacity : 0));
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t igs_cumsum_workspace(int n) { return 0; }
+
+int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *stream) {
+    IGS_REQUIRE(n >= 0, "igs_cumsum: negative size");
+    if (n == 0) {
+        if (total) return cudaMemsetAsync(total, 0, sizeof(int), igs::as_stream(stream)) == cudaSuccess ? IGS_OK : igs::check_launch("igs_cumsum");
+        return IGS_OK;
+    }
+    IGS_REQUIRE(num_tiles_hit && cum_tiles_hit, "igs_cumsum: null pointer");
+    cumsum_kernel<<<1, kScanThreads, 0, igs::as_stream(stream)>>>(n, num_tiles_hit, cum_tiles_hit, total);
+    return igs::check_launch("igs_cumsum");
+}
+
+size_t igs_sort_workspace(int capacity, int tiles_x, int tiles_y) { return sort_workspace_bytes(capacity, tiles_x * tiles_y); }
+
+int igs_sort_intersects(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                        int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace, size_t workspace_bytes,
+                        void *stream) {
+    IGS_REQUIRE(num_points >= 0 && tiles_x >= 0 && tiles_y >= 0, "igs_sort_intersects: negative size");
+    const int num_tiles = tiles_x * tiles_y;
+    cudaStream_t s = igs::as_stream(stream);
+    if (num_tiles == 0) return IGS_OK;
+    IGS_REQUIRE(tile_bins != nullptr, "igs_sort_intersects: null tile_bins");
+    IGS_REQUIRE(igs::aligned(tile_bins, 8), "igs_sort_intersects: tile_bins must be 8-byte aligned [T, 2] int32");
+    if (capacity <= 0) {
+        // the reference returns no intersections and zero tile ranges (bindings.cu:124-126)
+        if (cudaMemsetAsync(tile_bins, 0, sizeof(int) * 2 * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch("igs_sort_intersects");
+        return IGS_OK;
+    }
+    IGS_REQUIRE(gaussian_ids_sorted && workspace, "igs_sort_intersects: null pointer");
+    IGS_REQUIRE(workspace_bytes >= sort_workspace_bytes(capacity, num_tiles), "igs_sort_intersects: workspace too small (%zu < %zu)",
+                workspace_bytes, sort_workspace_bytes(capacity, num_tiles));
+    IGS_REQUIRE(num_points == 0 || (xys && radii && cum_tiles_hit), "igs_sort_intersects: null pointer");
+    IGS_REQUIRE(num_points == 0 || igs::aligned(xys, 8), "igs_sort_intersects: xys must be 8-byte aligned");
+
+    char *ws = static_cast<char *>(workspace);
+    int *tile_count = reinterpret_cast<int *>(ws);
+    ws += ((sizeof(int) * (size_t)num_tiles + 255) & ~(size_t)255);
+    int *total = reinterpret_cast<int *>(ws);
+    ws += 256;
+    int *unsorted = reinterpret_cast<int *>(ws);
+
+    if (cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch("igs_sort_intersects");
+    const int blocks = igs::ceil_div(num_points, 256);
+    if (num_points > 0) {
+        count_kernel<<<blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
+                                            (unsigned)tiles_x, (unsigned)tiles_y, tile_count);
+    }
+    tile_scan_kernel<<<1, kScanThreads, 0, s>>>(num_tiles, tile_count, reinterpret_cast<int2 *>(tile_bins), total);
+    if (num_points > 0) {
+        scatter_kernel<<<blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
+                                              (unsigned)tiles_x, (unsigned)tiles_y, tile_count, unsorted);
+    }
+    order_kernel<<<igs::ceil_div(num_tiles, kOrderWarps), kOrderWarps * 32, 0, s>>>(num_tiles, capacity,
+                                                                                    reinterpret_cast<const int2 *>(tile_bins), unsorted,
+                                                                                    total, gaussian_ids_sorted);
+    return igs::check_launch("igs_sort_intersects");
+}
+
+}  // extern "C"

@@ -1,0 +1,38 @@
+// Shared constants and host-side plumbing of the igs_b200 CUDA library: the compile-time constants of the rasterizer (16x16 tiles, top-10
+// lists, normalization epsilon, at most 12 channels; the reference fixes the same values in gsplat/gsplat/cuda/csrc/config.h:1-10), the
+// thread-local error message behind igs_last_error(), and launch checking that returns a status instead of exiting the process.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/igs_b200.h"
+
+namespace igs {
+
+constexpr int kTile = IGS_TILE;                 // pixels per tile side
+constexpr int kTilePixels = kTile * kTile;      // one CTA of the tile kernels, one thread per pixel
+constexpr int kTopK = IGS_TOP_K;                // Gaussians kept per pixel
+constexpr int kMaxChannels = IGS_MAX_CHANNELS;  // feature channels
+constexpr double kNormEps = 1e-4;               // added to the sum of the top-K weights (a double in the reference's forward pass)
+constexpr uint16_t kNoSlot = 0xFFFF;            // empty entry of the compact per-tile top-K lists
+
+// Record a printf-style message for igs_last_error() and return the status code
+int set_error(int status, const char *fmt, ...);
+
+// Status of the last launch on this thread: IGS_OK, or IGS_ERR_CUDA with the CUDA error recorded
+int check_launch(const char *what);
+
+inline cudaStream_t as_stream(void *stream) { return reinterpret_cast<cudaStream_t>(stream); }
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+inline bool aligned(const void *p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+}  // namespace igs
+
+#define IGS_REQUIRE(cond, ...)                                          \
+    do {                                                                \
+        if (!(cond)) return ::igs::set_error(IGS_ERR_INVALID, __VA_ARGS__); \
+    } while (0)

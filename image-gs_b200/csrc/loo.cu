@@ -1,0 +1,107 @@
+// Leave-one-out loss increase per Gaussian (topk_norm_loo_loss_increase, gsplat/gsplat/cuda/csrc/forward.cu:667-738; called once per
+// pruning round by compress/pruning.py:13-27): with the top-K weights w = exp(-sigma) of a pixel, S_w = sum_k w_k and S_f = sum_k w_k f_k,
+// removing slot k changes the pixel from S_f / (S_w + eps) to (S_f - w_k f_k) / (S_w - w_k + eps); the change of the pixel's absolute
+// (or squared) error summed over channels is added to that Gaussian.
+//
+// One thread per pixel over the [H, W, 10] lists; before the global atomics, each warp merges the additions of lanes that target the same
+// Gaussian in the same slot (neighbouring pixels mostly share their lists), one atomic per distinct Gaussian and slot instead of one per
+// lane. Compiled with --use_fast_math like the reference.
+#include "igs_common.cuh"
+
+namespace {
+
+using igs::kMaxChannels;
+using igs::kTopK;
+
+template <int C>
+__global__ void __launch_bounds__(256) loo_kernel(const int img_w, const int num_pixels, const int channels_rt, const float2 *__restrict__ xys,
+                                                  const float *__restrict__ conics, const float *__restrict__ colors,
+                                                  const int *__restrict__ pixel_topk, const float *__restrict__ targets, const bool squared,
+                                                  const float eps, float *__restrict__ loss_increase) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    const int channels = C > 0 ? C : channels_rt;
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = p < num_pixels;
+    const float px = valid ? (float)(p % img_w) : 0.f, py = valid ? (float)(p / img_w) : 0.f;
+    int ids[kTopK];
+    float w[kTopK];
+    float sum_w = 0.f, sum_f[kMaxC], target[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+        sum_f[c] = 0.f;
+        target[c] = (valid && c < channels) ? targets[(size_t)c * num_pixels + p] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const int g = valid ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        ids[k] = g;
+        w[k] = 0.f;
+        if (g < 0) continue;
+        const float2 xy = __ldg(&xys[g]);
+        const float a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), cc = __ldg(&conics[3 * g + 2]);
+        const float dx = xy.x - px, dy = xy.y - py;
+        w[k] = __expf(-(0.5f * (a * dx * dx + cc * dy * dy) + b * dx * dy));
+        sum_w += w[k];
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) sum_f[c] += w[k] * __ldg(&colors[(size_t)g * channels + c]);
+    }
+    float error = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+        if (c >= channels) continue;
+        const float diff = sum_f[c] / (sum_w + eps) - target[c];
+        error += squared ? diff * diff : fabsf(diff);
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const int g = ids[k];
+        float delta = 0.f;
+        if (g >= 0) {
+            const float inv = 1.f / (sum_w - w[k] + eps);
+            float loo = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) {
+                if (c >= channels) continue;
+                const float diff = (sum_f[c] - w[k] * __ldg(&colors[(size_t)g * channels + c])) * inv - target[c];
+                loo += squared ? diff * diff : fabsf(diff);
+            }
+            delta = loo - error;
+        }
+        // lanes with the same Gaussian in this slot add their deltas in one atomic
+        const unsigned peers = __match_any_sync(0xffffffffu, g);
+        const int leader = __ffs(peers) - 1;
+        float merged = 0.f;
+        for (unsigned m = peers; m; m &= m - 1) merged += __shfl_sync(peers, delta, __ffs(m) - 1);
+        if (g >= 0 && (int)(threadIdx.x & 31) == leader) atomicAdd(&loss_increase[g], merged);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
+                          const float *colors, const int32_t *pixel_topk, const float *targets, int squared, float eps,
+                          float *loss_increase, void *stream) {
+    IGS_REQUIRE(img_height >= 0 && img_width >= 0 && num_points >= 0, "igs_loo_loss_increase: negative size");
+    IGS_REQUIRE(channels >= 0 && channels <= kMaxChannels, "igs_loo_loss_increase: at most %d channels", kMaxChannels);
+    cudaStream_t s = igs::as_stream(stream);
+    if (num_points == 0) return IGS_OK;
+    IGS_REQUIRE(loss_increase, "igs_loo_loss_increase: null output");
+    if (cudaMemsetAsync(loss_increase, 0, sizeof(float) * (size_t)num_points, s) != cudaSuccess) return igs::check_launch("igs_loo_loss_increase");
+    const int num_pixels = img_height * img_width;
+    if (num_pixels == 0) return IGS_OK;
+    IGS_REQUIRE(xys && conics && (colors || channels == 0) && pixel_topk && (targets || channels == 0), "igs_loo_loss_increase: null pointer");
+    IGS_REQUIRE(igs::aligned(xys, 8), "igs_loo_loss_increase: xys must be 8-byte aligned");
+    const int blocks = igs::ceil_div(num_pixels, 256);
+    if (channels == 3)
+        loo_kernel<3><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, reinterpret_cast<const float2 *>(xys), conics, colors,
+                                             pixel_topk, targets, squared != 0, eps, loss_increase);
+    else
+        loo_kernel<0><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, reinterpret_cast<const float2 *>(xys), conics, colors,
+                                             pixel_topk, targets, squared != 0, eps, loss_increase);
+    return igs::check_launch("igs_loo_loss_increase");
+}
+
+}  // extern "C"

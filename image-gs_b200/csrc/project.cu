@@ -1,0 +1,184 @@
+// 2D projection of the Gaussians: pixel centers, conics (inverse covariances), 3-sigma radii and tile footprints, and the backward pass to
+// means, scales and rotations. Compiled with --use_fast_math like the reference extension (gsplat/setup.py:70), because the radius
+// ceil(3 sqrt(lambda_max)) and the tile bounding box decide the tile binning, which must agree with the reference bit for bit: the same
+// approximate sqrt / reciprocal / sin / cos and the same product order (glm's mat2 product, which the M2 helper below reproduces so that
+// the compiler contracts the same multiply-adds).
+//
+// One thread per Gaussian, parameters read as float2 vectors; every output element is written (the reference relies on zero-initialized
+// outputs instead), so callers need no memset.
+#include "igs_common.cuh"
+
+namespace {
+
+using igs::kTile;
+
+// 2x2 matrix stored [column][row]; product terms in glm's order: (a*b)[c][r] = a[0][r]*b[c][0] + a[1][r]*b[c][1]
+struct M2 {
+    float m[2][2];
+};
+
+__device__ __forceinline__ M2 mul(const M2 &a, const M2 &b) {
+    M2 o;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) o.m[c][r] = a.m[0][r] * b.m[c][0] + a.m[1][r] * b.m[c][1];
+    return o;
+}
+
+__device__ __forceinline__ M2 transpose(const M2 &a) {
+    M2 o;
+    o.m[0][0] = a.m[0][0];
+    o.m[0][1] = a.m[1][0];
+    o.m[1][0] = a.m[0][1];
+    o.m[1][1] = a.m[1][1];
+    return o;
+}
+
+// Rotation by theta as in helpers.cuh:265-276 (cos on the diagonal, [0][1] = -sin), and its derivative (helpers.cuh:278-289)
+__device__ __forceinline__ M2 rotation(float cs, float sn) { return M2{{{cs, -sn}, {sn, cs}}}; }
+__device__ __forceinline__ M2 rotation_grad(float cs, float sn) { return M2{{{-sn, -cs}, {cs, -sn}}}; }
+__device__ __forceinline__ M2 diag(float a, float b) { return M2{{{a, 0.f}, {0.f, b}}}; }
+
+// Tile rectangle [x0, x1) x [y0, y1) covered by a pixel center and radius, clamped to the grid (helpers.cuh:11-43)
+__device__ __forceinline__ void tile_rect(float cx, float cy, float radius, unsigned tiles_x, unsigned tiles_y, unsigned &x0, unsigned &y0,
+                                          unsigned &x1, unsigned &y1) {
+    const float tcx = cx / (float)kTile, tcy = cy / (float)kTile;
+    const float trx = radius / (float)kTile, try_ = radius / (float)kTile;
+    x0 = min((unsigned)max(0, (int)(tcx - trx)), tiles_x);
+    x1 = min((unsigned)max(0, (int)(tcx + trx + 1)), tiles_x);
+    y0 = min((unsigned)max(0, (int)(tcy - try_)), tiles_y);
+    y1 = min((unsigned)max(0, (int)(tcy + try_ + 1)), tiles_y);
+}
+
+__global__ void __launch_bounds__(256) project_fwd_kernel(const int n, const float2 *__restrict__ means, const float2 *__restrict__ scales,
+                                                          const float *__restrict__ rotations, const float img_w, const float img_h,
+                                                          const unsigned tiles_x, const unsigned tiles_y, float2 *__restrict__ xys,
+                                                          int *__restrict__ radii, float *__restrict__ conics, int *__restrict__ hits) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float2 mean = __ldg(&means[i]);
+    const float2 scale = __ldg(&scales[i]);
+    const float theta = __ldg(&rotations[i]);
+    const float cx = mean.x * img_w, cy = mean.y * img_h;
+    const M2 R = rotation(cosf(theta), sinf(theta));
+    const M2 M = mul(R, diag(scale.x, scale.y));
+    const M2 cov = mul(M, transpose(M));
+    const float a = cov.m[0][0], b = cov.m[0][1], c = cov.m[1][1];
+    const float det = a * c - b * b;
+
+    float2 xy = make_float2(0.f, 0.f);
+    float ca = 0.f, cb = 0.f, cc = 0.f;
+    int radius_px = 0, tiles_hit = 0;
+    if (det != 0.f) {
+        const float inv_det = 1.f / det;
+        ca = c * inv_det;
+        cb = -b * inv_det;
+        cc = a * inv_det;
+        const float mid = 0.5f * (a + c);
+        const float spread = sqrtf(fmaxf(0.1f, mid * mid - det));
+        const float radius = ceilf(3.f * sqrtf(fmaxf(mid + spread, mid - spread)));
+        xy = make_float2(cx, cy);
+        radius_px = (int)radius;
+        unsigned x0, y0, x1, y1;
+        tile_rect(cx, cy, radius, tiles_x, tiles_y, x0, y0, x1, y1);
+        const int area = (int)((x1 - x0) * (y1 - y0));
+        tiles_hit = area > 0 ? area : 0;
+    }
+    xys[i] = xy;
+    radii[i] = radius_px;
+    conics[3 * i + 0] = ca;
+    conics[3 * i + 1] = cb;
+    conics[3 * i + 2] = cc;
+    hits[i] = tiles_hit;
+}
+
+// Backward of the projection, the reference's formula (backward2d.cu:53-100, helpers.cuh:71-82) term by term: v_cov2d = -X G X with the
+// conic X and G built from v_conic (its off-diagonal used as is), v_scale and v_rot contract v_cov2d with dSigma/ds and dSigma/dtheta
+// weighting the off-diagonal by 2, v_mean2d = v_xy (W, H). Gaussians with radius <= 0 get zeros.
+__global__ void __launch_bounds__(256) project_bwd_kernel(const int n, const float2 *__restrict__ scales, const float *__restrict__ rotations,
+                                                          const float img_w, const float img_h, const int *__restrict__ radii,
+                                                          const float *__restrict__ conics, const float2 *__restrict__ v_xy,
+                                                          const float *__restrict__ v_conic, float *__restrict__ v_cov2d,
+                                                          float2 *__restrict__ v_mean2d, float2 *__restrict__ v_scale,
+                                                          float *__restrict__ v_rot) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (__ldg(&radii[i]) <= 0) {
+        v_cov2d[3 * i + 0] = 0.f;
+        v_cov2d[3 * i + 1] = 0.f;
+        v_cov2d[3 * i + 2] = 0.f;
+        v_mean2d[i] = make_float2(0.f, 0.f);
+        v_scale[i] = make_float2(0.f, 0.f);
+        v_rot[i] = 0.f;
+        return;
+    }
+    const float x = conics[3 * i], y = conics[3 * i + 1], z = conics[3 * i + 2];
+    const float gx = v_conic[3 * i], gy = v_conic[3 * i + 1], gz = v_conic[3 * i + 2];
+    const M2 X{{{x, y}, {y, z}}};
+    const M2 G{{{gx, gy}, {gy, gz}}};
+    const M2 negX{{{-x, -y}, {-y, -z}}};
+    const M2 V = mul(mul(negX, G), X);
+    const float G11 = V.m[0][0], G12 = V.m[1][0] + V.m[0][1], G22 = V.m[1][1];
+
+    const float2 s = __ldg(&scales[i]);
+    const float theta = __ldg(&rotations[i]);
+    const float cs = cosf(theta), sn = sinf(theta);
+    const M2 R = rotation(cs, sn);
+    const M2 Rg = rotation_grad(cs, sn);
+    const M2 S = diag(s.x, s.y);
+    const M2 M = mul(R, S);
+    const M2 t1 = mul(mul(Rg, S), transpose(M));
+    const M2 t2 = mul(mul(M, transpose(S)), transpose(Rg));
+    M2 th;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) th.m[c][r] = t1.m[c][r] + t2.m[c][r];
+    const M2 sxg = mul(mul(R, diag(2.f * s.x, 0.f)), transpose(R));
+    const M2 syg = mul(mul(R, diag(0.f, 2.f * s.y)), transpose(R));
+
+    v_cov2d[3 * i + 0] = G11;
+    v_cov2d[3 * i + 1] = G12;
+    v_cov2d[3 * i + 2] = G22;
+    v_scale[i] = make_float2(G11 * sxg.m[0][0] + 2 * G12 * sxg.m[0][1] + G22 * sxg.m[1][1],
+                             G11 * syg.m[0][0] + 2 * G12 * syg.m[0][1] + G22 * syg.m[1][1]);
+    v_rot[i] = G11 * th.m[0][0] + 2 * G12 * th.m[0][1] + G22 * th.m[1][1];
+    const float2 vxy = v_xy[i];
+    v_mean2d[i] = make_float2(vxy.x * img_w, vxy.y * img_h);
+}
+
+}  // namespace
+
+extern "C" {
+
+int igs_project_fwd(int num_points, const float *means2d, const float *scales2d, const float *rotation, int img_height, int img_width,
+                    int tiles_x, int tiles_y, float *xys, int32_t *radii, float *conics, int32_t *num_tiles_hit, void *stream) {
+    IGS_REQUIRE(num_points >= 0 && img_height >= 0 && img_width >= 0 && tiles_x >= 0 && tiles_y >= 0, "igs_project_fwd: negative size");
+    if (num_points == 0) return IGS_OK;
+    IGS_REQUIRE(means2d && scales2d && rotation && xys && radii && conics && num_tiles_hit, "igs_project_fwd: null pointer");
+    IGS_REQUIRE(igs::aligned(means2d, 8) && igs::aligned(scales2d, 8) && igs::aligned(xys, 8),
+                "igs_project_fwd: means2d, scales2d and xys must be 8-byte aligned [N, 2] float32");
+    project_fwd_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
+        num_points, reinterpret_cast<const float2 *>(means2d), reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width,
+        (float)img_height, (unsigned)tiles_x, (unsigned)tiles_y, reinterpret_cast<float2 *>(xys), radii, conics, num_tiles_hit);
+    return igs::check_launch("igs_project_fwd");
+}
+
+int igs_project_bwd(int num_points, const float *scales2d, const float *rotation, int img_height, int img_width, const int32_t *radii,
+                    const float *conics, const float *v_xy, const float *v_conic, float *v_cov2d, float *v_mean2d, float *v_scale,
+                    float *v_rot, void *stream) {
+    IGS_REQUIRE(num_points >= 0, "igs_project_bwd: negative size");
+    if (num_points == 0) return IGS_OK;
+    IGS_REQUIRE(scales2d && rotation && radii && conics && v_xy && v_conic && v_cov2d && v_mean2d && v_scale && v_rot,
+                "igs_project_bwd: null pointer");
+    IGS_REQUIRE(igs::aligned(scales2d, 8) && igs::aligned(v_xy, 8) && igs::aligned(v_mean2d, 8) && igs::aligned(v_scale, 8),
+                "igs_project_bwd: [N, 2] tensors must be 8-byte aligned");
+    project_bwd_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
+        num_points, reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width, (float)img_height, radii, conics,
+        reinterpret_cast<const float2 *>(v_xy), v_conic, v_cov2d, reinterpret_cast<float2 *>(v_mean2d), reinterpret_cast<float2 *>(v_scale),
+        v_rot);
+    return igs::check_launch("igs_project_bwd");
+}
+
+}  // extern "C"

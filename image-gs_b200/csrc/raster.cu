@@ -1,0 +1,505 @@
+// Top-K normalized rasterization of 2D Gaussians, forward and backward, for 16x16 tiles.
+//
+// Forward (the semantics of nd_rasterize_forward_topk_norm, gsplat/gsplat/cuda/csrc/forward.cu:223-375): every pixel walks its tile's
+// Gaussian list in order and keeps the 10 largest alpha = exp(-sigma), sigma = (a dx^2 + c dy^2) / 2 + b dx dy, skipping sigma < 0, NaN or
+// Inf. A Gaussian enters if its alpha exceeds the cached minimum (-1 while slots are free): into the next free slot, or else into the first
+// slot holding the strict minimum, after which the minimum is rescanned. The pixel's value is sum_k f_k alpha_k / (sum_k alpha_k + 1e-4),
+// accumulated over the slots in slot order. Slot order and contents are part of the output (pixel_topk), so the insertion rule is kept
+// exactly.
+//
+// B200 layout: one CTA of 256 threads per tile (grid = tiles, so the hardware balances uneven list lengths over the 148 SMs); each warp
+// owns a compact 8x4 pixel patch; the tile's list is staged in shared memory in chunks of 256 entries (one 16-byte and one 4-byte
+// broadcast load per Gaussian and pixel). Two output forms of the top-K lists:
+//   * pixel_topk [H, W, 10] int32 Gaussian IDs (the reference's operator output), written through shared memory as coalesced 8-byte rows;
+//   * tile lists (autograd path): per tile, slot-major [10][256] uint16 positions in the tile's Gaussian list, 20 bytes per pixel instead
+//     of 40, written as coalesced 64-byte warp rows, and read back by the backward pass, which stages the same list in shared memory.
+// Compiled with --use_fast_math like the reference (__expf, approximate division), so alpha values and hence the lists match bit for bit.
+//
+// Backward (the math of nd_rasterize_backward_topk_norm_kernel, backward.cu:187-308): with D = 1e-4 + sum_k d_k and s_k = f_k . v_out,
+// v_sigma_k = -d_k (s_k / D - sum_j d_j s_j / D^2) and the colour weight d_k / D; per Gaussian v_conic += (v_sigma dx^2 / 2, v_sigma dx dy,
+// v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Each warp visits the union of its 32 pixels'
+// top-K Gaussians in increasing list position (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a
+// recursive-halving reduce-scatter, and adds them into per-tile accumulators in shared memory; at the end of the tile one global atomic per
+// (tile, Gaussian, value) flushes them, instead of one per (warp, Gaussian, value).
+#include "igs_common.cuh"
+
+namespace {
+
+using igs::kMaxChannels;
+using igs::kNoSlot;
+using igs::kTile;
+using igs::kTilePixels;
+using igs::kTopK;
+
+constexpr int kThreads = kTilePixels;  // one thread per pixel of the tile
+constexpr int kChunk = 256;            // list entries staged per round in the forward pass
+// list entries staged by the backward pass (fewer for the widest value vectors, to stay within 48 KB of static shared memory); longer
+// lists read the Gaussians from global memory and accumulate with global atomics
+template <int NV>
+constexpr int bwd_stage() { return NV <= 16 ? 256 : 128; }
+
+struct PixelCoord {
+    int i, j;  // row, column in the image
+    int tid;   // thread / pixel index within the tile
+};
+
+// Warp w covers the 8x4 patch (w % 2, w / 2) of the tile; lane l its pixel (l % 8, l / 8)
+__device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lx = (warp & 1) * 8 + (lane & 7), ly = (warp >> 1) * 4 + (lane >> 3);
+    return {(tile / tiles_x) * kTile + ly, (tile % tiles_x) * kTile + lx, tid};
+}
+
+// sigma of a Gaussian at a pixel, with the reference's operation order (forward.cu:309-311)
+__device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, float b, float c, float px, float py) {
+    const float dx = gx - px, dy = gy - py;
+    return 0.5f * (a * dx * dx + c * dy * dy) + b * dx * dy;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
+                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
+                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
+                                                              const float *__restrict__ colors, float *__restrict__ out_img,
+                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    const int channels = C > 0 ? C : channels_rt;
+    __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
+    __shared__ float s_cc[kChunk];    // conic c
+    __shared__ int s_ids[kThreads * kTopK];
+
+    const int tile = blockIdx.x;
+    const PixelCoord pc = tile_pixel(tile, tiles_x);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const float px = (float)pc.j, py = (float)pc.i;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+
+    int pos[kTopK];
+    float val[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        pos[k] = -1;
+        val[k] = 0.f;
+    }
+    int filled = 0, min_slot = 0;
+    float min_val = -1.f;
+
+    for (int base = 0; base < len; base += kChunk) {
+        const int count = min(kChunk, len - base);
+        __syncthreads();
+        if (pc.tid < count) {
+            const int g = __ldg(&ids_sorted[range.x + base + pc.tid]);
+            const float2 xy = __ldg(&xys[g]);
+            s_geo[pc.tid] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            s_cc[pc.tid] = __ldg(&conics[3 * g + 2]);
+        }
+        __syncthreads();
+        if (!inside) continue;
+        for (int e = 0; e < count; ++e) {
+            const float4 q = s_geo[e];
+            const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
+            if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
+            const float alpha = __expf(-sigma);
+            if (!(alpha > min_val)) continue;
+            // free slots fill in order; once full, the first slot holding the minimum is replaced
+            const int slot = filled < kTopK ? filled : min_slot;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                if (k == slot) {
+                    pos[k] = base + e;
+                    val[k] = alpha;
+                }
+            }
+            filled += filled < kTopK;
+            if (filled == kTopK) {
+                min_slot = 0;
+                min_val = val[0];
+#pragma unroll
+                for (int k = 1; k < kTopK; ++k) {
+                    if (val[k] < min_val) {
+                        min_slot = k;
+                        min_val = val[k];
+                    }
+                }
+            }
+        }
+    }
+
+    // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
+    int gid[kTopK];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        gid[k] = pos[k] >= 0 ? __ldg(&ids_sorted[range.x + pos[k]]) : -1;
+        if (pos[k] >= 0) sum += val[k];
+    }
+    const double inv = 1.0 / ((double)sum + igs::kNormEps);
+    float pix[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        if (gid[k] < 0) continue;
+        const float vis = (float)((double)val[k] * inv);
+        const float *f = colors + (size_t)gid[k] * channels;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+    }
+    const int num_pixels = img_h * img_w;
+    if (inside) {
+        const int p = pc.i * img_w + pc.j;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) out_img[(size_t)c * num_pixels + p] = pix[c];
+    }
+
+    if (tile_topk != nullptr) {
+        uint16_t *dst = tile_topk + (size_t)tile * kTopK * kThreads + pc.tid;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) dst[k * kThreads] = pos[k] >= 0 ? (uint16_t)pos[k] : kNoSlot;
+    }
+    if (pixel_topk != nullptr) {
+        // stage the IDs by thread, then write each tile row of 16 pixels x 10 IDs (80 int2) with consecutive threads
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) s_ids[pc.tid * kTopK + k] = gid[k];
+        __syncthreads();
+        const int i0 = (tile / tiles_x) * kTile, j0 = (tile % tiles_x) * kTile;
+        const int row_pairs = kTile * kTopK / 2;
+        for (int idx = threadIdx.x; idx < kTile * row_pairs; idx += kThreads) {
+            const int ly = idx / row_pairs, rem = idx % row_pairs;
+            const int lx = rem / (kTopK / 2), pair = rem % (kTopK / 2);
+            const int i = i0 + ly, j = j0 + lx;
+            if (i >= img_h || j >= img_w) continue;
+            const int src = ((ly >> 2) * 2 + (lx >> 3)) * 32 + (ly & 3) * 8 + (lx & 7);
+            const int2 v = make_int2(s_ids[src * kTopK + 2 * pair], s_ids[src * kTopK + 2 * pair + 1]);
+            reinterpret_cast<int2 *>(pixel_topk)[((size_t)i * img_w + j) * (kTopK / 2) + pair] = v;
+        }
+    }
+}
+
+// Sum of NV values over the 32 lanes of a warp by recursive halving: at each step a lane keeps half of its values, adds the partner's
+// copy of that half and hands over the other half, so NV - 1 + log2(32 / NV) shuffles replace 5 NV. Afterwards lane l holds the warp
+// total of value index halving_index<NV>(l); lanes with l % (32 / NV) == 0 hold each index exactly once.
+template <int NV>
+__device__ __forceinline__ float warp_sum_scatter(float (&v)[NV], int lane) {
+    int width = NV;
+#pragma unroll
+    for (int bit = 16; bit >= 32 / NV; bit >>= 1) {
+        width >>= 1;
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int k = 0; k < NV / 2; ++k) {
+            if (k < width) {
+                const float keep = upper ? v[k + width] : v[k];
+                const float give = upper ? v[k] : v[k + width];
+                v[k] = keep + __shfl_xor_sync(0xffffffffu, give, bit);
+            }
+        }
+    }
+    float total = v[0];
+#pragma unroll
+    for (int bit = 16 / NV; bit >= 1; bit >>= 1) total += __shfl_xor_sync(0xffffffffu, total, bit);
+    return total;
+}
+
+template <int NV>
+__device__ __forceinline__ int halving_index(int lane) {
+    int index = 0, width = NV;
+#pragma unroll
+    for (int bit = 16; bit >= 32 / NV; bit >>= 1) {
+        width >>= 1;
+        if (lane & bit) index += width;
+    }
+    return index;
+}
+
+constexpr int kNone = 0x7fffffff;
+
+// Gaussian parameters for the backward pass: from the staged tile list, or from global memory by ID
+struct Params {
+    float x, y, a, b, c;
+};
+
+template <int C, int NV>
+__global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
+                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
+                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
+                                                              const float *__restrict__ colors, const float *__restrict__ v_output,
+                                                              const int *__restrict__ pixel_topk, const uint16_t *__restrict__ tile_topk,
+                                                              float *__restrict__ v_xy, float *__restrict__ v_conic,
+                                                              float *__restrict__ v_colors) {
+    // channel registers: C when fixed, else as many as the NV-wide value vector holds
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
+    static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry values and the channels");
+    const int channels = C > 0 ? C : channels_rt;
+    constexpr int kBwdStage = bwd_stage<NV>();
+    __shared__ float4 s_geo[kBwdStage];
+    __shared__ float s_cc[kBwdStage];
+    __shared__ float s_col[kBwdStage * kMaxC];
+    __shared__ float s_acc[kBwdStage * NV];
+
+    const int tile = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const PixelCoord pc = tile_pixel(tile, tiles_x);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const float px = (float)pc.j, py = (float)pc.i;
+    const int num_pixels = img_h * img_w;
+    const int p = inside ? pc.i * img_w + pc.j : 0;
+
+    // Keys of the pixel's entries: list positions (tile lists) or Gaussian IDs (pixel_topk); kNone for empty slots and outside pixels
+    const bool by_position = tile_topk != nullptr;
+    int2 range = make_int2(0, 0);
+    if (by_position) range = tile_bins[tile];
+    const int len = range.y - range.x;
+    const bool staged = by_position && len <= kBwdStage;
+    if (staged) {
+        for (int e = threadIdx.x; e < len; e += kThreads) {
+            const int g = __ldg(&ids_sorted[range.x + e]);
+            const float2 xy = __ldg(&xys[g]);
+            s_geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            s_cc[e] = __ldg(&conics[3 * g + 2]);
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s_col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+        }
+        for (int e = threadIdx.x; e < len * NV; e += kThreads) s_acc[e] = 0.f;
+        __syncthreads();
+    }
+
+    auto params_of = [&](int key) -> Params {
+        if (staged) {
+            const float4 q = s_geo[key];
+            return {q.x, q.y, q.z, q.w, s_cc[key]};
+        }
+        const int g = by_position ? __ldg(&ids_sorted[range.x + key]) : key;
+        const float2 xy = __ldg(&xys[g]);
+        return {xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2])};
+    };
+    auto color_of = [&](int key, int c) -> float {
+        if (staged) return s_col[key * kMaxC + c];
+        const int g = by_position ? __ldg(&ids_sorted[range.x + key]) : key;
+        return __ldg(&colors[(size_t)g * channels + c]);
+    };
+
+    float v_out[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
+
+    int key[kTopK];
+    float d[kTopK];
+    float denom = (float)igs::kNormEps;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        int kk = kNone;
+        if (inside) {
+            if (by_position) {
+                const uint16_t v = __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + pc.tid]);
+                kk = v == kNoSlot ? kNone : (int)v;
+            } else {
+                const int g = __ldg(&pixel_topk[(size_t)p * kTopK + k]);
+                kk = g < 0 ? kNone : g;
+            }
+        }
+        key[k] = kk;
+        d[k] = 0.f;
+        if (kk == kNone) continue;
+        const Params q = params_of(kk);
+        d[k] = __expf(-gaussian_sigma(q.x, q.y, q.a, q.b, q.c, px, py));
+        denom += d[k];
+    }
+    // dL/dd_k = s_k / D - sum_j d_j s_j / D^2 with s_k = f_k . v_out
+    float s[kTopK];
+    float shared = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        s[k] = 0.f;
+        if (key[k] == kNone) continue;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) s[k] += color_of(key[k], c) * v_out[c];
+        shared += -d[k] / (denom * denom) * s[k];
+    }
+    float w[kTopK], vsig[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        w[k] = d[k] / denom;
+        vsig[k] = -d[k] * (s[k] / denom + shared);
+    }
+
+    // union walk over the warp's entries in increasing key order
+    const int value_index = halving_index<NV>(lane);
+    const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    while (true) {
+        int head = key[0];
+#pragma unroll
+        for (int k = 1; k < kTopK; ++k) head = min(head, key[k]);
+        const int cur = __reduce_min_sync(0xffffffffu, head);
+        if (cur == kNone) break;
+        float ws = 0.f, vs = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            if (key[k] == cur) {
+                ws = w[k];
+                vs = vsig[k];
+                key[k] = kNone;
+            }
+        }
+        const Params q = params_of(cur);
+        const float dx = q.x - px, dy = q.y - py;
+        float val[NV];
+        val[0] = 0.5f * vs * dx * dx;
+        val[1] = vs * dx * dy;
+        val[2] = 0.5f * vs * dy * dy;
+        val[3] = vs * (q.a * dx + q.b * dy);
+        val[4] = vs * (q.b * dx + q.c * dy);
+#pragma unroll
+        for (int c = 0; c < NV - 5; ++c) val[5 + c] = c < kMaxC ? ws * v_out[c < kMaxC ? c : 0] : 0.f;
+        const float total = warp_sum_scatter<NV>(val, lane);
+        if (holds_total) {
+            if (staged) {
+                atomicAdd(&s_acc[cur * NV + value_index], total);
+            } else {
+                const int g = by_position ? __ldg(&ids_sorted[range.x + cur]) : cur;
+                float *target = value_index < 3   ? v_conic + 3 * (size_t)g + value_index
+                                : value_index < 5 ? v_xy + 2 * (size_t)g + (value_index - 3)
+                                                  : v_colors + (size_t)g * channels + (value_index - 5);
+                atomicAdd(target, total);
+            }
+        }
+    }
+
+    if (staged) {
+        __syncthreads();
+        const int nvals = 5 + channels;
+        for (int e = threadIdx.x; e < len * nvals; e += kThreads) {
+            const int entry = e / nvals, v = e % nvals;
+            const float total = s_acc[entry * NV + v];
+            if (total == 0.f) continue;
+            const int g = __ldg(&ids_sorted[range.x + entry]);
+            float *target = v < 3 ? v_conic + 3 * (size_t)g + v : v < 5 ? v_xy + 2 * (size_t)g + (v - 3) : v_colors + (size_t)g * channels + (v - 5);
+            atomicAdd(target, total);
+        }
+    }
+}
+
+template <int C>
+cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
+                       const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk, cudaStream_t s) {
+    raster_fwd_kernel<C><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, out, pixel_topk,
+                                                     tile_topk);
+    return cudaGetLastError();
+}
+
+int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int channels, const int32_t *ids_sorted, const int32_t *tile_bins,
+               const float *xys, const float *conics, const float *colors, float *out_img, int32_t *pixel_topk, uint16_t *tile_topk,
+               void *stream, const char *who) {
+    IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && img_h >= 0 && img_w >= 0, "%s: negative size", who);
+    IGS_REQUIRE(channels >= 0 && channels <= kMaxChannels, "%s: at most %d channels (got %d)", who, kMaxChannels, channels);
+    IGS_REQUIRE(tiles_x == igs::ceil_div(img_w, kTile) && tiles_y == igs::ceil_div(img_h, kTile),
+                "%s: tile grid %dx%d does not cover a %dx%d image with %dx%d tiles", who, tiles_x, tiles_y, img_w, img_h, kTile, kTile);
+    const int tiles = tiles_x * tiles_y;
+    if (tiles == 0) return IGS_OK;
+    IGS_REQUIRE(tile_bins && xys && conics && (colors || channels == 0) && (out_img || channels == 0), "%s: null pointer", who);
+    IGS_REQUIRE(igs::aligned(tile_bins, 8) && igs::aligned(xys, 8), "%s: tile_bins and xys must be 8-byte aligned", who);
+    IGS_REQUIRE(pixel_topk == nullptr || igs::aligned(pixel_topk, 8), "%s: pixel_topk must be 8-byte aligned", who);
+    cudaStream_t s = igs::as_stream(stream);
+    const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
+    const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
+    cudaError_t err;
+    switch (channels) {
+        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s);
+    }
+    if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+    return IGS_OK;
+}
+
+template <int C, int NV>
+cudaError_t launch_bwd(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
+                       const float *conics, const float *colors, const float *v_output, const int *pixel_topk, const uint16_t *tile_topk,
+                       float *v_xy, float *v_conic, float *v_colors, cudaStream_t s) {
+    raster_bwd_kernel<C, NV><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
+                                                         pixel_topk, tile_topk, v_xy, v_conic, v_colors);
+    return cudaGetLastError();
+}
+
+int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys,
+               const float *conics, const float *colors, const float *v_output, const int32_t *pixel_topk, const uint16_t *tile_topk,
+               float *v_xy, float *v_conic, float *v_colors, void *stream, const char *who) {
+    IGS_REQUIRE(img_h >= 0 && img_w >= 0 && num_points >= 0, "%s: negative size", who);
+    IGS_REQUIRE(channels >= 0 && channels <= kMaxChannels, "%s: at most %d channels (got %d)", who, kMaxChannels, channels);
+    cudaStream_t s = igs::as_stream(stream);
+    if (num_points > 0) {
+        IGS_REQUIRE(v_xy && v_conic && (v_colors || channels == 0), "%s: null gradient pointer", who);
+        // the kernel accumulates with atomics
+        if (cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * (size_t)num_points, s) != cudaSuccess ||
+            cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * (size_t)num_points, s) != cudaSuccess ||
+            (channels > 0 && cudaMemsetAsync(v_colors, 0, sizeof(float) * (size_t)channels * num_points, s) != cudaSuccess))
+            return igs::check_launch(who);
+    }
+    const int tiles_x = igs::ceil_div(img_w, kTile), tiles_y = igs::ceil_div(img_h, kTile);
+    const int tiles = tiles_x * tiles_y;
+    if (tiles == 0 || num_points == 0) return IGS_OK;
+    IGS_REQUIRE(xys && conics && (colors || channels == 0) && (v_output || channels == 0), "%s: null pointer", who);
+    IGS_REQUIRE(pixel_topk || (tile_topk && tile_bins && ids_sorted), "%s: null top-K lists", who);
+    IGS_REQUIRE(igs::aligned(xys, 8), "%s: xys must be 8-byte aligned", who);
+    const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
+    const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
+    cudaError_t err;
+    if (channels == 3)
+        err = launch_bwd<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
+    else if (channels <= 3)
+        err = launch_bwd<0, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
+    else if (channels == 9)
+        err = launch_bwd<9, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
+    else if (channels <= 11)
+        err = launch_bwd<0, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
+    else
+        err = launch_bwd<0, 32>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
+    if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+    return IGS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int igs_raster_fwd_topk(int tiles_x, int tiles_y, int img_height, int img_width, int channels, const int32_t *gaussian_ids_sorted,
+                        const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, float *out_img,
+                        int32_t *pixel_topk, void *stream) {
+    IGS_REQUIRE(pixel_topk != nullptr || (int64_t)img_height * img_width == 0, "igs_raster_fwd_topk: null pixel_topk");
+    return raster_fwd(tiles_x, tiles_y, img_height, img_width, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors, out_img,
+                      pixel_topk, nullptr, stream, "igs_raster_fwd_topk");
+}
+
+int igs_raster_fwd_topk_tiles(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
+                              const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                              const float *colors, float *out_img, uint16_t *tile_topk, void *stream) {
+    IGS_REQUIRE(tile_topk != nullptr || tiles_x * tiles_y == 0, "igs_raster_fwd_topk_tiles: null tile_topk");
+    IGS_REQUIRE(max_list_len >= 0 && max_list_len < (int)kNoSlot,
+                "igs_raster_fwd_topk_tiles: tile lists may hold up to %d entries, more than 16-bit positions address (use igs_raster_fwd_topk)",
+                max_list_len);
+    return raster_fwd(tiles_x, tiles_y, img_height, img_width, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors, out_img,
+                      nullptr, tile_topk, stream, "igs_raster_fwd_topk_tiles");
+}
+
+int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
+                        const float *colors, const float *v_output, const int32_t *pixel_topk, float *v_xy, float *v_conic,
+                        float *v_colors, void *stream) {
+    return raster_bwd(img_height, img_width, channels, num_points, nullptr, nullptr, xys, conics, colors, v_output, pixel_topk, nullptr,
+                      v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk");
+}
+
+int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int num_points, const int32_t *gaussian_ids_sorted,
+                              const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
+                              const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream) {
+    IGS_REQUIRE(tile_topk != nullptr, "igs_raster_bwd_topk_tiles: null tile_topk");
+    return raster_bwd(img_height, img_width, channels, num_points, gaussian_ids_sorted, tile_bins, xys, conics, colors, v_output, nullptr,
+                      tile_topk, v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk_tiles");
+}
+
+}  // extern "C"

@@ -1,0 +1,163 @@
+"""
+The rasterization training step with every buffer preallocated, issued as direct C-ABI launches and replayable as one CUDA graph: the
+path of Image-GS's CUDA-graph step (model.py:1160-1209) for the hot path only:
+
+    [quantize-STE] -> project -> prefix sum -> tile binning -> top-K forward -> L1 loss + gradient -> top-K backward -> projection backward
+    [-> rate term forward/backward]
+
+The intersection buffers hold `capacity` entries (capacity_ratio times the count of the first step, at least 1024, as model.py:110,1186),
+so nothing is read back to the host inside the step; the true count is kept on the device (num_intersects) for overflow checks.
+"""
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib, ops
+from ._lib import ptr
+
+TILE = ops.TILE
+TOP_K = ops.TOP_K
+
+
+class RasterStep:
+    """One image's step. Inputs are device tensors: means [N,2], scales [N,2] (pixels), rotations [N,1], features [N,C], target [C,H,W]."""
+
+    def __init__(self, means, scales, rotations, features, target, capacity: Optional[int] = None, capacity_ratio: float = 2.0,
+                 l1_ratio: float = 1.0, tile_row_range=None):
+        self.lib = _lib.load()
+        self.device = means.device
+        self.n, self.c = features.shape
+        c, self.h, self.w = target.shape
+        assert c == self.c
+        self.means, self.scales, self.rotations, self.features, self.target = means, scales, rotations, features, target
+        self.tb = ops.tile_grid(self.h, self.w)
+        self.num_tiles = self.tb[0] * self.tb[1]
+        self.l1_ratio = float(l1_ratio)
+        dev, f32, i32 = self.device, torch.float32, torch.int32
+        n, nc = self.n, self.c
+        self.xys = torch.empty(n, 2, device=dev, dtype=f32)
+        self.radii = torch.empty(n, device=dev, dtype=i32)
+        self.conics = torch.empty(n, 3, device=dev, dtype=f32)
+        self.hits = torch.empty(n, device=dev, dtype=i32)
+        self.cum = torch.empty(n, device=dev, dtype=i32)
+        self.num_intersects = torch.empty(1, device=dev, dtype=i32)
+        self.image = torch.empty(nc, self.h, self.w, device=dev, dtype=f32)
+        self.v_image = torch.empty_like(self.image)
+        self.loss = torch.empty((), device=dev, dtype=f32)
+        self.l1_ws_bytes = self.lib.igs_l1_workspace(self.image.numel())
+        self.l1_ws = torch.zeros(self.l1_ws_bytes, device=dev, dtype=torch.uint8)
+        self.grads = torch.empty(n * (5 + nc), device=dev, dtype=f32)
+        self.v_xy, self.v_conic, self.v_colors = self.grads[:2 * n].view(n, 2), self.grads[2 * n:5 * n].view(n, 3), self.grads[5 * n:].view(n, nc)
+        self.v_cov2d = torch.empty(n, 3, device=dev, dtype=f32)
+        self.v_mean2d = torch.empty(n, 2, device=dev, dtype=f32)
+        self.v_scale = torch.empty(n, 2, device=dev, dtype=f32)
+        self.v_rot = torch.empty(n, 1, device=dev, dtype=f32)
+        if capacity is None:
+            self._project()
+            self._cumsum()
+            count = int(self.num_intersects.item())
+            capacity = max(1024, round(capacity_ratio * count))
+        self.capacity = int(capacity)
+        self.ids = torch.empty(self.capacity, device=dev, dtype=i32)
+        self.bins = torch.empty(self.num_tiles, 2, device=dev, dtype=i32)
+        self.sort_ws_bytes = self.lib.igs_sort_workspace(self.capacity, self.tb[0], self.tb[1])
+        self.sort_ws = torch.empty(self.sort_ws_bytes, device=dev, dtype=torch.uint8)
+        self.max_list = min(self.n, self.capacity)
+        self.tile_form = self.max_list <= ops.MAX_TILE_LIST
+        if self.tile_form:
+            self.topk = torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        else:
+            self.topk = torch.empty(self.h, self.w, TOP_K, device=dev, dtype=i32)
+        self.graph = None
+
+    # ---- stages (each one C-ABI call on the current stream) ----
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _check(self, status, what):
+        _lib.check(status, what)
+
+    def _project(self):
+        self._check(self.lib.igs_project_fwd(self.n, ptr(self.means), ptr(self.scales), ptr(self.rotations), self.h, self.w, self.tb[0],
+                                             self.tb[1], ptr(self.xys), ptr(self.radii), ptr(self.conics), ptr(self.hits), self._stream()),
+                    "project")
+
+    def _cumsum(self):
+        self._check(self.lib.igs_cumsum(self.n, ptr(self.hits), ptr(self.cum), ptr(self.num_intersects), self._stream()), "cumsum")
+
+    def _bin(self):
+        self._check(self.lib.igs_sort_intersects(self.n, self.capacity, ptr(self.xys), ptr(self.radii), ptr(self.cum), self.tb[0], self.tb[1],
+                                                 ptr(self.ids), ptr(self.bins), ptr(self.sort_ws), self.sort_ws_bytes, self._stream()),
+                    "bin")
+
+    def _forward(self):
+        if self.tile_form:
+            st = self.lib.igs_raster_fwd_topk_tiles(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
+                                                    ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.image),
+                                                    ptr(self.topk), self._stream())
+        else:
+            st = self.lib.igs_raster_fwd_topk(self.tb[0], self.tb[1], self.h, self.w, self.c, ptr(self.ids), ptr(self.bins), ptr(self.xys),
+                                              ptr(self.conics), ptr(self.features), ptr(self.image), ptr(self.topk), self._stream())
+        self._check(st, "forward")
+
+    def _loss(self):
+        self._check(self.lib.igs_l1_loss(self.image.numel(), ptr(self.image), ptr(self.target), self.l1_ratio, ptr(self.loss),
+                                         ptr(self.v_image), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "l1")
+
+    def _backward(self):
+        if self.tile_form:
+            st = self.lib.igs_raster_bwd_topk_tiles(self.h, self.w, self.c, self.n, ptr(self.ids), ptr(self.bins), ptr(self.xys),
+                                                    ptr(self.conics), ptr(self.features), ptr(self.v_image), ptr(self.topk), ptr(self.v_xy),
+                                                    ptr(self.v_conic), ptr(self.v_colors), self._stream())
+        else:
+            st = self.lib.igs_raster_bwd_topk(self.h, self.w, self.c, self.n, ptr(self.xys), ptr(self.conics), ptr(self.features),
+                                              ptr(self.v_image), ptr(self.topk), ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_colors),
+                                              self._stream())
+        self._check(st, "backward")
+
+    def _project_backward(self):
+        self._check(self.lib.igs_project_bwd(self.n, ptr(self.scales), ptr(self.rotations), self.h, self.w, ptr(self.radii), ptr(self.conics),
+                                             ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
+                                             ptr(self.v_rot), self._stream()), "project_backward")
+
+    STAGES = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward", "_project_backward")
+    # kernels each stage launches (memsets excluded)
+    KERNELS = {"_project": 1, "_cumsum": 1, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1}
+
+    def launch(self):
+        for s in self.STAGES:
+            getattr(self, s)()
+
+    @property
+    def kernels_per_step(self):
+        return sum(self.KERNELS.values())
+
+    def capture(self, stages=None):
+        """A CUDA graph of the step (or of the given stages)."""
+        stages = stages or self.STAGES
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for s in stages:  # warm-up outside the capture
+                getattr(self, s)()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for s in stages:
+                getattr(self, s)()
+        return graph
+
+    def replay(self):
+        if self.graph is None:
+            self.graph = self.capture()
+        self.graph.replay()
+
+    def gaussian_pixel_evals(self):
+        """Forward evaluations of the step: sum over tiles of list length x in-image pixels of the tile."""
+        bins = self.bins.to(torch.int64)
+        lengths = (bins[:, 1] - bins[:, 0]).view(self.tb[1], self.tb[0])
+        rows = torch.clamp(self.h - torch.arange(self.tb[1], device=self.device) * TILE, max=TILE)
+        cols = torch.clamp(self.w - torch.arange(self.tb[0], device=self.device) * TILE, max=TILE)
+        return int((lengths * rows[:, None] * cols[None, :]).sum().item())

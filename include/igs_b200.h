@@ -1,0 +1,142 @@
+/*
+ * igs_b200 — B200-native (sm_100a) CUDA kernels of Image-GS's per-step 2D Gaussian rasterization, behind a plain C ABI.
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are CUDA device pointers to contiguous row-major arrays (float32 / int32 unless stated), sizes are element counts.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); work is enqueued asynchronously on it and nothing synchronizes.
+ *   - The library never allocates device memory: outputs and workspaces are the caller's (query sizes with the *_workspace functions),
+ *     so every call can be captured in a CUDA graph.
+ *   - Return IGS_OK (0) or an error code; igs_last_error() gives this thread's message. No entry point exits the process.
+ * Reference citations are paths inside BaylorMultimediaLab/image-gs (the gsplat fork under gsplat/gsplat/, the rate/quantization code
+ * under compress/, the training step in model.py).
+ */
+#ifndef IGS_B200_H
+#define IGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IGS_VERSION 1
+
+#define IGS_OK 0
+#define IGS_ERR_INVALID 1     /* bad argument: caught on the host before any launch */
+#define IGS_ERR_CUDA 2        /* a CUDA launch or runtime call failed */
+#define IGS_ERR_UNSUPPORTED 3 /* a valid request this build does not handle */
+
+/* Compile-time constants (gsplat/gsplat/cuda/csrc/config.h:1-10; mirrored in model.py:447-448) */
+#define IGS_TILE 16
+#define IGS_TOP_K 10
+#define IGS_MAX_CHANNELS 12
+
+const char *igs_last_error(void);
+int igs_version(void);
+/* tile side, K of the top-K lists, maximum channels, normalization epsilon */
+int igs_constants(int *tile, int *top_k, int *max_channels, double *eps);
+
+/* ---- projection ---------------------------------------------------------------------------------------------------------------- */
+
+/* project_gaussians_2d_scale_rot_forward (gsplat/gsplat/cuda/csrc/bindings.cu:791-837, kernel foward2d.cu:9-59).
+ * means2d [N,2] in [0,1) image coordinates, scales2d [N,2] in pixels, rotation [N] radians. Outputs: xys [N,2] pixel centers,
+ * radii [N], conics [N,3] (upper triangle of the inverse covariance), num_tiles_hit [N]. Every output element is written. */
+int igs_project_fwd(int num_points, const float *means2d, const float *scales2d, const float *rotation, int img_height, int img_width,
+                    int tiles_x, int tiles_y, float *xys, int32_t *radii, float *conics, int32_t *num_tiles_hit, void *stream);
+
+/* project_gaussians_2d_scale_rot_backward (bindings.cu:845-891, kernel backward2d.cu:53-100); the reference's means2d argument is
+ * unused there and omitted. Outputs v_cov2d [N,3], v_mean2d [N,2], v_scale [N,2], v_rot [N] are fully written. */
+int igs_project_bwd(int num_points, const float *scales2d, const float *rotation, int img_height, int img_width, const int32_t *radii,
+                    const float *conics, const float *v_xy, const float *v_conic, float *v_cov2d, float *v_mean2d, float *v_scale,
+                    float *v_rot, void *stream);
+
+/* ---- tile binning --------------------------------------------------------------------------------------------------------------- */
+
+/* compute_cumulative_intersects (gsplat/gsplat/utils.py:96-115): inclusive int32 prefix sum; `total` (device int32, may be NULL) gets
+ * the last element without a host read-back. */
+size_t igs_cumsum_workspace(int n);
+int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *stream);
+
+/* sort_intersects_by_tile (gsplat/gsplat/utils.py:165-186 -> bindings.cu:106-167): Gaussian IDs of the tile intersections sorted by tile,
+ * increasing Gaussian ID within a tile, in `capacity` slots (intersections beyond the capacity dropped, unused slots 0), and
+ * tile_bins [T,2] = [start, end) per tile ((0,0) when empty). */
+size_t igs_sort_workspace(int capacity, int tiles_x, int tiles_y);
+int igs_sort_intersects(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                        int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace, size_t workspace_bytes,
+                        void *stream);
+
+/* ---- top-K normalized rasterization ---------------------------------------------------------------------------------------------- */
+
+/* nd_rasterize_forward_topk_norm (bindings.cu:380-437, kernel forward.cu:223-375): out_img [C,H,W] (channel-planar) and
+ * pixel_topk [H,W,10] Gaussian IDs (-1 empty). colors [N,C], C <= IGS_MAX_CHANNELS. */
+int igs_raster_fwd_topk(int tiles_x, int tiles_y, int img_height, int img_width, int channels, const int32_t *gaussian_ids_sorted,
+                        const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, float *out_img,
+                        int32_t *pixel_topk, void *stream);
+
+/* The same forward pass for the training step (rasterize_sum.py:169-267's autograd path): instead of pixel_topk, tile_topk
+ * [T,10,256] uint16 holds each pixel's slots as positions in its tile's Gaussian list (0xFFFF empty), indexed by the pixel's lane in
+ * the tile (warp w covers the 8x4 patch (w%2, w/2), lane l its pixel (l%8, l/8)). max_list_len bounds every tile list
+ * (e.g. min(num_points, capacity)) and must be below 65535. */
+int igs_raster_fwd_topk_tiles(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
+                              const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                              const float *colors, float *out_img, uint16_t *tile_topk, void *stream);
+
+/* nd_rasterize_backward_topk_norm (bindings.cu:444-502, kernel backward.cu:187-335): v_output [C,H,W]; outputs v_xy [N,2],
+ * v_conic [N,3], v_colors [N,C] are zeroed and accumulated (float atomics: the last bits vary run to run). */
+int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
+                        const float *colors, const float *v_output, const int32_t *pixel_topk, float *v_xy, float *v_conic,
+                        float *v_colors, void *stream);
+
+/* The backward pass from igs_raster_fwd_topk_tiles' lists, with the same gaussian_ids_sorted / tile_bins. */
+int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int num_points, const int32_t *gaussian_ids_sorted,
+                              const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
+                              const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream);
+
+/* topk_norm_loo_loss_increase (bindings.cu:895-936, kernel forward.cu:667-738): per Gaussian, the increase of the absolute (squared
+ * when `squared`) error summed over pixels and channels when it alone leaves the top-K lists; targets [C,H,W]. */
+int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
+                          const float *colors, const int32_t *pixel_topk, const float *targets, int squared, float eps,
+                          float *loss_increase, void *stream);
+
+/* ---- training-step losses and quantization -------------------------------------------------------------------------------------- */
+
+/* L1 loss and its gradient in one pass (model.py:1224-1227, F.l1_loss): loss = ratio * mean|image - target| (device scalar) and
+ * grad = ratio * sign(image - target) / numel. Deterministic (fixed-order block sums). partials: igs_l1_workspace bytes. */
+size_t igs_l1_workspace(int64_t numel);
+int igs_l1_loss(int64_t numel, const float *image, const float *target, float ratio, float *loss, float *grad, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* Straight-through "step" quantization of the Gaussian parameters during optimization (model.py:993-1006 with
+ * compress/quantization.py:36-46,61-74,151-172,188-199; quarter turns off, log-domain scales): symbols
+ * q_xy = round(xy / pos_steps), q_scale = round(log2|scale| / scale_step), q_rot = round(rot / rot_step), q_feat = round(feat / feat_steps)
+ * (round half to even, IEEE division), and forward values x + (dequantize(q) - x) with dequantize(q_scale) = exp2(q_scale * scale_step).
+ * xy [N,2], scale [N,2] (pixels), rot [N], feat [N,C]; pos_steps [2], feat_steps [C] device arrays. Symbol outputs may be NULL.
+ * feat_transform (may be NULL): a [C,C] matrix T; then out_feat_t [N,C] = out_feat T^T as well (model.py:963-964, YUV loss space). */
+int igs_quantize_ste(int num_points, int channels, const float *xy, const float *scale, const float *rot, const float *feat,
+                     const float *pos_steps, float scale_step, float rot_step, const float *feat_steps, const float *feat_transform,
+                     float *out_xy, float *out_scale, float *out_rot, float *out_feat, float *out_feat_t, float *q_xy, float *q_scale,
+                     float *q_rot, float *q_feat, void *stream);
+
+/* rate_loss_forward (gsplat/gsplat/cuda/csrc/rate.cu:201-279; definition compress/rate.py:167-175 rate_bits): loss (device scalar)
+ * = factor / max(l1_loss / l1_ratio, 1e-4) * (sum_{g,c} feat_coeffs[c] (sqrt(r^2 + 1/4) - 1/2) + sum_g rot_coeffs[g] (sqrt(t^2 + 1/4) - 1/2)),
+ * own_grad [N,C] and rot_grad [N] for the backward pass. color_refs / pred_refs: C host integers each. neighbors [N,K] int32.
+ * Workspace: igs_rate_workspace bytes (per-block bit sums). */
+size_t igs_rate_workspace(int num_gaussians);
+int igs_rate_fwd(int num_gaussians, int channels, int num_neighbors, const float *feat, const float *rot, const float *l1_loss,
+                 const int32_t *neighbors, const float *weights, const float *slope, const int32_t *color_refs, const int32_t *pred_refs,
+                 const float *inv_steps, const float *feat_coeffs, const float *rot_coeffs, float inv_rot_step, float l1_ratio,
+                 float factor, float *loss, float *loss_weight, float *own_grad, float *rot_grad, void *workspace, size_t workspace_bytes,
+                 void *stream);
+
+/* rate_loss_backward (rate.cu:281-321): grad_feat [N,C], grad_rot [N] from the forward's own gradients and the CSR list of the
+ * Gaussians that predict from each one (offsets [N+1], sources [E], source_weights [E]). Deterministic, no atomics. */
+int igs_rate_bwd(int num_gaussians, int channels, const float *grad_loss, const float *loss_weight, const float *own_grad,
+                 const float *rot_grad, const int32_t *offsets, const int32_t *sources, const float *source_weights, float *grad_feat,
+                 float *grad_rot, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IGS_B200_H */

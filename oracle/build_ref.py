@@ -1,0 +1,67 @@
+"""
+Test infrastructure, not product code: builds the reference's own gsplat CUDA extension from its sources, unmodified, into oracle/_ref/, so
+that GPU tests and the golden-vector script can run the reference kernels beside ours on the same B200 and compare bit for bit.
+
+Recipe (our own, not the reference's setup.py): torch.utils.cpp_extension compiles every gsplat/gsplat/cuda/csrc/*.cu and ext.cpp where they
+lie under the reference tree, with the flags of gsplat/setup.py:45-80 (-O3 --use_fast_math --expt-relaxed-constexpr for nvcc, -O3 for the
+host compiler, the vendored glm on the include path), for sm_100a. Objects and the module go to oracle/_ref/ only; the reference tree is
+read-only. The resulting module is named gsplat_ref_csrc and exposes the reference's pybind functions (gsplat/gsplat/cuda/csrc/ext.cpp:4-32).
+
+Usage: python oracle/build_ref.py [REFERENCE_ROOT]   (default: /root/reference). Needs nvcc, no GPU.
+"""
+import glob
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "_ref")
+MODULE = "gsplat_ref_csrc"
+
+
+def built_module_path():
+    """Path of the built reference module, or None if it has not been built."""
+    hits = glob.glob(os.path.join(OUT, MODULE + "*.so"))
+    return hits[0] if hits else None
+
+
+def build(reference_root="/root/reference", verbose=False):
+    csrc = os.path.join(reference_root, "gsplat", "gsplat", "cuda", "csrc")
+    if not os.path.isdir(csrc):
+        raise FileNotFoundError(f"reference CUDA sources not found at {csrc}")
+    os.makedirs(OUT, exist_ok=True)
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    from torch.utils.cpp_extension import load
+
+    sources = sorted(glob.glob(os.path.join(csrc, "*.cu"))) + sorted(glob.glob(os.path.join(csrc, "*.cpp")))
+    load(
+        name=MODULE,
+        sources=sources,
+        extra_include_paths=[os.path.join(csrc, "third_party", "glm")],
+        extra_cflags=["-O3", "-Wno-sign-compare"],
+        extra_cuda_cflags=["-O3", "--use_fast_math", "--expt-relaxed-constexpr",
+                           "-gencode=arch=compute_100a,code=sm_100a"],
+        build_directory=OUT,
+        verbose=verbose,
+        is_python_module=True,
+    )
+    return built_module_path()
+
+
+def load_module():
+    """Import the built reference module (raises ImportError when oracle/_ref holds no build)."""
+    path = built_module_path()
+    if path is None:
+        raise ImportError("reference extension not built (python oracle/build_ref.py)")
+    import importlib.util
+
+    import torch  # noqa: F401  (the module links against libtorch)
+
+    spec = importlib.util.spec_from_file_location(MODULE, path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+if __name__ == "__main__":
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    print(build(root, verbose=True))
