@@ -45,7 +45,7 @@ def _i32(a):
 
 
 def tile_grid(h, w):
-    return (w + 15) // 16, (h + 15) // 16
+    return (int(w) + 15) // 16, (int(h) + 15) // 16
 
 
 def project_fwd(means, scales, rot, h, w):
@@ -55,7 +55,7 @@ def project_fwd(means, scales, rot, h, w):
     tx, ty = tile_grid(h, w)
     xys, conics = np.zeros((n, 2), np.float32), np.zeros((n, 3), np.float32)
     radii, hits = np.zeros(n, np.int32), np.zeros(n, np.int32)
-    lib().orc_project_fwd(n, _p(means), _p(scales), _p(rot), h, w, tx, ty, _p(xys), _p(radii), _p(conics), _p(hits))
+    lib().orc_project_fwd(n, _p(means), _p(scales), _p(rot), int(h), int(w), tx, ty, _p(xys), _p(radii), _p(conics), _p(hits))
     return xys, radii, conics, hits
 
 
@@ -66,7 +66,7 @@ def project_bwd(scales, rot, h, w, radii, conics, v_xy, v_conic):
     n = len(scales)
     v_cov2d, v_mean2d = np.zeros((n, 3), np.float32), np.zeros((n, 2), np.float32)
     v_scale, v_rot = np.zeros((n, 2), np.float32), np.zeros((n, 1), np.float32)
-    lib().orc_project_bwd(n, _p(scales), _p(rot), h, w, _p(radii), _p(conics), _p(v_xy), _p(v_conic), _p(v_cov2d), _p(v_mean2d),
+    lib().orc_project_bwd(n, _p(scales), _p(rot), int(h), int(w), _p(radii), _p(conics), _p(v_xy), _p(v_conic), _p(v_cov2d), _p(v_mean2d),
                           _p(v_scale), _p(v_rot))
     return v_cov2d, v_mean2d, v_scale, v_rot
 
@@ -82,9 +82,9 @@ def sort_intersects(num_points, capacity, xys, radii, cum, h, w):
     """bindings.cu:106-167 -> gaussian_ids_sorted [capacity], tile_bins [T,2]"""
     xys, radii, cum = _f32(xys), _i32(radii), _i32(cum)
     tx, ty = tile_grid(h, w)
-    ids = np.zeros(max(capacity, 0), np.int32)
+    ids = np.zeros(max(int(capacity), 0), np.int32)
     bins = np.zeros((tx * ty, 2), np.int32)
-    lib().orc_sort_intersects(num_points, capacity, _p(xys), _p(radii), _p(cum), tx, ty, _p(ids), _p(bins))
+    lib().orc_sort_intersects(int(num_points), int(capacity), _p(xys), _p(radii), _p(cum), tx, ty, _p(ids), _p(bins))
     return ids, bins
 
 
@@ -93,9 +93,10 @@ def raster_fwd(h, w, ids_sorted, tile_bins, xys, conics, colors):
     ids_sorted, tile_bins, xys, conics, colors = _i32(ids_sorted), _i32(tile_bins), _f32(xys), _f32(conics), _f32(colors)
     c = colors.shape[1]
     tx, ty = tile_grid(h, w)
+    h, w = int(h), int(w)
     out = np.zeros((c, h, w), np.float32)
     topk = np.zeros((h, w, 10), np.int32)
-    lib().orc_raster_fwd(tx, ty, h, w, c, _p(ids_sorted), _p(tile_bins), _p(xys), _p(conics), _p(colors), _p(out), _p(topk))
+    lib().orc_raster_fwd(tx, ty, int(h), int(w), c, _p(ids_sorted), _p(tile_bins), _p(xys), _p(conics), _p(colors), _p(out), _p(topk))
     return out, topk
 
 
@@ -104,7 +105,7 @@ def raster_bwd(h, w, xys, conics, colors, v_output, pixel_topk):
     xys, conics, colors, v_output, pixel_topk = _f32(xys), _f32(conics), _f32(colors), _f32(v_output), _i32(pixel_topk)
     n, c = colors.shape
     v_xy, v_conic, v_colors = np.zeros((n, 2), np.float32), np.zeros((n, 3), np.float32), np.zeros((n, c), np.float32)
-    lib().orc_raster_bwd(h, w, c, n, _p(xys), _p(conics), _p(colors), _p(v_output), _p(pixel_topk), _p(v_xy), _p(v_conic), _p(v_colors))
+    lib().orc_raster_bwd(int(h), int(w), c, n, _p(xys), _p(conics), _p(colors), _p(v_output), _p(pixel_topk), _p(v_xy), _p(v_conic), _p(v_colors))
     return v_xy, v_conic, v_colors
 
 
@@ -113,7 +114,7 @@ def loo_loss_increase(h, w, xys, conics, colors, pixel_topk, targets, squared, e
     xys, conics, colors, pixel_topk, targets = _f32(xys), _f32(conics), _f32(colors), _i32(pixel_topk), _f32(targets)
     n, c = colors.shape
     out = np.zeros(n, np.float32)
-    lib().orc_loo_loss_increase(h, w, c, n, _p(xys), _p(conics), _p(colors), _p(pixel_topk), _p(targets), int(bool(squared)),
+    lib().orc_loo_loss_increase(int(h), int(w), c, n, _p(xys), _p(conics), _p(colors), _p(pixel_topk), _p(targets), int(bool(squared)),
                                 ctypes.c_float(eps), _p(out))
     return out
 
