@@ -17,7 +17,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -44,56 +43,53 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """SM clocks and throttle reasons of one GPU sampled through NVML every ~2 ms while running (the timed region can be a few ms)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
         self.gpu_index = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.stop = threading.Event()
+        self.ok = False
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.gpu_index]) if visible else self.gpu_index
+            self.nvml, self.handle = pynvml, pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except (FileNotFoundError, OSError):
-            self.proc = None
+        except Exception:  # no NVML: report no samples
+            self.ok = False
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                mhz = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                reasons = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.ok:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() in ("active", "1"):
-                    reasons.add(name)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted({name for _, r in self.samples for name, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML, 2 ms polling during the timed steps"}
 
 
 def dist_setup(gpus):
@@ -227,10 +223,12 @@ def run_ours(args, wl):
 
     # per-stage breakdown and the dominant kernel's roofline (graphs of single stages, same flush discipline)
     stage_ms = {}
-    for s in pipeline.RasterStep.STAGES:
+    for s in pipeline.RasterStep.STAGES if not args.no_stages else ():
         g = step.capture([s])
         stage_ms[s.strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g
+    if not stage_ms:
+        stage_ms = {"forward": ms_per_step, "backward": 0.0}
     hbm_peak, peak_kind = peaks()
     p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
     fwd_bytes = p * (4 * c + 4 * k) + num_isect * 4 + n * 4 * (5 + c)
@@ -243,7 +241,7 @@ def run_ours(args, wl):
     loss_bytes = 12 * c * p
 
     # end to end through the drop-in gsplat API (autograd), host -> device parameters and device -> host loss every step
-    e2e = run_e2e(args, wl, inp, device, step.capacity, world)
+    e2e = run_e2e(args, wl, inp, device, step.capacity, world) if not args.no_e2e else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -330,6 +328,8 @@ def main():
     ap.add_argument("--workload", default="cfg3_1080p")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
+    ap.add_argument("--no-stages", action="store_true", help="skip the per-stage timing")
     args = ap.parse_args()
     wl = workloads.get_workload(args.workload)
     if args.impl == "reference":
