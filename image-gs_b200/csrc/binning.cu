@@ -3,14 +3,18 @@
 //
 // The reference maps each intersection slot to its Gaussian by binary search, radix-sorts 32-bit tile keys with CUB (stable, so within a
 // tile the Gaussians are in increasing ID order) and finds the tile ranges in a third pass. Here the same order comes from a counting sort
-// on the tile grid, which needs no key buffer and no sort passes over all intersections:
-//   1. count:   one thread per Gaussian adds 1 to each tile of its footprint (only slots below the capacity, as the reference drops the
-//               intersections beyond it in Gaussian-major order),
-//   2. scan:    one CTA turns the per-tile counts into the tile ranges [start, end) (empty tiles (0, 0)) and per-tile write cursors,
-//   3. scatter: one thread per Gaussian claims a position in each of its tiles with an atomic cursor,
+// on the tile grid, with no sort passes over all intersections:
+//   1. count:   one thread per intersection slot below min(total, capacity) (the reference drops the slots beyond the capacity, in
+//               Gaussian-major order) finds its Gaussian by binary search in the prefix sum and its tile, and takes a rank within the
+//               tile from one returning atomic on the tile's counter,
+//   2. scan:    one CTA turns the per-tile counts into the tile ranges [start, end) (empty tiles (0, 0)),
+//   3. place:   each slot writes its Gaussian at start + rank,
 //   4. order:   one warp per tile ranks its few entries (IDs are unique within a tile), restoring increasing Gaussian ID, and zero-fills the
 //               padding slots after the last intersection, as the reference's padding entries (key num_tiles, value 0) sort last.
+// Every thread does a bounded, balanced amount of work (a large Gaussian's footprint is spread over as many threads as it has tiles).
 // Integer-only and deterministic; outputs are bit-identical to the reference for inputs whose tile counts come from the projection.
+#include <algorithm>
+
 #include "igs_common.cuh"
 
 namespace {
@@ -31,54 +35,70 @@ __device__ __forceinline__ void tile_rect(float cx, float cy, float radius, unsi
 }
 
 // Inclusive block-wide scan of one value per thread (blockDim.x == kScanThreads); returns the inclusive prefix, *total gets the sum
-__device__ __forceinline__ int block_inclusive_scan(int v, int *warp_sums, int *total) {
+__device__ __forceinline__ unsigned block_inclusive_scan(unsigned v, unsigned *warp_sums, unsigned *total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        const unsigned n = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += n;
     }
     if (lane == 31) warp_sums[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        int w = lane < (kScanThreads / 32) ? warp_sums[lane] : 0;
+        unsigned w = lane < (kScanThreads / 32) ? warp_sums[lane] : 0u;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, w, o);
+            const unsigned n = __shfl_up_sync(0xffffffffu, w, o);
             if (lane >= o) w += n;
         }
         warp_sums[lane] = w;
     }
     __syncthreads();
-    const int result = v + (warp > 0 ? warp_sums[warp - 1] : 0);
+    const unsigned result = v + (warp > 0 ? warp_sums[warp - 1] : 0u);
     *total = warp_sums[kScanThreads / 32 - 1];
     __syncthreads();
     return result;
 }
 
-// Inclusive int32 prefix sum (wrapping, as torch.cumsum in int32) by one CTA: thread t scans a contiguous run of per_thread elements
-__global__ void __launch_bounds__(kScanThreads) cumsum_kernel(const int n, const int *__restrict__ in, int *__restrict__ out,
-                                                              int *__restrict__ total_out) {
-    __shared__ int warp_sums[32];
-    const int per_thread = (n + kScanThreads - 1) / kScanThreads;
-    const int begin = min(n, (int)threadIdx.x * per_thread), end = min(n, begin + per_thread);
-    unsigned run = 0;
-    for (int i = begin; i < end; ++i) run += (unsigned)__ldg(&in[i]);
-    int total;
-    const int inclusive = block_inclusive_scan((int)run, warp_sums, &total);
-    unsigned acc = (unsigned)inclusive - run;
-    for (int i = begin; i < end; ++i) {
-        acc += (unsigned)__ldg(&in[i]);
-        out[i] = (int)acc;
+constexpr int kScanItems = 8;  // consecutive elements per thread and chunk: coalesced 32-byte runs
+
+// Scan of in[0, n) by one CTA in chunks of kScanThreads * kScanItems elements; visit(i, exclusive, value) gets each element's exclusive
+// prefix (wrapping uint32, as int32 sums). Returns the total.
+template <typename Visit>
+__device__ __forceinline__ unsigned chunked_scan(const int *__restrict__ in, int n, Visit visit) {
+    __shared__ unsigned warp_sums[32];
+    unsigned carry = 0u;
+    for (int base = 0; base < n; base += kScanThreads * kScanItems) {
+        const int first = base + (int)threadIdx.x * kScanItems;
+        unsigned v[kScanItems];
+        unsigned run = 0u;
+        if (first + kScanItems <= n && (reinterpret_cast<uintptr_t>(in + first) & 15) == 0) {
+            const int4 a = __ldg(reinterpret_cast<const int4 *>(in + first));
+            const int4 b = __ldg(reinterpret_cast<const int4 *>(in + first) + 1);
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < kScanItems; ++k) v[k] = first + k < n ? (unsigned)__ldg(&in[first + k]) : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) run += v[k];
+        unsigned total;
+        unsigned excl = block_inclusive_scan(run, warp_sums, &total) - run + carry;
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            if (first + k < n) visit(first + k, excl, v[k]);
+            excl += v[k];
+        }
+        carry += total;
     }
-    if (threadIdx.x == 0 && total_out) *total_out = total;
+    return carry;
 }
 
-// Slots of Gaussian g that fit below the capacity (the reference maps slot idx < min(capacity, total) only)
-__device__ __forceinline__ int kept_slots(const int *__restrict__ cum, int g, int capacity) {
-    const int base = g > 0 ? __ldg(&cum[g - 1]) : 0;
-    const int count = __ldg(&cum[g]) - base;
-    return max(0, min(count, capacity - base));
+// Inclusive int32 prefix sum (wrapping, as torch.cumsum in int32) by one CTA
+__global__ void __launch_bounds__(kScanThreads) cumsum_kernel(const int n, const int *__restrict__ in, int *__restrict__ out,
+                                                              int *__restrict__ total_out) {
+    const unsigned total = chunked_scan(in, n, [&](int i, unsigned excl, unsigned v) { out[i] = (int)(excl + v); });
+    if (threadIdx.x == 0 && total_out) *total_out = (int)total;
 }
 
 // Tile key of slot `local` of a Gaussian's footprint: row-major position in its tile rectangle (forward.cu:102-103 of the reference)
@@ -86,59 +106,60 @@ __device__ __forceinline__ unsigned slot_tile(int local, unsigned x0, unsigned y
     return (y0 + (unsigned)local / width) * tiles_x + x0 + (unsigned)local % width;
 }
 
+// The Gaussian owning intersection slot idx: the first g with cum[g] > idx (forward.cu:89-98 of the reference)
+__device__ __forceinline__ int owner_of(const int *__restrict__ cum, int n, int idx) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(&cum[mid]) > idx)
+            hi = mid;
+        else
+            lo = mid + 1;
+    }
+    return lo;
+}
+
+// One thread per intersection slot below min(total, capacity): its Gaussian, its tile, and a rank within the tile from the returning
+// atomic on the tile's counter (arbitrary order; the order pass restores increasing Gaussian ID)
 __global__ void __launch_bounds__(256) count_kernel(const int n, const int capacity, const float2 *__restrict__ xys,
                                                     const int *__restrict__ radii, const int *__restrict__ cum, const unsigned tiles_x,
-                                                    const unsigned tiles_y, int *__restrict__ tile_count) {
-    const int g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= n) return;
-    const int kept = kept_slots(cum, g, capacity);
-    if (kept == 0) return;
-    const float2 xy = __ldg(&xys[g]);
-    unsigned x0, y0, x1, y1;
-    tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
-    const unsigned width = x1 - x0, num_tiles = tiles_x * tiles_y;
-    if (width == 0) return;
-    for (int local = 0; local < kept; ++local) {
-        const unsigned tile = slot_tile(local, x0, y0, width, tiles_x);
-        if (tile < num_tiles) atomicAdd(&tile_count[tile], 1);
+                                                    const unsigned tiles_y, int *__restrict__ tile_count, int2 *__restrict__ slot_tile_rank,
+                                                    int *__restrict__ slot_gaussian) {
+    const int slots = min(__ldg(&cum[n - 1]), capacity);
+    const unsigned num_tiles = tiles_x * tiles_y;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < slots; idx += gridDim.x * blockDim.x) {
+        const int g = owner_of(cum, n, idx);
+        const int local = idx - (g > 0 ? __ldg(&cum[g - 1]) : 0);
+        const float2 xy = __ldg(&xys[g]);
+        unsigned x0, y0, x1, y1;
+        tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
+        const unsigned width = x1 - x0;
+        unsigned tile = num_tiles;  // inconsistent inputs (an empty footprint with slots): dropped
+        if (width > 0) tile = slot_tile(local, x0, y0, width, tiles_x);
+        int rank = -1;
+        if (tile < num_tiles) rank = atomicAdd(&tile_count[tile], 1);
+        slot_tile_rank[idx] = make_int2((int)tile, rank);
+        slot_gaussian[idx] = g;
     }
 }
 
-// Exclusive scan of the tile counts by one CTA: tile_bins[t] = (start, end), (0, 0) for empty tiles; the counts become write cursors
-__global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const int num_tiles, int *__restrict__ tile_count,
+// Exclusive scan of the tile counts by one CTA: tile_bins[t] = (start, end), (0, 0) for empty tiles
+__global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const int num_tiles, const int *__restrict__ tile_count,
                                                                  int2 *__restrict__ tile_bins, int *__restrict__ total_out) {
-    __shared__ int warp_sums[32];
-    const int per_thread = (num_tiles + kScanThreads - 1) / kScanThreads;
-    const int begin = min(num_tiles, (int)threadIdx.x * per_thread), end = min(num_tiles, begin + per_thread);
-    int run = 0;
-    for (int t = begin; t < end; ++t) run += tile_count[t];
-    int total;
-    const int inclusive = block_inclusive_scan(run, warp_sums, &total);
-    int start = inclusive - run;
-    for (int t = begin; t < end; ++t) {
-        const int count = tile_count[t];
-        tile_bins[t] = count > 0 ? make_int2(start, start + count) : make_int2(0, 0);
-        tile_count[t] = start;
-        start += count;
-    }
-    if (threadIdx.x == 0) *total_out = total;
+    const unsigned total = chunked_scan(tile_count, num_tiles, [&](int t, unsigned excl, unsigned v) {
+        tile_bins[t] = v > 0u ? make_int2((int)excl, (int)(excl + v)) : make_int2(0, 0);
+    });
+    if (threadIdx.x == 0) *total_out = (int)total;
 }
 
-__global__ void __launch_bounds__(256) scatter_kernel(const int n, const int capacity, const float2 *__restrict__ xys,
-                                                      const int *__restrict__ radii, const int *__restrict__ cum, const unsigned tiles_x,
-                                                      const unsigned tiles_y, int *__restrict__ tile_cursor, int *__restrict__ unsorted) {
-    const int g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= n) return;
-    const int kept = kept_slots(cum, g, capacity);
-    if (kept == 0) return;
-    const float2 xy = __ldg(&xys[g]);
-    unsigned x0, y0, x1, y1;
-    tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
-    const unsigned width = x1 - x0, num_tiles = tiles_x * tiles_y;
-    if (width == 0) return;
-    for (int local = 0; local < kept; ++local) {
-        const unsigned tile = slot_tile(local, x0, y0, width, tiles_x);
-        if (tile < num_tiles) unsorted[atomicAdd(&tile_cursor[tile], 1)] = g;
+// Each slot's Gaussian to its tile's range at its rank
+__global__ void __launch_bounds__(256) place_kernel(const int n, const int capacity, const int *__restrict__ cum, const unsigned num_tiles,
+                                                    const int2 *__restrict__ tile_bins, const int2 *__restrict__ slot_tile_rank,
+                                                    const int *__restrict__ slot_gaussian, int *__restrict__ unsorted) {
+    const int slots = min(__ldg(&cum[n - 1]), capacity);
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < slots; idx += gridDim.x * blockDim.x) {
+        const int2 tr = slot_tile_rank[idx];
+        if ((unsigned)tr.x < num_tiles) unsorted[tile_bins[tr.x].x + tr.y] = slot_gaussian[idx];
     }
 }
 
@@ -190,10 +211,12 @@ __global__ void __launch_bounds__(kOrderWarps * 32) order_kernel(const int num_t
     }
 }
 
+size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
+
 size_t sort_workspace_bytes(int capacity, int num_tiles) {
-    // tile counts / cursors, the intersection total, and the unsorted IDs, each 256-byte aligned
-    auto round = [](size_t b) { return (b + 255) & ~(size_t)255; };
-    return round(sizeof(int) * (size_t)num_tiles) + round(sizeof(int)) + round(sizeof(int) * (size_t)(capacity > 0 ? capacity : 0));
+    // tile counts, the intersection total, per-slot (tile, rank) and Gaussian, and the unsorted IDs
+    const size_t cap = capacity > 0 ? (size_t)capacity : 0;
+    return round256(sizeof(int) * (size_t)num_tiles) + round256(sizeof(int)) + round256(sizeof(int2) * cap) + 2 * round256(sizeof(int) * cap);
 }
 
 }  // namespace
@@ -237,21 +260,26 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
 
     char *ws = static_cast<char *>(workspace);
     int *tile_count = reinterpret_cast<int *>(ws);
-    ws += ((sizeof(int) * (size_t)num_tiles + 255) & ~(size_t)255);
+    ws += round256(sizeof(int) * (size_t)num_tiles);
     int *total = reinterpret_cast<int *>(ws);
-    ws += 256;
+    ws += round256(sizeof(int));
+    int2 *slot_tile_rank = reinterpret_cast<int2 *>(ws);
+    ws += round256(sizeof(int2) * (size_t)capacity);
+    int *slot_gaussian = reinterpret_cast<int *>(ws);
+    ws += round256(sizeof(int) * (size_t)capacity);
     int *unsorted = reinterpret_cast<int *>(ws);
 
     if (cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch("igs_sort_intersects");
-    const int blocks = igs::ceil_div(num_points, 256);
+    // slots are bounded by the capacity; a grid-stride loop over them reads the true count on the device
+    const int slot_blocks = std::min(igs::ceil_div(capacity, 256), 148 * 16);
     if (num_points > 0) {
-        count_kernel<<<blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
-                                            (unsigned)tiles_x, (unsigned)tiles_y, tile_count);
+        count_kernel<<<slot_blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
+                                                 (unsigned)tiles_x, (unsigned)tiles_y, tile_count, slot_tile_rank, slot_gaussian);
     }
     tile_scan_kernel<<<1, kScanThreads, 0, s>>>(num_tiles, tile_count, reinterpret_cast<int2 *>(tile_bins), total);
     if (num_points > 0) {
-        scatter_kernel<<<blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
-                                              (unsigned)tiles_x, (unsigned)tiles_y, tile_count, unsorted);
+        place_kernel<<<slot_blocks, 256, 0, s>>>(num_points, capacity, cum_tiles_hit, (unsigned)num_tiles,
+                                                 reinterpret_cast<const int2 *>(tile_bins), slot_tile_rank, slot_gaussian, unsorted);
     }
     order_kernel<<<igs::ceil_div(num_tiles, kOrderWarps), kOrderWarps * 32, 0, s>>>(num_tiles, capacity,
                                                                                     reinterpret_cast<const int2 *>(tile_bins), unsorted,

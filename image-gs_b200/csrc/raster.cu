@@ -17,10 +17,12 @@
 //
 // Backward (the math of nd_rasterize_backward_topk_norm_kernel, backward.cu:187-308): with D = 1e-4 + sum_k d_k and s_k = f_k . v_out,
 // v_sigma_k = -d_k (s_k / D - sum_j d_j s_j / D^2) and the colour weight d_k / D; per Gaussian v_conic += (v_sigma dx^2 / 2, v_sigma dx dy,
-// v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Each warp visits the union of its 32 pixels'
-// top-K Gaussians in increasing list position (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a
-// recursive-halving reduce-scatter, and adds them into per-tile accumulators in shared memory; at the end of the tile one global atomic per
-// (tile, Gaussian, value) flushes them, instead of one per (warp, Gaussian, value).
+// v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Two kernels:
+//   * raster_bwd_pairs_kernel (training step, tile lists up to 256 entries): the tile's (pixel, slot) pairs grouped by Gaussian in shared
+//     memory and summed in register runs, then one global atomic per (tile, Gaussian, value); see the comment above it;
+//   * raster_bwd_kernel (the [H, W, 10] operator and longer tile lists): each warp visits the union of its 32 pixels' top-K Gaussians in
+//     increasing key order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving
+//     reduce-scatter, and adds them into per-tile shared accumulators or directly to the outputs.
 #include "igs_common.cuh"
 
 namespace {
@@ -33,6 +35,8 @@ using igs::kTopK;
 
 constexpr int kThreads = kTilePixels;  // one thread per pixel of the tile
 constexpr int kChunk = 256;            // list entries staged per round in the forward pass
+constexpr int kPairStage = 256;        // longest tile list of the pairs-grouped backward pass
+constexpr int kPairs = kThreads * kTopK;
 // list entries staged by the backward pass (fewer for the widest value vectors, to stay within 48 KB of static shared memory); longer
 // lists read the Gaussians from global memory and accumulate with global atomics
 template <int NV>
@@ -96,7 +100,40 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
         }
         __syncthreads();
         if (!inside) continue;
-        for (int e = 0; e < count; ++e) {
+        int e = 0;
+        if (base == 0 && count >= kTopK) {
+            // Fast fill: when none of the list's first ten entries is skipped for this pixel they take slots 0..9 in order, exactly
+            // what the insertion rule does while slots are free, so they are written with fixed slot indices; otherwise start over.
+            bool all_valid = true;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const float4 q = s_geo[k];
+                const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[k], px, py);
+                all_valid = all_valid && !(sigma < 0.f || isnan(sigma) || isinf(sigma));
+                val[k] = __expf(-sigma);
+                pos[k] = k;
+            }
+            if (all_valid) {
+                filled = kTopK;
+                e = kTopK;
+                min_slot = 0;
+                min_val = val[0];
+#pragma unroll
+                for (int k = 1; k < kTopK; ++k) {
+                    if (val[k] < min_val) {
+                        min_slot = k;
+                        min_val = val[k];
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) {
+                    pos[k] = -1;
+                    val[k] = 0.f;
+                }
+            }
+        }
+        for (; e < count; ++e) {
             const float4 q = s_geo[e];
             const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
             if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
@@ -253,6 +290,7 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
     int2 range = make_int2(0, 0);
     if (by_position) range = tile_bins[tile];
     const int len = range.y - range.x;
+    if (by_position && len <= kPairStage) return;  // handled by raster_bwd_pairs_kernel
     const bool staged = by_position && len <= kBwdStage;
     if (staged) {
         for (int e = threadIdx.x; e < len; e += kThreads) {
@@ -384,6 +422,226 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
     }
 }
 
+// ---- backward pass from the tile lists, pairs grouped by Gaussian ---------------------------------------------------------------------
+//
+// For tiles whose list fits the stage (kPairStage entries), one CTA of 256 threads (one per pixel):
+//   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
+//      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
+//   2. the tile's (pixel, slot) pairs are grouped by list position: per slot, lanes holding the same entry find each other with
+//      __match_any_sync and one leader counts for the group; a scan of the counts gives each entry's segment; a second pass places the
+//      pairs, each group reserving its run with one atomic;
+//   3. each thread walks a run of ceil(pairs / 256) consecutive pairs and accumulates, per entry, the sums of v dx^2, v dx dy, v dy^2,
+//      v dx, v dy and w v_out in registers (dx, dy from the Gaussian's center), adding them into the entry's shared accumulators when the
+//      entry changes: one shared atomic per value and run, instead of one warp reduction per Gaussian and warp;
+//   4. per entry: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the reference's per-pixel v (a dx + b dy, b dx + c dy)
+//      summed), v_color = S_c, added to the outputs with one global atomic per value.
+template <int kMaxC>
+struct PairSmem {
+    float4 geo[kPairStage];          // x, y, conic a, conic b
+    float cc[kPairStage];            // conic c
+    float col[kPairStage * kMaxC];   // features
+    float2 vw[kTopK][kThreads];      // (dL/dsigma, colour weight) per slot and pixel
+    float vout[kMaxC][kThreads];     // dL/dout per channel and pixel
+    float2 pxy[kThreads];            // pixel coordinates
+    unsigned pairs[kPairs];          // (entry << 12) | (slot << 8) | pixel, grouped by entry
+    int count[kPairStage + 1];       // pairs per entry, then segment starts
+    int cursor[kPairStage];
+    float acc[kPairStage * (5 + kMaxC)];
+};
+
+template <int C>
+__global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
+                                                                    const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
+                                                                    const float2 *__restrict__ xys, const float *__restrict__ conics,
+                                                                    const float *__restrict__ colors, const float *__restrict__ v_output,
+                                                                    const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy,
+                                                                    float *__restrict__ v_conic, float *__restrict__ v_colors) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    constexpr int kNV = 5 + kMaxC;  // accumulated values per entry
+    const int channels = C > 0 ? C : channels_rt;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    PairSmem<kMaxC> &sm = *reinterpret_cast<PairSmem<kMaxC> *>(smem_raw);
+
+    const int tile = blockIdx.x;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+    if (len <= 0 || len > kPairStage) return;  // empty, or left to the global-memory kernel
+    const int tid = threadIdx.x, lane = tid & 31;
+    const PixelCoord pc = tile_pixel(tile, tiles_x);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const float px = (float)pc.j, py = (float)pc.i;
+    const int num_pixels = img_h * img_w;
+    const int p = inside ? pc.i * img_w + pc.j : 0;
+
+    for (int e = tid; e < len; e += kThreads) {
+        const int g = __ldg(&ids_sorted[range.x + e]);
+        const float2 xy = __ldg(&xys[g]);
+        sm.geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+        sm.cc[e] = __ldg(&conics[3 * g + 2]);
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+        sm.count[e] = 0;
+    }
+    for (int e = tid; e < len * kNV; e += kThreads) sm.acc[e] = 0.f;
+    sm.pxy[tid] = make_float2(px, py);
+    __syncthreads();
+
+    // 1. per-pixel gradients with respect to sigma and the colour weights
+    float v_out[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+        v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
+        sm.vout[c][tid] = v_out[c];
+    }
+    int key[kTopK];
+    float d[kTopK];
+    float denom = (float)igs::kNormEps;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
+        key[k] = v == kNoSlot ? -1 : (int)v;
+        d[k] = 0.f;
+        if (key[k] < 0) continue;
+        const float4 q = sm.geo[key[k]];
+        d[k] = __expf(-gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[key[k]], px, py));
+        denom += d[k];
+    }
+    float s[kTopK];
+    float shared = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        s[k] = 0.f;
+        if (key[k] < 0) continue;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
+        shared += -d[k] / (denom * denom) * s[k];
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] / denom + shared), d[k] / denom);
+
+    // 2. group the pairs by entry: count per entry (one atomic per group of lanes sharing it), scan, place
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const unsigned peers = __match_any_sync(0xffffffffu, key[k]);
+        if (key[k] >= 0 && lane == __ffs(peers) - 1) atomicAdd(&sm.count[key[k]], __popc(peers));
+    }
+    __syncthreads();
+    if (tid < 32) {
+        // exclusive scan of count[0, len) by one warp, kPairStage / 32 entries per lane
+        constexpr int kPer = kPairStage / 32;
+        int local[kPer], run = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int e = lane * kPer + j;
+            local[j] = e < len ? sm.count[e] : 0;
+            run += local[j];
+        }
+        int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        int start = incl - run;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int e = lane * kPer + j;
+            if (e < len) {
+                sm.count[e] = start;
+                sm.cursor[e] = start;
+            }
+            start += local[j];
+        }
+        if (lane == 31) sm.count[len] = incl;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const unsigned peers = __match_any_sync(0xffffffffu, key[k]);
+        const int leader = __ffs(peers) - 1;
+        int base = 0;
+        if (key[k] >= 0 && lane == leader) base = atomicAdd(&sm.cursor[key[k]], __popc(peers));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        if (key[k] >= 0) sm.pairs[base + __popc(peers & ((1u << lane) - 1u))] = ((unsigned)key[k] << 12) | ((unsigned)k << 8) | (unsigned)tid;
+    }
+    __syncthreads();
+
+    // 3. runs of pairs: per-entry sums in registers, added to the shared accumulators when the entry changes
+    const int total = sm.count[len];
+    const int per = (total + kThreads - 1) / kThreads;
+    const int begin = min(total, tid * per), end = min(total, begin + per);
+    int cur = -1;
+    float gx = 0.f, gy = 0.f;
+    float a_xx = 0.f, a_xy = 0.f, a_yy = 0.f, a_x = 0.f, a_y = 0.f, a_c[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) a_c[c] = 0.f;
+    auto flush = [&]() {
+        float *dst = &sm.acc[cur * kNV];
+        atomicAdd(dst + 0, a_xx);
+        atomicAdd(dst + 1, a_xy);
+        atomicAdd(dst + 2, a_yy);
+        atomicAdd(dst + 3, a_x);
+        atomicAdd(dst + 4, a_y);
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) atomicAdd(dst + 5 + c, a_c[c]);
+    };
+    for (int i = begin; i < end; ++i) {
+        const unsigned rec = sm.pairs[i];
+        const int entry = (int)(rec >> 12), slot = (int)((rec >> 8) & 15u), pix = (int)(rec & 255u);
+        if (entry != cur) {
+            if (cur >= 0) flush();
+            cur = entry;
+            const float4 q = sm.geo[entry];
+            gx = q.x;
+            gy = q.y;
+            a_xx = a_xy = a_yy = a_x = a_y = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) a_c[c] = 0.f;
+        }
+        const float2 vw = sm.vw[slot][pix];
+        const float2 xy = sm.pxy[pix];
+        const float dx = gx - xy.x, dy = gy - xy.y;
+        const float tx = vw.x * dx, ty = vw.x * dy;
+        a_xx = fmaf(tx, dx, a_xx);
+        a_xy = fmaf(tx, dy, a_xy);
+        a_yy = fmaf(ty, dy, a_yy);
+        a_x += tx;
+        a_y += ty;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) a_c[c] = fmaf(vw.y, sm.vout[c][pix], a_c[c]);
+    }
+    if (cur >= 0) flush();
+    __syncthreads();
+
+    // 4. per entry and output value, one global atomic
+    const int nout = 5 + channels;
+    for (int e = tid; e < len * nout; e += kThreads) {
+        const int entry = e / nout, o = e % nout;
+        const float *A = &sm.acc[entry * kNV];
+        float value;
+        if (o == 0 || o == 2) {
+            value = 0.5f * A[o];
+        } else if (o == 1) {
+            value = A[1];
+        } else if (o == 3) {
+            const float4 q = sm.geo[entry];
+            value = q.z * A[3] + q.w * A[4];
+        } else if (o == 4) {
+            value = sm.geo[entry].w * A[3] + sm.cc[entry] * A[4];
+        } else {
+            value = A[o];
+        }
+        if (value == 0.f) continue;
+        const int g = __ldg(&ids_sorted[range.x + entry]);
+        float *target = o < 3 ? v_conic + 3 * (size_t)g + o : o < 5 ? v_xy + 2 * (size_t)g + (o - 3) : v_colors + (size_t)g * channels + (o - 5);
+        atomicAdd(target, value);
+    }
+}
+
 template <int C>
 cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
                        const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk, cudaStream_t s) {
@@ -427,6 +685,20 @@ cudaError_t launch_bwd(int tiles, int tiles_x, int img_h, int img_w, int channel
     return cudaGetLastError();
 }
 
+template <int C>
+cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
+                             const float *conics, const float *colors, const float *v_output, const uint16_t *tile_topk, float *v_xy,
+                             float *v_conic, float *v_colors, cudaStream_t s) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    const size_t bytes = sizeof(PairSmem<kMaxC>);
+    // more than the 48 KB default of dynamic shared memory (set on every call: cheap, and correct for whichever device is current)
+    cudaError_t err = cudaFuncSetAttribute(raster_bwd_pairs_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err != cudaSuccess) return err;
+    raster_bwd_pairs_kernel<C><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
+                                                              tile_topk, v_xy, v_conic, v_colors);
+    return cudaGetLastError();
+}
+
 int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys,
                const float *conics, const float *colors, const float *v_output, const int32_t *pixel_topk, const uint16_t *tile_topk,
                float *v_xy, float *v_conic, float *v_colors, void *stream, const char *who) {
@@ -449,7 +721,19 @@ int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t
     IGS_REQUIRE(igs::aligned(xys, 8), "%s: xys must be 8-byte aligned", who);
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
-    cudaError_t err;
+    cudaError_t err = cudaSuccess;
+    if (tile_topk != nullptr) {
+        // tiles with lists up to kPairStage entries; the union-walk kernel below takes the longer ones
+        if (channels == 3)
+            err = launch_bwd_pairs<3>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        else if (channels == 1)
+            err = launch_bwd_pairs<1>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        else if (channels == 9)
+            err = launch_bwd_pairs<9>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        else
+            err = launch_bwd_pairs<0>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+    }
     if (channels == 3)
         err = launch_bwd<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
     else if (channels <= 3)
