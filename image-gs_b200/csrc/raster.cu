@@ -427,37 +427,52 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 // For tiles whose list fits the stage (kPairStage entries), one CTA of 256 threads (one per pixel):
 //   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
 //      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
-//   2. the tile's (pixel, slot) pairs are grouped by list position: per slot, lanes holding the same entry find each other with
-//      __match_any_sync and one leader counts for the group; a scan of the counts gives each entry's segment; a second pass places the
-//      pairs, each group reserving its run with one atomic;
-//   3. each thread walks a run of ceil(pairs / 256) consecutive pairs and accumulates, per entry, the sums of v dx^2, v dx dy, v dy^2,
-//      v dx, v dy and w v_out in registers (dx, dy from the Gaussian's center), adding them into the entry's shared accumulators when the
-//      entry changes: one shared atomic per value and run, instead of one warp reduction per Gaussian and warp;
-//   4. per entry: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the reference's per-pixel v (a dx + b dy, b dx + c dy)
-//      summed), v_color = S_c, added to the outputs with one global atomic per value.
+//   2. the tile's (pixel, slot) pairs are grouped by list position (a counting sort in shared memory): per slot, each warp visits the
+//      distinct entries its lanes hold (one step when all lanes agree) and one lane per group counts or reserves the group's run;
+//   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
+//      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v dx, v dy and w v_out (dx, dy from the Gaussian's center), then one
+//      reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the
+//      reference's per-pixel v (a dx + b dy, b dx + c dy) summed), v_color = S_c.
 template <int kMaxC>
 struct PairSmem {
-    float4 geo[kPairStage];          // x, y, conic a, conic b
-    float cc[kPairStage];            // conic c
-    float col[kPairStage * kMaxC];   // features
-    float2 vw[kTopK][kThreads];      // (dL/dsigma, colour weight) per slot and pixel
-    float vout[kMaxC][kThreads];     // dL/dout per channel and pixel
-    float2 pxy[kThreads];            // pixel coordinates
-    unsigned pairs[kPairs];          // (entry << 12) | (slot << 8) | pixel, grouped by entry
-    int count[kPairStage + 1];       // pairs per entry, then segment starts
+    float4 geo[kPairStage];            // x, y, conic a, conic b
+    float cc[kPairStage];              // conic c
+    float col[kPairStage * kMaxC];     // features
+    float2 vw[kTopK][kThreads];        // (dL/dsigma, colour weight) per slot and pixel
+    float vout[kMaxC][kThreads];       // dL/dout per channel and pixel
+    float2 pxy[kThreads];              // pixel coordinates
+    uint16_t pairs[kPairs];            // (slot << 8) | pixel, grouped by entry
+    int start[kPairStage + 1];         // pairs per entry, then segment starts
     int cursor[kPairStage];
-    float acc[kPairStage * (5 + kMaxC)];
 };
 
-template <int C>
+// Calls fn(key, peers) once per distinct valid key among the warp's lanes, from the lane `leader` of each group (the group's lowest lane)
+template <typename Fn>
+__device__ __forceinline__ void for_each_group(int key, int lane, Fn fn) {
+    const int first = __shfl_sync(0xffffffffu, key, 0);
+    if (__all_sync(0xffffffffu, key == first)) {  // the common case: the slot holds the same entry in the whole patch
+        if (first >= 0) fn(first, 0xffffffffu, 0);
+        return;
+    }
+    unsigned todo = __ballot_sync(0xffffffffu, key >= 0);
+    while (todo) {
+        const int leader = __ffs(todo) - 1;
+        const int k = __shfl_sync(0xffffffffu, key, leader);
+        const unsigned peers = __ballot_sync(0xffffffffu, key == k);
+        fn(k, peers, leader);
+        todo &= ~peers;
+    }
+}
+
+template <int C, int NV>
 __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
                                                                     const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
                                                                     const float2 *__restrict__ xys, const float *__restrict__ conics,
                                                                     const float *__restrict__ colors, const float *__restrict__ v_output,
                                                                     const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy,
                                                                     float *__restrict__ v_conic, float *__restrict__ v_colors) {
-    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
-    constexpr int kNV = 5 + kMaxC;  // accumulated values per entry
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
+    static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry sums and the channels");
     const int channels = C > 0 ? C : channels_rt;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PairSmem<kMaxC> &sm = *reinterpret_cast<PairSmem<kMaxC> *>(smem_raw);
@@ -466,7 +481,7 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     const int2 range = tile_bins[tile];
     const int len = range.y - range.x;
     if (len <= 0 || len > kPairStage) return;  // empty, or left to the global-memory kernel
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PixelCoord pc = tile_pixel(tile, tiles_x);
     const bool inside = pc.i < img_h && pc.j < img_w;
     const float px = (float)pc.j, py = (float)pc.i;
@@ -481,9 +496,8 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)
             if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
-        sm.count[e] = 0;
+        sm.start[e] = 0;
     }
-    for (int e = tid; e < len * kNV; e += kThreads) sm.acc[e] = 0.f;
     sm.pxy[tid] = make_float2(px, py);
     __syncthreads();
 
@@ -521,21 +535,20 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] / denom + shared), d[k] / denom);
 
-    // 2. group the pairs by entry: count per entry (one atomic per group of lanes sharing it), scan, place
+    // 2. counting sort of the pairs by entry
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        const unsigned peers = __match_any_sync(0xffffffffu, key[k]);
-        if (key[k] >= 0 && lane == __ffs(peers) - 1) atomicAdd(&sm.count[key[k]], __popc(peers));
-    }
+    for (int k = 0; k < kTopK; ++k)
+        for_each_group(key[k], lane, [&](int e, unsigned peers, int leader) {
+            if (lane == leader) atomicAdd(&sm.start[e], __popc(peers));
+        });
     __syncthreads();
-    if (tid < 32) {
-        // exclusive scan of count[0, len) by one warp, kPairStage / 32 entries per lane
-        constexpr int kPer = kPairStage / 32;
+    if (warp == 0) {
+        constexpr int kPer = kPairStage / 32;  // exclusive scan of the counts by one warp
         int local[kPer], run = 0;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int e = lane * kPer + j;
-            local[j] = e < len ? sm.count[e] : 0;
+            local[j] = e < len ? sm.start[e] : 0;
             run += local[j];
         }
         int incl = run;
@@ -548,97 +561,69 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int e = lane * kPer + j;
-            if (e < len) {
-                sm.count[e] = start;
-                sm.cursor[e] = start;
-            }
+            if (e < len) sm.start[e] = sm.cursor[e] = start;
             start += local[j];
         }
-        if (lane == 31) sm.count[len] = incl;
+        if (lane == 31) sm.start[len] = incl;
     }
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        const unsigned peers = __match_any_sync(0xffffffffu, key[k]);
-        const int leader = __ffs(peers) - 1;
-        int base = 0;
-        if (key[k] >= 0 && lane == leader) base = atomicAdd(&sm.cursor[key[k]], __popc(peers));
-        base = __shfl_sync(0xffffffffu, base, leader);
-        if (key[k] >= 0) sm.pairs[base + __popc(peers & ((1u << lane) - 1u))] = ((unsigned)key[k] << 12) | ((unsigned)k << 8) | (unsigned)tid;
-    }
-    __syncthreads();
-
-    // 3. runs of pairs: per-entry sums in registers, added to the shared accumulators when the entry changes
-    const int total = sm.count[len];
-    const int per = (total + kThreads - 1) / kThreads;
-    const int begin = min(total, tid * per), end = min(total, begin + per);
-    int cur = -1;
-    float gx = 0.f, gy = 0.f;
-    float a_xx = 0.f, a_xy = 0.f, a_yy = 0.f, a_x = 0.f, a_y = 0.f, a_c[kMaxC];
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) a_c[c] = 0.f;
-    auto flush = [&]() {
-        float *dst = &sm.acc[cur * kNV];
-        atomicAdd(dst + 0, a_xx);
-        atomicAdd(dst + 1, a_xy);
-        atomicAdd(dst + 2, a_yy);
-        atomicAdd(dst + 3, a_x);
-        atomicAdd(dst + 4, a_y);
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) atomicAdd(dst + 5 + c, a_c[c]);
-    };
-    for (int i = begin; i < end; ++i) {
-        const unsigned rec = sm.pairs[i];
-        const int entry = (int)(rec >> 12), slot = (int)((rec >> 8) & 15u), pix = (int)(rec & 255u);
-        if (entry != cur) {
-            if (cur >= 0) flush();
-            cur = entry;
-            const float4 q = sm.geo[entry];
-            gx = q.x;
-            gy = q.y;
-            a_xx = a_xy = a_yy = a_x = a_y = 0.f;
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c) a_c[c] = 0.f;
-        }
-        const float2 vw = sm.vw[slot][pix];
-        const float2 xy = sm.pxy[pix];
-        const float dx = gx - xy.x, dy = gy - xy.y;
-        const float tx = vw.x * dx, ty = vw.x * dy;
-        a_xx = fmaf(tx, dx, a_xx);
-        a_xy = fmaf(tx, dy, a_xy);
-        a_yy = fmaf(ty, dy, a_yy);
-        a_x += tx;
-        a_y += ty;
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) a_c[c] = fmaf(vw.y, sm.vout[c][pix], a_c[c]);
-    }
-    if (cur >= 0) flush();
+    for (int k = 0; k < kTopK; ++k)
+        for_each_group(key[k], lane, [&](int e, unsigned peers, int leader) {
+            int base = 0;
+            if (lane == leader) base = atomicAdd(&sm.cursor[e], __popc(peers));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (peers & (1u << lane)) sm.pairs[base + __popc(peers & ((1u << lane) - 1u))] = (uint16_t)((k << 8) | tid);
+        });
     __syncthreads();
 
-    // 4. per entry and output value, one global atomic
-    const int nout = 5 + channels;
-    for (int e = tid; e < len * nout; e += kThreads) {
-        const int entry = e / nout, o = e % nout;
-        const float *A = &sm.acc[entry * kNV];
-        float value;
-        if (o == 0 || o == 2) {
-            value = 0.5f * A[o];
-        } else if (o == 1) {
-            value = A[1];
-        } else if (o == 3) {
-            const float4 q = sm.geo[entry];
-            value = q.z * A[3] + q.w * A[4];
-        } else if (o == 4) {
-            value = sm.geo[entry].w * A[3] + sm.cc[entry] * A[4];
-        } else {
-            value = A[o];
+    // 3. one warp per entry
+    const int value_index = halving_index<NV>(lane);
+    const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    const int lane_of_x = 3 * (32 / NV) - 0, lane_of_y = 4 * (32 / NV);  // lanes holding S_x and S_y after the reduce-scatter
+    for (int e = warp; e < len; e += kThreads / 32) {
+        const int b = sm.start[e], n = sm.start[e + 1] - b;
+        if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
+        const float4 q = sm.geo[e];
+        float acc[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const unsigned rec = sm.pairs[b + i];
+            const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
+            const float2 vw = sm.vw[slot][pix];
+            const float2 xy = sm.pxy[pix];
+            const float dx = q.x - xy.x, dy = q.y - xy.y;
+            const float tx = vw.x * dx, ty = vw.x * dy;
+            acc[0] = fmaf(tx, dx, acc[0]);
+            acc[1] = fmaf(tx, dy, acc[1]);
+            acc[2] = fmaf(ty, dy, acc[2]);
+            acc[3] += tx;
+            acc[4] += ty;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) acc[5 + c] = fmaf(vw.y, sm.vout[c][pix], acc[5 + c]);
         }
-        if (value == 0.f) continue;
-        const int g = __ldg(&ids_sorted[range.x + entry]);
-        float *target = o < 3 ? v_conic + 3 * (size_t)g + o : o < 5 ? v_xy + 2 * (size_t)g + (o - 3) : v_colors + (size_t)g * channels + (o - 5);
-        atomicAdd(target, value);
+        const float total = warp_sum_scatter<NV>(acc, lane);
+        const float sx = __shfl_sync(0xffffffffu, total, lane_of_x), sy = __shfl_sync(0xffffffffu, total, lane_of_y);
+        if (holds_total) {
+            const int g = __ldg(&ids_sorted[range.x + e]);
+            float value, *target;
+            if (value_index < 3) {
+                value = value_index == 1 ? total : 0.5f * total;
+                target = v_conic + 3 * (size_t)g + value_index;
+            } else if (value_index == 3) {
+                value = q.z * sx + q.w * sy;
+                target = v_xy + 2 * (size_t)g;
+            } else if (value_index == 4) {
+                value = q.w * sx + sm.cc[e] * sy;
+                target = v_xy + 2 * (size_t)g + 1;
+            } else {
+                value = total;
+                target = v_colors + (size_t)g * channels + (value_index - 5);
+            }
+            if (value != 0.f) atomicAdd(target, value);
+        }
     }
 }
 
@@ -685,17 +670,17 @@ cudaError_t launch_bwd(int tiles, int tiles_x, int img_h, int img_w, int channel
     return cudaGetLastError();
 }
 
-template <int C>
+template <int C, int NV>
 cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
                              const float *conics, const float *colors, const float *v_output, const uint16_t *tile_topk, float *v_xy,
                              float *v_conic, float *v_colors, cudaStream_t s) {
-    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
     const size_t bytes = sizeof(PairSmem<kMaxC>);
     // more than the 48 KB default of dynamic shared memory (set on every call: cheap, and correct for whichever device is current)
-    cudaError_t err = cudaFuncSetAttribute(raster_bwd_pairs_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    cudaError_t err = cudaFuncSetAttribute(raster_bwd_pairs_kernel<C, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (err != cudaSuccess) return err;
-    raster_bwd_pairs_kernel<C><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
-                                                              tile_topk, v_xy, v_conic, v_colors);
+    raster_bwd_pairs_kernel<C, NV><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
+                                                                  tile_topk, v_xy, v_conic, v_colors);
     return cudaGetLastError();
 }
 
@@ -725,13 +710,15 @@ int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t
     if (tile_topk != nullptr) {
         // tiles with lists up to kPairStage entries; the union-walk kernel below takes the longer ones
         if (channels == 3)
-            err = launch_bwd_pairs<3>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        else if (channels == 1)
-            err = launch_bwd_pairs<1>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        else if (channels <= 3)
+            err = launch_bwd_pairs<0, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else if (channels == 9)
-            err = launch_bwd_pairs<9>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<9, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+        else if (channels <= 11)
+            err = launch_bwd_pairs<0, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else
-            err = launch_bwd_pairs<0>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<0, 32>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     }
     if (channels == 3)
