@@ -94,11 +94,80 @@ __device__ __forceinline__ unsigned chunked_scan(const int *__restrict__ in, int
     return carry;
 }
 
-// Inclusive int32 prefix sum (wrapping, as torch.cumsum in int32) by one CTA
-__global__ void __launch_bounds__(kScanThreads) cumsum_kernel(const int n, const int *__restrict__ in, int *__restrict__ out,
-                                                              int *__restrict__ total_out) {
-    const unsigned total = chunked_scan(in, n, [&](int i, unsigned excl, unsigned v) { out[i] = (int)(excl + v); });
-    if (threadIdx.x == 0 && total_out) *total_out = (int)total;
+// Inclusive int32 prefix sum (wrapping, as torch.cumsum in int32) in two fully parallel passes over blocks of kCumBlock elements: the
+// block sums, then each block's offset (the sum of the preceding block sums, reduced by the block) and the scan of its own elements
+constexpr int kCumThreads = 256;
+constexpr int kCumItems = 8;
+constexpr int kCumBlock = kCumThreads * kCumItems;
+
+__device__ __forceinline__ void load_items(const int *__restrict__ in, int n, int first, unsigned (&v)[kCumItems]) {
+    if (first + kCumItems <= n && (reinterpret_cast<uintptr_t>(in + first) & 15) == 0) {
+        const int4 a = __ldg(reinterpret_cast<const int4 *>(in + first));
+        const int4 b = __ldg(reinterpret_cast<const int4 *>(in + first) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kCumItems; ++k) v[k] = first + k < n ? (unsigned)__ldg(&in[first + k]) : 0u;
+    }
+}
+
+__device__ __forceinline__ unsigned block_sum_u32(unsigned v, unsigned *scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    unsigned t = 0u;
+#pragma unroll
+    for (int w = 0; w < kCumThreads / 32; ++w) t += scratch[w];
+    __syncthreads();
+    return t;
+}
+
+__global__ void __launch_bounds__(kCumThreads) cumsum_partials_kernel(const int n, const int *__restrict__ in, unsigned *__restrict__ partials) {
+    __shared__ unsigned scratch[kCumThreads / 32];
+    unsigned v[kCumItems], run = 0u;
+    load_items(in, n, blockIdx.x * kCumBlock + threadIdx.x * kCumItems, v);
+#pragma unroll
+    for (int k = 0; k < kCumItems; ++k) run += v[k];
+    const unsigned t = block_sum_u32(run, scratch);
+    if (threadIdx.x == 0) partials[blockIdx.x] = t;
+}
+
+__global__ void __launch_bounds__(kCumThreads) cumsum_scan_kernel(const int n, const int *__restrict__ in, const unsigned *__restrict__ partials,
+                                                                  int *__restrict__ out, int *__restrict__ total_out) {
+    __shared__ unsigned scratch[kCumThreads / 32];
+    unsigned before = 0u;
+    for (int b = threadIdx.x; b < (int)blockIdx.x; b += kCumThreads) before += partials[b];
+    before = block_sum_u32(before, scratch);
+    const int first = blockIdx.x * kCumBlock + threadIdx.x * kCumItems;
+    unsigned v[kCumItems], run = 0u;
+    load_items(in, n, first, v);
+#pragma unroll
+    for (int k = 0; k < kCumItems; ++k) run += v[k];
+    // exclusive scan of the per-thread runs within the block
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned m = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += m;
+    }
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    unsigned warp_before = 0u, block_total = 0u;
+#pragma unroll
+    for (int w = 0; w < kCumThreads / 32; ++w) {
+        warp_before += w < warp ? scratch[w] : 0u;
+        block_total += scratch[w];
+    }
+    unsigned acc = before + warp_before + incl - run;
+#pragma unroll
+    for (int k = 0; k < kCumItems; ++k) {
+        acc += v[k];
+        if (first + k < n) out[first + k] = (int)acc;
+    }
+    if (total_out && blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) *total_out = (int)(before + block_total);
 }
 
 // Tile key of slot `local` of a Gaussian's footprint: row-major position in its tile rectangle (forward.cu:102-103 of the reference)
@@ -223,16 +292,22 @@ size_t sort_workspace_bytes(int capacity, int num_tiles) {
 
 extern "C" {
 
-size_t igs_cumsum_workspace(int n) { return 0; }
+size_t igs_cumsum_workspace(int n) { return sizeof(unsigned) * (size_t)igs::ceil_div(n > 0 ? n : 1, kCumBlock); }
 
-int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *stream) {
+int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *workspace, size_t workspace_bytes,
+               void *stream) {
     IGS_REQUIRE(n >= 0, "igs_cumsum: negative size");
+    cudaStream_t s = igs::as_stream(stream);
     if (n == 0) {
-        if (total) return cudaMemsetAsync(total, 0, sizeof(int), igs::as_stream(stream)) == cudaSuccess ? IGS_OK : igs::check_launch("igs_cumsum");
+        if (total && cudaMemsetAsync(total, 0, sizeof(int), s) != cudaSuccess) return igs::check_launch("igs_cumsum");
         return IGS_OK;
     }
-    IGS_REQUIRE(num_tiles_hit && cum_tiles_hit, "igs_cumsum: null pointer");
-    cumsum_kernel<<<1, kScanThreads, 0, igs::as_stream(stream)>>>(n, num_tiles_hit, cum_tiles_hit, total);
+    IGS_REQUIRE(num_tiles_hit && cum_tiles_hit && workspace, "igs_cumsum: null pointer");
+    IGS_REQUIRE(workspace_bytes >= igs_cumsum_workspace(n), "igs_cumsum: workspace too small");
+    const int blocks = igs::ceil_div(n, kCumBlock);
+    unsigned *partials = static_cast<unsigned *>(workspace);
+    cumsum_partials_kernel<<<blocks, kCumThreads, 0, s>>>(n, num_tiles_hit, partials);
+    cumsum_scan_kernel<<<blocks, kCumThreads, 0, s>>>(n, num_tiles_hit, partials, cum_tiles_hit, total);
     return igs::check_launch("igs_cumsum");
 }
 

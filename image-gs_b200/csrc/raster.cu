@@ -18,9 +18,9 @@
 // Backward (the math of nd_rasterize_backward_topk_norm_kernel, backward.cu:187-308): with D = 1e-4 + sum_k d_k and s_k = f_k . v_out,
 // v_sigma_k = -d_k (s_k / D - sum_j d_j s_j / D^2) and the colour weight d_k / D; per Gaussian v_conic += (v_sigma dx^2 / 2, v_sigma dx dy,
 // v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Two kernels:
-//   * raster_bwd_pairs_kernel (training step, tile lists up to 256 entries): the tile's (pixel, slot) pairs grouped by Gaussian in shared
-//     memory and summed in register runs, then one global atomic per (tile, Gaussian, value); see the comment above it;
-//   * raster_bwd_kernel (the [H, W, 10] operator and longer tile lists): each warp visits the union of its 32 pixels' top-K Gaussians in
+//   * raster_bwd_pairs_kernel (training step, from the tile lists): the tile's (pixel, slot) pairs grouped by Gaussian in shared memory,
+//     one warp per Gaussian summing its pairs, then one global atomic per (tile, Gaussian, value); see the comment above it;
+//   * raster_bwd_kernel (the [H, W, 10] operator): each warp visits the union of its 32 pixels' top-K Gaussians in
 //     increasing key order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving
 //     reduce-scatter, and adds them into per-tile shared accumulators or directly to the outputs.
 #include "igs_common.cuh"
@@ -290,7 +290,6 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
     int2 range = make_int2(0, 0);
     if (by_position) range = tile_bins[tile];
     const int len = range.y - range.x;
-    if (by_position && len <= kPairStage) return;  // handled by raster_bwd_pairs_kernel
     const bool staged = by_position && len <= kBwdStage;
     if (staged) {
         for (int e = threadIdx.x; e < len; e += kThreads) {
@@ -424,11 +423,11 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 
 // ---- backward pass from the tile lists, pairs grouped by Gaussian ---------------------------------------------------------------------
 //
-// For tiles whose list fits the stage (kPairStage entries), one CTA of 256 threads (one per pixel):
+// One CTA of 256 threads (one per pixel) per tile; lists longer than kPairStage entries go through steps 2-3 in chunks of kPairStage:
 //   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
 //      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
-//   2. the tile's (pixel, slot) pairs are grouped by list position (a counting sort in shared memory): per slot, each warp visits the
-//      distinct entries its lanes hold (one step when all lanes agree) and one lane per group counts or reserves the group's run;
+//   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory (per-pair shared atomics
+//      count each entry's pairs; a one-warp scan gives the segments; a returning atomic per pair takes a place in its segment);
 //   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
 //      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v dx, v dy and w v_out (dx, dy from the Gaussian's center), then one
 //      reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the
@@ -446,24 +445,6 @@ struct PairSmem {
     int cursor[kPairStage];
 };
 
-// Calls fn(key, peers) once per distinct valid key among the warp's lanes, from the lane `leader` of each group (the group's lowest lane)
-template <typename Fn>
-__device__ __forceinline__ void for_each_group(int key, int lane, Fn fn) {
-    const int first = __shfl_sync(0xffffffffu, key, 0);
-    if (__all_sync(0xffffffffu, key == first)) {  // the common case: the slot holds the same entry in the whole patch
-        if (first >= 0) fn(first, 0xffffffffu, 0);
-        return;
-    }
-    unsigned todo = __ballot_sync(0xffffffffu, key >= 0);
-    while (todo) {
-        const int leader = __ffs(todo) - 1;
-        const int k = __shfl_sync(0xffffffffu, key, leader);
-        const unsigned peers = __ballot_sync(0xffffffffu, key == k);
-        fn(k, peers, leader);
-        todo &= ~peers;
-    }
-}
-
 template <int C, int NV>
 __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
                                                                     const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
@@ -480,7 +461,7 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     const int tile = blockIdx.x;
     const int2 range = tile_bins[tile];
     const int len = range.y - range.x;
-    if (len <= 0 || len > kPairStage) return;  // empty, or left to the global-memory kernel
+    if (len <= 0) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PixelCoord pc = tile_pixel(tile, tiles_x);
     const bool inside = pc.i < img_h && pc.j < img_w;
@@ -488,37 +469,55 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     const int num_pixels = img_h * img_w;
     const int p = inside ? pc.i * img_w + pc.j : 0;
 
-    for (int e = tid; e < len; e += kThreads) {
-        const int g = __ldg(&ids_sorted[range.x + e]);
-        const float2 xy = __ldg(&xys[g]);
-        sm.geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-        sm.cc[e] = __ldg(&conics[3 * g + 2]);
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
-        sm.start[e] = 0;
-    }
-    sm.pxy[tid] = make_float2(px, py);
-    __syncthreads();
-
-    // 1. per-pixel gradients with respect to sigma and the colour weights
+    // the pixel's loads, issued before the staging barrier so that their latency overlaps it
     float v_out[kMaxC];
 #pragma unroll
-    for (int c = 0; c < kMaxC; ++c) {
-        v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
-        sm.vout[c][tid] = v_out[c];
-    }
+    for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
     int key[kTopK];
-    float d[kTopK];
-    float denom = (float)igs::kNormEps;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
         const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
         key[k] = v == kNoSlot ? -1 : (int)v;
+    }
+
+    // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
+    // memory in step 1)
+    auto stage = [&](int chunk) {
+        const int n = min(kPairStage, len - chunk);
+        for (int e = tid; e < n; e += kThreads) {
+            const int g = __ldg(&ids_sorted[range.x + chunk + e]);
+            const float2 xy = __ldg(&xys[g]);
+            sm.geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            sm.cc[e] = __ldg(&conics[3 * g + 2]);
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+            sm.start[e] = 0;
+        }
+    };
+    stage(0);
+    sm.pxy[tid] = make_float2(px, py);
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+    __syncthreads();
+
+    // 1. per-pixel gradients with respect to sigma and the colour weights
+    float d[kTopK];
+    float denom = (float)igs::kNormEps;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
         d[k] = 0.f;
         if (key[k] < 0) continue;
-        const float4 q = sm.geo[key[k]];
-        d[k] = __expf(-gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[key[k]], px, py));
+        float gx, gy, a, b, c;
+        if (key[k] < kPairStage) {
+            const float4 q = sm.geo[key[k]];
+            gx = q.x, gy = q.y, a = q.z, b = q.w, c = sm.cc[key[k]];
+        } else {
+            const int g = __ldg(&ids_sorted[range.x + key[k]]);
+            const float2 xy = __ldg(&xys[g]);
+            gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
+        }
+        d[k] = __expf(-gaussian_sigma(gx, gy, a, b, c, px, py));
         denom += d[k];
     }
     float s[kTopK];
@@ -527,102 +526,115 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     for (int k = 0; k < kTopK; ++k) {
         s[k] = 0.f;
         if (key[k] < 0) continue;
+        if (key[k] < kPairStage) {
 #pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
+        } else {
+            const int g = __ldg(&ids_sorted[range.x + key[k]]);
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += __ldg(&colors[(size_t)g * channels + c]) * v_out[c];
+        }
         shared += -d[k] / (denom * denom) * s[k];
     }
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] / denom + shared), d[k] / denom);
 
-    // 2. counting sort of the pairs by entry
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k)
-        for_each_group(key[k], lane, [&](int e, unsigned peers, int leader) {
-            if (lane == leader) atomicAdd(&sm.start[e], __popc(peers));
-        });
-    __syncthreads();
-    if (warp == 0) {
-        constexpr int kPer = kPairStage / 32;  // exclusive scan of the counts by one warp
-        int local[kPer], run = 0;
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const int e = lane * kPer + j;
-            local[j] = e < len ? sm.start[e] : 0;
-            run += local[j];
-        }
-        int incl = run;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += n;
-        }
-        int start = incl - run;
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const int e = lane * kPer + j;
-            if (e < len) sm.start[e] = sm.cursor[e] = start;
-            start += local[j];
-        }
-        if (lane == 31) sm.start[len] = incl;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k)
-        for_each_group(key[k], lane, [&](int e, unsigned peers, int leader) {
-            int base = 0;
-            if (lane == leader) base = atomicAdd(&sm.cursor[e], __popc(peers));
-            base = __shfl_sync(0xffffffffu, base, leader);
-            if (peers & (1u << lane)) sm.pairs[base + __popc(peers & ((1u << lane) - 1u))] = (uint16_t)((k << 8) | tid);
-        });
-    __syncthreads();
-
-    // 3. one warp per entry
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
-    const int lane_of_x = 3 * (32 / NV) - 0, lane_of_y = 4 * (32 / NV);  // lanes holding S_x and S_y after the reduce-scatter
-    for (int e = warp; e < len; e += kThreads / 32) {
-        const int b = sm.start[e], n = sm.start[e + 1] - b;
-        if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
-        const float4 q = sm.geo[e];
-        float acc[NV];
-#pragma unroll
-        for (int v = 0; v < NV; ++v) acc[v] = 0.f;
-        for (int i = lane; i < n; i += 32) {
-            const unsigned rec = sm.pairs[b + i];
-            const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
-            const float2 vw = sm.vw[slot][pix];
-            const float2 xy = sm.pxy[pix];
-            const float dx = q.x - xy.x, dy = q.y - xy.y;
-            const float tx = vw.x * dx, ty = vw.x * dy;
-            acc[0] = fmaf(tx, dx, acc[0]);
-            acc[1] = fmaf(tx, dy, acc[1]);
-            acc[2] = fmaf(ty, dy, acc[2]);
-            acc[3] += tx;
-            acc[4] += ty;
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) acc[5 + c] = fmaf(vw.y, sm.vout[c][pix], acc[5 + c]);
+    const int lane_of_x = 3 * (32 / NV), lane_of_y = 4 * (32 / NV);  // lanes holding S_x and S_y after the reduce-scatter
+    for (int chunk = 0; chunk < len; chunk += kPairStage) {
+        const int n_entries = min(kPairStage, len - chunk);
+        if (chunk > 0) {
+            __syncthreads();  // the previous chunk's pairs and parameters are consumed
+            stage(chunk);
+            __syncthreads();
         }
-        const float total = warp_sum_scatter<NV>(acc, lane);
-        const float sx = __shfl_sync(0xffffffffu, total, lane_of_x), sy = __shfl_sync(0xffffffffu, total, lane_of_y);
-        if (holds_total) {
-            const int g = __ldg(&ids_sorted[range.x + e]);
-            float value, *target;
-            if (value_index < 3) {
-                value = value_index == 1 ? total : 0.5f * total;
-                target = v_conic + 3 * (size_t)g + value_index;
-            } else if (value_index == 3) {
-                value = q.z * sx + q.w * sy;
-                target = v_xy + 2 * (size_t)g;
-            } else if (value_index == 4) {
-                value = q.w * sx + sm.cc[e] * sy;
-                target = v_xy + 2 * (size_t)g + 1;
-            } else {
-                value = total;
-                target = v_colors + (size_t)g * channels + (value_index - 5);
+        // 2. counting sort of this chunk's pairs by entry (shared-memory atomics; lanes adding to the same counter are merged by the
+        //    hardware)
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int e = key[k] - chunk;
+            if (key[k] >= 0 && e >= 0 && e < n_entries) atomicAdd(&sm.start[e], 1);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            constexpr int kPer = kPairStage / 32;  // exclusive scan of the counts by one warp
+            int local[kPer], run = 0;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int e = lane * kPer + j;
+                local[j] = e < n_entries ? sm.start[e] : 0;
+                run += local[j];
             }
-            if (value != 0.f) atomicAdd(target, value);
+            int incl = run;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            int start = incl - run;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int e = lane * kPer + j;
+                if (e < n_entries) sm.start[e] = sm.cursor[e] = start;
+                start += local[j];
+            }
+            if (lane == 31) sm.start[n_entries] = incl;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int e = key[k] - chunk;
+            if (key[k] >= 0 && e >= 0 && e < n_entries) sm.pairs[atomicAdd(&sm.cursor[e], 1)] = (uint16_t)((k << 8) | tid);
+        }
+        __syncthreads();
+
+        // 3. one warp per entry
+        for (int e = warp; e < n_entries; e += kThreads / 32) {
+            const int b = sm.start[e], n = sm.start[e + 1] - b;
+            if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
+            const float4 q = sm.geo[e];
+            float acc[NV];
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+            for (int i = lane; i < n; i += 32) {
+                const unsigned rec = sm.pairs[b + i];
+                const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
+                const float2 vw = sm.vw[slot][pix];
+                const float2 xy = sm.pxy[pix];
+                const float dx = q.x - xy.x, dy = q.y - xy.y;
+                const float tx = vw.x * dx, ty = vw.x * dy;
+                acc[0] = fmaf(tx, dx, acc[0]);
+                acc[1] = fmaf(tx, dy, acc[1]);
+                acc[2] = fmaf(ty, dy, acc[2]);
+                acc[3] += tx;
+                acc[4] += ty;
+#pragma unroll
+                for (int c = 0; c < kMaxC; ++c)
+                    if (c < channels) acc[5 + c] = fmaf(vw.y, sm.vout[c][pix], acc[5 + c]);
+            }
+            const float total = warp_sum_scatter<NV>(acc, lane);
+            const float sx = __shfl_sync(0xffffffffu, total, lane_of_x), sy = __shfl_sync(0xffffffffu, total, lane_of_y);
+            if (holds_total) {
+                const int g = __ldg(&ids_sorted[range.x + chunk + e]);
+                float value, *target;
+                if (value_index < 3) {
+                    value = value_index == 1 ? total : 0.5f * total;
+                    target = v_conic + 3 * (size_t)g + value_index;
+                } else if (value_index == 3) {
+                    value = q.z * sx + q.w * sy;
+                    target = v_xy + 2 * (size_t)g;
+                } else if (value_index == 4) {
+                    value = q.w * sx + sm.cc[e] * sy;
+                    target = v_xy + 2 * (size_t)g + 1;
+                } else {
+                    value = total;
+                    target = v_colors + (size_t)g * channels + (value_index - 5);
+                }
+                if (value != 0.f) atomicAdd(target, value);
+            }
         }
     }
 }
@@ -721,6 +733,7 @@ int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t
             err = launch_bwd_pairs<0, 32>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     }
+    if (tile_topk != nullptr) return IGS_OK;  // the pairs kernel handled every tile
     if (channels == 3)
         err = launch_bwd<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
     else if (channels <= 3)

@@ -22,7 +22,7 @@ SIGNATURES = {
     "igs_project_fwd": (c_int, [c_int, P, P, P, c_int, c_int, c_int, c_int, P, P, P, P, P]),
     "igs_project_bwd": (c_int, [c_int, P, P, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     "igs_cumsum_workspace": (c_size_t, [c_int]),
-    "igs_cumsum": (c_int, [c_int, P, P, P, P]),
+    "igs_cumsum": (c_int, [c_int, P, P, P, P, c_size_t, P]),
     "igs_sort_workspace": (c_size_t, [c_int, c_int, c_int]),
     "igs_sort_intersects": (c_int, [c_int, c_int, P, P, P, c_int, c_int, P, P, P, c_size_t, P]),
     "igs_raster_fwd_topk": (c_int, [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),

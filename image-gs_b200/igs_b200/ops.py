@@ -84,8 +84,10 @@ def cumulative_intersects(num_tiles_hit: torch.Tensor):
     dev = num_tiles_hit.device
     cum = torch.empty(n, device=dev, dtype=torch.int32)
     total = torch.empty(1, device=dev, dtype=torch.int32)
+    ws_bytes = _lib.load().igs_cumsum_workspace(n)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
-        _lib_call("igs_cumsum", int(n), ptr(num_tiles_hit), ptr(cum), ptr(total), stream_of(dev))
+        _lib_call("igs_cumsum", int(n), ptr(num_tiles_hit), ptr(cum), ptr(total), ptr(ws), ws_bytes, stream_of(dev))
     return cum, total
 
 

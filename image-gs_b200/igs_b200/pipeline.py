@@ -42,6 +42,8 @@ class RasterStep:
         self.hits = torch.empty(n, device=dev, dtype=i32)
         self.cum = torch.empty(n, device=dev, dtype=i32)
         self.num_intersects = torch.empty(1, device=dev, dtype=i32)
+        self.cum_ws_bytes = self.lib.igs_cumsum_workspace(n)
+        self.cum_ws = torch.empty(self.cum_ws_bytes, device=dev, dtype=torch.uint8)
         self.image = torch.empty(nc, self.h, self.w, device=dev, dtype=f32)
         self.v_image = torch.empty_like(self.image)
         self.loss = torch.empty((), device=dev, dtype=f32)
@@ -85,7 +87,8 @@ class RasterStep:
                     "project")
 
     def _cumsum(self):
-        self._check(self.lib.igs_cumsum(self.n, ptr(self.hits), ptr(self.cum), ptr(self.num_intersects), self._stream()), "cumsum")
+        self._check(self.lib.igs_cumsum(self.n, ptr(self.hits), ptr(self.cum), ptr(self.num_intersects), ptr(self.cum_ws), self.cum_ws_bytes,
+                                        self._stream()), "cumsum")
 
     def _bin(self):
         self._check(self.lib.igs_sort_intersects(self.n, self.capacity, ptr(self.xys), ptr(self.radii), ptr(self.cum), self.tb[0], self.tb[1],
@@ -124,7 +127,7 @@ class RasterStep:
 
     STAGES = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward", "_project_backward")
     # kernels each stage launches (memsets excluded)
-    KERNELS = {"_project": 1, "_cumsum": 1, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1}
+    KERNELS = {"_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1}
 
     def launch(self):
         for s in self.STAGES:

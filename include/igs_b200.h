@@ -54,9 +54,10 @@ int igs_project_bwd(int num_points, const float *scales2d, const float *rotation
 /* ---- tile binning --------------------------------------------------------------------------------------------------------------- */
 
 /* compute_cumulative_intersects (gsplat/gsplat/utils.py:96-115): inclusive int32 prefix sum; `total` (device int32, may be NULL) gets
- * the last element without a host read-back. */
+ * the last element without a host read-back. Workspace: igs_cumsum_workspace(n) bytes (per-block partial sums). */
 size_t igs_cumsum_workspace(int n);
-int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *stream);
+int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int32_t *total, void *workspace, size_t workspace_bytes,
+               void *stream);
 
 /* sort_intersects_by_tile (gsplat/gsplat/utils.py:165-186 -> bindings.cu:106-167): Gaussian IDs of the tile intersections sorted by tile,
  * increasing Gaussian ID within a tile, in `capacity` slots (intersections beyond the capacity dropped, unused slots 0), and

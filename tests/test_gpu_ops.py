@@ -1,0 +1,204 @@
+"""
+GPU parity of the training-step operators around the rasterizer: the fused straight-through quantizer (symbols bit-exact against the
+reference's quantization code, run here by ATen on the GPU and by the reference itself on the CPU for the fixtures), the rate term
+(against the reference's rate_bits and its own CUDA kernels), the fused L1 loss, the leave-one-out kernel, the autograd / drop-in gsplat
+path end to end, and the graph-captured pipeline.
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from common import assert_close_grad, assert_close_render, make_case, np_, ours_stages, to_dev
+from igs_b200 import autograd as ag
+from igs_b200 import ops, pipeline, workloads
+from oracle import cpu as orc
+from oracle import quant as oquant
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+PY_CASES = ["cfg2_480p_yuv", "rgb_subgreen_320x200"]
+
+
+def py_fixture(name):
+    return dict(np.load(os.path.join(GOLDEN, f"py_{name}.npz")))
+
+
+def py_inputs(name):
+    wl = workloads.get_workload(name) if name in workloads.CONFIGS else workloads.custom_workload(200, 320, 800, 3, math.log(2.5), 0.5, 6.0,
+                                                                                                    seed=31)
+    return wl, workloads.make_inputs(wl)
+
+
+@pytest.mark.parametrize("numel_shape", [(3, 37, 53), (3, 64, 64), (9, 16, 1)])
+def test_l1_loss_matches_torch(numel_shape, device):
+    g = torch.Generator().manual_seed(3)
+    img = torch.rand(numel_shape, generator=g).to(device)
+    tgt = torch.rand(numel_shape, generator=g).to(device)
+    tgt.view(-1)[::7] = img.view(-1)[::7]  # exact ties: zero gradient
+    loss, grad = ops.l1_loss_and_grad(img, tgt, ratio=0.75)
+    x = img.clone().requires_grad_(True)
+    ref = 0.75 * F.l1_loss(x, tgt)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) <= 1e-6 * abs(float(ref))
+    torch.testing.assert_close(grad, x.grad, rtol=0, atol=0)
+    loss2, _ = ops.l1_loss_and_grad(img, tgt, ratio=0.75)  # the workspace ticket resets: repeatable, deterministic
+    assert float(loss2) == float(loss)
+
+
+@pytest.mark.parametrize("name", PY_CASES)
+def test_quantize_ste_symbols_bit_exact(name, device):
+    z = py_fixture(name)
+    wl, inp = py_inputs(name)
+    d = to_dev(inp, device)
+    pos_steps = torch.from_numpy(z["steps_xy"]).to(device)
+    feat_steps = torch.from_numpy(z["feat_steps"]).to(device)
+    scale = d["scales"].abs()
+    (oxy, osc, orot, ofeat), _, sym = ops.quantize_ste_forward(d["means"], scale, d["rotations"], d["features"], pos_steps,
+                                                               float(z["scale_step"]), float(z["rot_step"]), feat_steps, with_symbols=True)
+    # ATen on the GPU running the reference's quantization arithmetic: bit-exact
+    values, ref_sym = oquant.quantize_ste(d["means"], scale, d["rotations"], d["features"], pos_steps, float(z["scale_step"]),
+                                          float(z["rot_step"]), feat_steps)
+    for a, b in zip(sym, ref_sym):
+        assert torch.equal(a, b)
+    for a, b in zip((oxy, osc, orot, ofeat), values):
+        assert torch.equal(a, b)
+    # the reference's own code on the CPU (the fixture): equal except where log2 of a scale lands within rounding of a half step
+    for a, key in zip(sym, ("q_xy", "q_scale", "q_rot", "q_feat")):
+        diff = np_(a) != z[key]
+        assert diff.sum() <= 2, f"{key}: {int(diff.sum())} symbols differ from the CPU reference"
+
+
+def test_quantize_ste_autograd_passes_gradients(device):
+    wl, inp = make_case(32, 32, 50, seed=41)
+    d = to_dev(inp, device)
+    xs = [t.clone().requires_grad_(True) for t in (d["means"], d["scales"], d["rotations"], d["features"])]
+    out = ag.quantize_ste(*xs, torch.tensor([0.004, 0.004], device=device), 0.03125, 0.0123, torch.full((3,), 1 / 64, device=device))
+    sum(o.sum() * (i + 1) for i, o in enumerate(out)).backward()
+    for i, x in enumerate(xs):
+        assert torch.equal(x.grad, torch.full_like(x, float(i + 1)))
+
+
+class _Model:
+    """The fields of compress.rate.RateModel that the rate operators read."""
+
+    def __init__(self, z, device):
+        t = lambda k, dt=torch.float32: torch.from_numpy(z[k]).to(device=device, dtype=dt).contiguous()  # noqa: E731
+        self.neighbors = t("neighbors", torch.int32)
+        self.weights, self.slope, self.inv_steps, self.feat_coeffs, self.inv_rot = (t("weights"), t("slope"), t("inv_steps"),
+                                                                                    t("feat_coeffs"), t("inv_rot"))
+        self.offsets, self.sources, self.source_weights = t("offsets", torch.int32), t("sources", torch.int32), t("source_weights")
+        self.color_refs = tuple(int(v) for v in z["color_refs"])
+        self.pred_channels = tuple(int(v) for v in z["pred_channels"])
+
+
+@pytest.mark.parametrize("name", PY_CASES)
+def test_rate_loss_matches_reference_python(name, device):
+    z = py_fixture(name)
+    model = _Model(z, device)
+    feat = torch.from_numpy(z["out_feat"]).to(device).requires_grad_(True)
+    rot = torch.from_numpy(z["out_rot"]).to(device).requires_grad_(True)
+    l1 = torch.tensor(float(z["l1"]), device=device)
+    loss = ag.rate_loss(feat, rot, l1, model, float(z["inv_rot_step"]), float(z["l1_ratio"]), float(z["factor"]))
+    loss.backward()
+    assert abs(float(loss) - float(z["loss"])) <= 1e-5 * abs(float(z["loss"]))
+    assert_close_grad(feat.grad, z["grad_feat"], what="grad_feat")
+    assert_close_grad(rot.grad, z["grad_rot"], what="grad_rot")
+
+
+@pytest.mark.parametrize("name", PY_CASES)
+def test_rate_loss_matches_reference_kernels(name, device, ref_module):
+    z = py_fixture(name)
+    m = _Model(z, device)
+    feat = torch.from_numpy(z["out_feat"]).to(device)
+    rot = torch.from_numpy(z["out_rot"]).to(device)
+    l1 = torch.tensor(float(z["l1"]), device=device)
+    args = (feat, rot, l1, m.neighbors, m.weights, m.slope, list(m.color_refs), list(m.pred_channels), m.inv_steps, m.feat_coeffs,
+            m.inv_rot, float(z["inv_rot_step"]), float(z["l1_ratio"]), float(z["factor"]))
+    ours = ops.rate_loss_forward(*args)
+    ref = ref_module.rate_loss_forward(*args)
+    assert abs(float(ours[0]) - float(ref[0])) <= 1e-5 * abs(float(ref[0]))
+    assert float(ours[1]) == float(ref[1])
+    for a, b, what in zip(ours[2:], ref[2:], ("own_grad", "rot_grad")):
+        assert_close_grad(a, b, what=what)
+    g = torch.tensor(1.5, device=device)
+    bo = ops.rate_loss_backward(g, ours[1], ours[2], ours[3], m.offsets, m.sources, m.source_weights)
+    br = ref_module.rate_loss_backward(g, ref[1], ref[2], ref[3], m.offsets, m.sources, m.source_weights)
+    for a, b, what in zip(bo, br, ("grad_feat", "grad_rot")):
+        assert_close_grad(a, b, what=what)
+
+
+@pytest.mark.parametrize("case", [dict(h=88, w=120, n=300, seed=11), dict(h=64, w=80, n=200, c=9, seed=13)])
+def test_loo_matches_oracle(case, device):
+    case = dict(case)
+    h, w = case.pop("h"), case.pop("w")
+    wl, inp = make_case(h, w, **case)
+    d = to_dev(inp, device)
+    ours = ours_stages(d, h, w)
+    for squared in (False, True):
+        got = ops.topk_norm_loo_loss_increase(h, w, ours["xys"], ours["conics"], d["features"], ours["pixel_topk"], d["target"], squared, 1e-4)
+        want = orc.loo_loss_increase(h, w, np_(ours["xys"]), np_(ours["conics"]), inp["features"].numpy(), np_(ours["pixel_topk"]),
+                                     inp["target"].numpy(), squared, 1e-4)
+        assert_close_grad(got, want, rtol=1e-3, floor=1e-2, what=f"loo squared={squared}")
+
+
+def test_loo_matches_reference(device, ref_module):
+    wl, inp = make_case(88, 120, 300, seed=11)
+    d = to_dev(inp, device)
+    ours = ours_stages(d, 88, 120)
+    for squared in (False, True):
+        got = ops.topk_norm_loo_loss_increase(88, 120, ours["xys"], ours["conics"], d["features"], ours["pixel_topk"], d["target"], squared,
+                                              1e-4)
+        want = ref_module.topk_norm_loo_loss_increase(88, 120, ours["xys"], ours["conics"], d["features"], ours["pixel_topk"], d["target"],
+                                                      squared, 1e-4)
+        assert_close_grad(got, want, rtol=1e-3, floor=1e-2, what=f"loo squared={squared}")
+
+
+@pytest.mark.parametrize("capacity", [None, "x2"])
+def test_gsplat_shim_end_to_end(capacity, device):
+    """model.forward's calls through the drop-in gsplat package, then F.l1_loss and backward: gradients of means, scales, rotations and
+    features against the oracle's full step."""
+    import gsplat
+
+    wl, inp = make_case(96, 136, 500, seed=51)
+    h, w = wl.height, wl.width
+    d = to_dev(inp, device)
+    params = [d[k].clone().requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+    tb = ops.tile_grid(h, w)
+    xys, radii, conics, hits = gsplat.project_gaussians_2d_scale_rot(*params[:3], h, w, tb)
+    cap = None if capacity is None else 2 * int(hits.sum())
+    img = gsplat.rasterize_gaussians_sum(xys, radii, conics, hits, params[3], h, w, 16, 16, topk_norm=True, capacity=cap)
+    assert img.shape == (h, w, 3)
+    img_chw = img.view(-1, h, w, 3).permute(0, 3, 1, 2).contiguous().squeeze(0)  # model.py:975
+    loss = F.l1_loss(img_chw, d["target"])
+    loss.backward()
+    r = orc.train_step(*[inp[k].numpy() for k in ("means", "scales", "rotations", "features", "target")], h, w)
+    assert_close_render(img_chw, r["image"], rtol=3e-5, what="image")
+    assert abs(float(loss) - r["loss"]) <= 1e-5 * r["loss"]
+    # end to end the L1 sign can flip where the renders straddle the target within rounding; few pixels, small effect
+    for p, key in zip(params, ("v_mean2d", "v_scale", "v_rot", "v_colors")):
+        assert_close_grad(p.grad, r[key].reshape(p.shape), rtol=2e-3, what=key)
+
+
+def test_pipeline_graph_matches_autograd(device):
+    """The preallocated, graph-captured step computes what the autograd operators compute."""
+    wl, inp = make_case(120, 200, 800, seed=61)
+    d = to_dev(inp, device)
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"])
+    step.replay()
+    step.replay()
+    torch.cuda.synchronize()
+    params = [d[k].clone().requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+    h, w = wl.height, wl.width
+    xys, radii, conics, hits = ag.project_gaussians_2d_scale_rot(*params[:3], h, w, ops.tile_grid(h, w))
+    img = ag.rasterize_gaussians_sum_topk(xys, radii, conics, hits, params[3], h, w, capacity=step.capacity)
+    loss = ag.l1_loss(img.permute(2, 0, 1), d["target"])
+    loss.backward()
+    assert torch.equal(step.image, img.permute(2, 0, 1).detach())
+    assert float(step.loss) == float(loss)
+    for p, mine in zip(params, (step.v_mean2d, step.v_scale, step.v_rot, step.v_colors)):
+        assert_close_grad(mine, p.grad.reshape(mine.shape), what="pipeline grad")
+    assert int(step.num_intersects.item()) <= step.capacity
