@@ -363,3 +363,60 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
 }
 
 }  // extern "C"
+
+// ---- tile binning without device allocation -------------------------------------------------------------------------------------------
+//
+// For callers that cannot call cudaMalloc and have no workspace to lend: a plugin inside a host application that owns all device memory,
+// or code running where an allocation would synchronize the device and stall its other streams. The scratch lives in a fixed array of
+// this library instead, sized for IGS_NOALLOC_MAX_CAPACITY intersections over IGS_NOALLOC_MAX_TILES tiles (about 16 MiB). Every device that
+// loads the library holds one copy until the process exits. All calls on a device share it: calls that overlap on the GPU (on different
+// streams) race; what must start at zero (the per-tile counters) is cleared by every call.
+
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes =
+    ((sizeof(int) * (size_t)IGS_NOALLOC_MAX_TILES + 255) & ~(size_t)255) + 256 + ((sizeof(int2) * (size_t)IGS_NOALLOC_MAX_CAPACITY + 255) & ~(size_t)255) +
+    2 * ((sizeof(int) * (size_t)IGS_NOALLOC_MAX_CAPACITY + 255) & ~(size_t)255);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void *g_noalloc_address[kMaxDevices] = {};
+
+// The scratch array's device address on the current device. In host code g_noalloc_scratch names a host-side stand-in, so the address is
+// looked up once per device, with that device current.
+int noalloc_scratch(void **address) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return igs::check_launch("igs_sort_intersects_noalloc: cudaGetDevice");
+    if (device < 0 || device >= kMaxDevices) return igs::set_error(IGS_ERR_UNSUPPORTED, "igs_sort_intersects_noalloc: device %d", device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_address[device] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess)
+            return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
+        g_noalloc_address[device] = p;
+    }
+    *address = g_noalloc_address[device];
+    return IGS_OK;
+}
+
+}  // namespace
+
+extern "C" int igs_sort_intersects_noalloc(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit,
+                                           int tiles_x, int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *stream) {
+    IGS_REQUIRE(capacity <= IGS_NOALLOC_MAX_CAPACITY,
+                "igs_sort_intersects_noalloc: capacity %d exceeds the library's fixed scratch (at most %d intersections; use "
+                "igs_sort_intersects with a workspace)", capacity, IGS_NOALLOC_MAX_CAPACITY);
+    IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && (int64_t)tiles_x * tiles_y <= IGS_NOALLOC_MAX_TILES,
+                "igs_sort_intersects_noalloc: %d x %d tiles exceed the library's fixed scratch (at most %d tiles; use igs_sort_intersects "
+                "with a workspace)", tiles_x, tiles_y, IGS_NOALLOC_MAX_TILES);
+    void *scratch = nullptr;
+    const int status = noalloc_scratch(&scratch);
+    if (status != IGS_OK) return status;
+    return igs_sort_intersects(num_points, capacity, xys, radii, cum_tiles_hit, tiles_x, tiles_y, gaussian_ids_sorted, tile_bins, scratch,
+                               kNoAllocScratchBytes, stream);
+}

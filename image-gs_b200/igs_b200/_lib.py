@@ -25,6 +25,7 @@ SIGNATURES = {
     "igs_cumsum": (c_int, [c_int, P, P, P, P, c_size_t, P]),
     "igs_sort_workspace": (c_size_t, [c_int, c_int, c_int]),
     "igs_sort_intersects": (c_int, [c_int, c_int, P, P, P, c_int, c_int, P, P, P, c_size_t, P]),
+    "igs_sort_intersects_noalloc": (c_int, [c_int, c_int, P, P, P, c_int, c_int, P, P, P]),
     "igs_raster_fwd_topk": (c_int, [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),
     "igs_raster_fwd_topk_tiles": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),
     "igs_raster_bwd_topk": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P]),

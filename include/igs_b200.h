@@ -67,6 +67,17 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
                         int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace, size_t workspace_bytes,
                         void *stream);
 
+/* The binning of igs_sort_intersects for callers that cannot allocate device memory and have no workspace to lend (a plugin in a host
+ * application that owns all device memory, or code where an allocation would synchronize the device). No counterpart in the
+ * reference. Its scratch is a fixed array inside the library, about 16 MiB on every device that loads it, held until the process exits;
+ * capacity above IGS_NOALLOC_MAX_CAPACITY or more than IGS_NOALLOC_MAX_TILES tiles is rejected with IGS_ERR_INVALID. The first call on
+ * each device looks up the array's device address (with that device current); make that first call before any stream capture. All
+ * calls on a device share the array, so calls that overlap on the GPU race; each call clears what must start at zero. */
+#define IGS_NOALLOC_MAX_CAPACITY 1048576
+#define IGS_NOALLOC_MAX_TILES 65536
+int igs_sort_intersects_noalloc(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit,
+                                int tiles_x, int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *stream);
+
 /* ---- top-K normalized rasterization ---------------------------------------------------------------------------------------------- */
 
 /* nd_rasterize_forward_topk_norm (bindings.cu:380-437, kernel forward.cu:223-375): out_img [C,H,W] (channel-planar) and
