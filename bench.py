@@ -181,15 +181,30 @@ def time_graph(graph, reps, flush):
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / reps
 
 
+RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
+
+
+def step_options(wl, device):
+    """Extra stages of the workload's step: for the 480p YUV configuration the straight-through quantizer, the luma-weighted loss
+    transform and the rate term, whose fixed inputs (neighbours, slopes, Laplace scales) are the ones the reference's
+    compress.rate.rate_model computed for this seeded workload (tests/golden/py_cfg2_480p_yuv.npz)."""
+    if not wl.rate_term:
+        return {}
+    z = np.load(RATE_MODEL)
+    return dict(quant=workloads.quant_settings(wl, device), loss_transform=workloads.loss_transform_yuv().to(device),
+                rate=dict(model=workloads.RateModelTensors(z, device), inv_rot_step=float(z["inv_rot_step"]), factor=float(z["factor"])))
+
+
 def run_ours(args, wl):
     from igs_b200 import pipeline
 
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    inp = workloads.make_inputs(wl, image_index=rank)
+    inp = workloads.make_inputs(wl, image_index=rank if not wl.rate_term else 0)
     d = {k: v.to(device) for k, v in inp.items()}
-    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"])
+    target = d["loss_target"] if "loss_target" in d else d["target"]
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], target, **step_options(wl, device))
     graph = step.capture()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(args.warmup):
@@ -223,7 +238,7 @@ def run_ours(args, wl):
 
     # per-stage breakdown and the dominant kernel's roofline (graphs of single stages, same flush discipline)
     stage_ms = {}
-    for s in pipeline.RasterStep.STAGES if not args.no_stages else ():
+    for s in step.STAGES if not args.no_stages else ():
         g = step.capture([s])
         stage_ms[s.strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g
@@ -273,25 +288,190 @@ def run_ours(args, wl):
         torch.distributed.destroy_process_group()
 
 
+def run_bands(args, wl):
+    """One image in tile-row bands, one band per GPU (strong scaling): every rank projects all Gaussians, bins, renders and
+    back-propagates its rows; the partial gradients and loss are summed with one NCCL all-reduce; every rank finishes the projection
+    backward. value = whole-image steps/s; per-step time is the max over ranks."""
+    from igs_b200 import bands
+
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    inp = workloads.make_inputs(wl)  # the same image on every rank
+    d = {k: v.to(device) for k, v in inp.items()}
+    tiles_x, tiles_y, _ = wl.tile_bounds
+    per_row = bands.row_intersections(d["means"], d["scales"], d["rotations"], wl.height, wl.width)
+    r0, r1 = bands.band_rows(tiles_y, world, rank, [r + 32.0 * tiles_x for r in per_row])
+    group = torch.distributed.group.WORLD if world > 1 else None
+    step = bands.BandStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], wl.height, wl.width, r0, r1, group=group)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(args.warmup):
+        step.replay()
+    torch.cuda.synchronize()
+    band_isect = int(step.num_intersects.item())
+    if band_isect > step.capacity:
+        raise SystemExit(f"intersections {band_isect} exceed the capacity {step.capacity}")
+    evals = torch.tensor([step.gaussian_pixel_evals()], device=device, dtype=torch.float64)
+
+    barrier = (lambda: torch.distributed.barrier()) if world > 1 else (lambda: None)
+    # the ranks' steps are coupled by the all-reduce, so each L2 flush is followed by a one-float all-reduce that lines up the ranks'
+    # start events: otherwise a rank's timed step would include waiting for the other ranks' flushes
+    token = torch.zeros(1, device=device)
+    align = (lambda: torch.distributed.all_reduce(token)) if world > 1 else (lambda: None)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            align()
+            starts[i].record()
+            step.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(starts, ends))], device=device, dtype=torch.float64)
+
+    # the band's own work (one graph, no communication) and the all-reduce alone, per rank
+    local_ms = time_graph(step.local_graph, max(5, min(50, args.steps)), flush)
+    stage_ms = {}
+    for s_ in (("_forward",), ("_backward",)) if not args.no_stages else ():
+        g = step._capture(s_)
+        stage_ms[s_[0].strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
+        del g
+    ar_ms = 0.0
+    if world > 1:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record()
+        for _ in range(20):
+            step.all_reduce()
+        b.record()
+        torch.cuda.synchronize()
+        ar_ms = a.elapsed_time(b) / 20
+    per_rank = torch.tensor([local_ms, float(r1 - r0), float(band_isect)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(evals)
+        gathered = [torch.empty_like(per_rank) for _ in range(world)]
+        torch.distributed.all_gather(gathered, per_rank)
+    else:
+        gathered = [per_rank]
+    total_ms = float(total_ms.item())
+    ms_per_step = total_ms / args.steps
+    value = args.steps / (total_ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_band_e2e(args, step, inp, device, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, threads, steps = cpu_step_rate(wl, inp)
+        cpu = {"value": rate, "unit": "steps/s", "cores": threads, "kind": "port",
+               "sample": f"{steps} whole {wl.width}x{wl.height} steps of the C restatement on {threads} threads ({cpu_model()})"}
+
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        c, n, k = wl.channels, wl.num_gaussians, 10
+        p = step.band_h * wl.width
+        roofline = None
+        if stage_ms:
+            fwd_bytes = p * (4 * c + 4 * k) + band_isect * 4 + n * 4 * (5 + c)
+            bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
+            dominant = max(("forward", "backward"), key=lambda s_: stage_ms[s_])
+            dom_bytes = fwd_bytes if dominant == "forward" else bwd_bytes
+            achieved = dom_bytes / (stage_ms[dominant] * 1e-3) / 1e9
+            roofline = {"bound": "hbm", "kernel": f"raster_{dominant} (rank 0's band)", "achieved": achieved, "peak": hbm_peak,
+                        "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                        "algorithmic_bytes": dom_bytes, "kernel_ms": stage_ms[dominant]}
+        total_evals = float(evals.item())
+        out = {
+            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded sinusoid target, random Gaussians; one image split into tile-row bands)",
+            "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
+                       "tile": 16, "top_k": 10, "parallelism": f"{world} tile-row bands + NCCL all-reduce of {step.reduced.numel()} floats",
+                       "bands": [[int(g[1].item()), int(g[2].item())] for g in gathered],
+                       "l2": "flushed between timed steps (256 MB write outside the event intervals)",
+                       "graph": "band work as one CUDA graph, NCCL all-reduce, projection backward as a second graph"},
+            "gaussian_pixel_evals_per_step": total_evals, "gaussian_pixel_evals_per_s": total_evals * value,
+            "band_ms_per_rank": [float(g[0].item()) for g in gathered], "all_reduce_ms": ar_ms, "stages_ms": stage_ms,
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(out))
+    step.release()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_band_e2e(args, step, inp, device, world):
+    """The band step through the C ABI with host buffers: the Gaussian parameters copied host -> device from pinned memory and the loss
+    read back every step."""
+    host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
+    dev = {"means": step.means, "scales": step.scales, "rotations": step.rotations, "features": step.features}
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def one():
+        for k in dev:
+            dev[k].copy_(host[k], non_blocking=True)
+        step.replay()
+        loss_host.copy_(step.loss, non_blocking=True)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        one()
+        torch.cuda.current_stream().synchronize()
+        float(loss_host)
+    end.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    return {"value": args.steps / (float(t.item()) / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
+            "d2h_bytes_per_step": 4 * world, "api": "igs_b200.bands.BandStep over the C ABI (host parameters copied in every step)"}
+
+
 def run_e2e(args, wl, inp, device, capacity, world):
     import torch.nn.functional as F
 
     import gsplat
 
+    from igs_b200 import autograd as ag
+
     host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
-    target = inp["target"].to(device)
+    target = (inp["loss_target"] if "loss_target" in inp else inp["target"]).to(device)
     dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
     tb = wl.tile_bounds
+    opts = step_options(wl, device)
 
     def one():
         for k in dev:
             dev[k].copy_(host[k], non_blocking=True)
         means, scales, rots, feats = [dev[k].requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+        raw_feats, raw_rots = feats, rots
+        if "quant" in opts:  # model._get_params (model.py:993-1006) and the loss-space features (model.py:963-964)
+            q = opts["quant"]
+            means, scales, rots, feats = ag.quantize_ste(means, scales, rots, feats, q["pos_steps"], q["scale_step"], q["rot_step"],
+                                                         q["feat_steps"])
+            feats = feats @ opts["loss_transform"].T
         xys, radii, conics, hits = gsplat.project_gaussians_2d_scale_rot(means, scales, rots, wl.height, wl.width, tb)
         img = gsplat.rasterize_gaussians_sum(xys, radii, conics, hits, feats, wl.height, wl.width, topk_norm=True, capacity=capacity)
         img = img.permute(2, 0, 1).contiguous()
         loss = F.l1_loss(img, target)
+        if "rate" in opts:  # model._get_total_loss (model.py:1235-1240)
+            r = opts["rate"]
+            loss = loss + ag.rate_loss(raw_feats, raw_rots, loss, r["model"], r["inv_rot_step"], 1.0, r["factor"])
         loss.backward()
         loss_host.copy_(loss.detach(), non_blocking=True)
         for k in dev:
@@ -317,7 +497,9 @@ def run_e2e(args, wl, inp, device, capacity, world):
     value = world * args.steps / (float(t.item()) / 1e3)
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     return {"value": value, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-            "api": "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + F.l1_loss + backward"}
+            "api": ("igs_b200.autograd.quantize_ste + feat @ T.T + " if "quant" in opts else "") +
+                   "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + F.l1_loss" +
+                   (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward"}
 
 
 def main():
@@ -334,6 +516,8 @@ def main():
     wl = workloads.get_workload(args.workload)
     if args.impl == "reference":
         run_reference(args, wl)
+    elif wl.sharding == "bands":
+        run_bands(args, wl)
     else:
         run_ours(args, wl)
 

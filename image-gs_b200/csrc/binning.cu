@@ -189,27 +189,51 @@ __device__ __forceinline__ int owner_of(const int *__restrict__ cum, int n, int 
 }
 
 // One thread per intersection slot below min(total, capacity): its Gaussian, its tile, and a rank within the tile from the returning
-// atomic on the tile's counter (arbitrary order; the order pass restores increasing Gaussian ID)
+// atomic on the tile's counter (arbitrary order; the order pass restores increasing Gaussian ID). Only the tile rows [row_begin, row_end)
+// are binned (a band of the image; the whole grid otherwise): each Gaussian's rectangle is clipped to them, tiles are numbered within the
+// band, and the prefix sum must count the clipped rectangles (igs_band_tiles_hit).
 __global__ void __launch_bounds__(256) count_kernel(const int n, const int capacity, const float2 *__restrict__ xys,
                                                     const int *__restrict__ radii, const int *__restrict__ cum, const unsigned tiles_x,
-                                                    const unsigned tiles_y, int *__restrict__ tile_count, int2 *__restrict__ slot_tile_rank,
+                                                    const unsigned tiles_y, const unsigned row_begin, const unsigned row_end,
+                                                    int *__restrict__ tile_count, int2 *__restrict__ slot_tile_rank,
                                                     int *__restrict__ slot_gaussian) {
     const int slots = min(__ldg(&cum[n - 1]), capacity);
-    const unsigned num_tiles = tiles_x * tiles_y;
+    const unsigned num_tiles = tiles_x * (row_end - row_begin);
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < slots; idx += gridDim.x * blockDim.x) {
         const int g = owner_of(cum, n, idx);
         const int local = idx - (g > 0 ? __ldg(&cum[g - 1]) : 0);
         const float2 xy = __ldg(&xys[g]);
         unsigned x0, y0, x1, y1;
         tile_rect(xy.x, xy.y, (float)__ldg(&radii[g]), tiles_x, tiles_y, x0, y0, x1, y1);
+        y0 = max(y0, row_begin);
+        y1 = min(y1, row_end);
         const unsigned width = x1 - x0;
         unsigned tile = num_tiles;  // inconsistent inputs (an empty footprint with slots): dropped
-        if (width > 0) tile = slot_tile(local, x0, y0, width, tiles_x);
+        if (width > 0 && y1 > y0) tile = slot_tile(local, x0, y0 - row_begin, width, tiles_x);
         int rank = -1;
         if (tile < num_tiles) rank = atomicAdd(&tile_count[tile], 1);
         slot_tile_rank[idx] = make_int2((int)tile, rank);
         slot_gaussian[idx] = g;
     }
+}
+
+// Tiles of the rows [row_begin, row_end) that each Gaussian's rectangle covers (the band's num_tiles_hit)
+__global__ void __launch_bounds__(256) band_hits_kernel(const int n, const float2 *__restrict__ xys, const int *__restrict__ radii,
+                                                        const unsigned tiles_x, const unsigned tiles_y, const unsigned row_begin,
+                                                        const unsigned row_end, int *__restrict__ hits) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    int count = 0;
+    const int radius = __ldg(&radii[g]);
+    if (radius > 0) {
+        const float2 xy = __ldg(&xys[g]);
+        unsigned x0, y0, x1, y1;
+        tile_rect(xy.x, xy.y, (float)radius, tiles_x, tiles_y, x0, y0, x1, y1);
+        y0 = max(y0, row_begin);
+        y1 = min(y1, row_end);
+        if (y1 > y0) count = (int)((x1 - x0) * (y1 - y0));
+    }
+    hits[g] = count;
 }
 
 // Exclusive scan of the tile counts by one CTA: tile_bins[t] = (start, end), (0, 0) for empty tiles
@@ -313,25 +337,27 @@ int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int3
 
 size_t igs_sort_workspace(int capacity, int tiles_x, int tiles_y) { return sort_workspace_bytes(capacity, tiles_x * tiles_y); }
 
-int igs_sort_intersects(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
-                        int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace, size_t workspace_bytes,
-                        void *stream) {
-    IGS_REQUIRE(num_points >= 0 && tiles_x >= 0 && tiles_y >= 0, "igs_sort_intersects: negative size");
-    const int num_tiles = tiles_x * tiles_y;
+static int sort_band(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                     int tiles_y, int row_begin, int row_end, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace,
+                     size_t workspace_bytes, void *stream, const char *who) {
+    IGS_REQUIRE(num_points >= 0 && tiles_x >= 0 && tiles_y >= 0, "%s: negative size", who);
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
+                row_end, tiles_y);
+    const int num_tiles = tiles_x * (row_end - row_begin);
     cudaStream_t s = igs::as_stream(stream);
     if (num_tiles == 0) return IGS_OK;
-    IGS_REQUIRE(tile_bins != nullptr, "igs_sort_intersects: null tile_bins");
-    IGS_REQUIRE(igs::aligned(tile_bins, 8), "igs_sort_intersects: tile_bins must be 8-byte aligned [T, 2] int32");
+    IGS_REQUIRE(tile_bins != nullptr, "%s: null tile_bins", who);
+    IGS_REQUIRE(igs::aligned(tile_bins, 8), "%s: tile_bins must be 8-byte aligned [T, 2] int32", who);
     if (capacity <= 0) {
         // the reference returns no intersections and zero tile ranges (bindings.cu:124-126)
-        if (cudaMemsetAsync(tile_bins, 0, sizeof(int) * 2 * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch("igs_sort_intersects");
+        if (cudaMemsetAsync(tile_bins, 0, sizeof(int) * 2 * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch(who);
         return IGS_OK;
     }
-    IGS_REQUIRE(gaussian_ids_sorted && workspace, "igs_sort_intersects: null pointer");
-    IGS_REQUIRE(workspace_bytes >= sort_workspace_bytes(capacity, num_tiles), "igs_sort_intersects: workspace too small (%zu < %zu)",
-                workspace_bytes, sort_workspace_bytes(capacity, num_tiles));
-    IGS_REQUIRE(num_points == 0 || (xys && radii && cum_tiles_hit), "igs_sort_intersects: null pointer");
-    IGS_REQUIRE(num_points == 0 || igs::aligned(xys, 8), "igs_sort_intersects: xys must be 8-byte aligned");
+    IGS_REQUIRE(gaussian_ids_sorted && workspace, "%s: null pointer", who);
+    IGS_REQUIRE(workspace_bytes >= sort_workspace_bytes(capacity, num_tiles), "%s: workspace too small (%zu < %zu)", who, workspace_bytes,
+                sort_workspace_bytes(capacity, num_tiles));
+    IGS_REQUIRE(num_points == 0 || (xys && radii && cum_tiles_hit), "%s: null pointer", who);
+    IGS_REQUIRE(num_points == 0 || igs::aligned(xys, 8), "%s: xys must be 8-byte aligned", who);
 
     char *ws = static_cast<char *>(workspace);
     int *tile_count = reinterpret_cast<int *>(ws);
@@ -344,12 +370,13 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
     ws += round256(sizeof(int) * (size_t)capacity);
     int *unsorted = reinterpret_cast<int *>(ws);
 
-    if (cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch("igs_sort_intersects");
+    if (cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch(who);
     // slots are bounded by the capacity; a grid-stride loop over them reads the true count on the device
     const int slot_blocks = std::min(igs::ceil_div(capacity, 256), 148 * 16);
     if (num_points > 0) {
         count_kernel<<<slot_blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
-                                                 (unsigned)tiles_x, (unsigned)tiles_y, tile_count, slot_tile_rank, slot_gaussian);
+                                                 (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin, (unsigned)row_end, tile_count,
+                                                 slot_tile_rank, slot_gaussian);
     }
     tile_scan_kernel<<<1, kScanThreads, 0, s>>>(num_tiles, tile_count, reinterpret_cast<int2 *>(tile_bins), total);
     if (num_points > 0) {
@@ -359,7 +386,35 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
     order_kernel<<<igs::ceil_div(num_tiles, kOrderWarps), kOrderWarps * 32, 0, s>>>(num_tiles, capacity,
                                                                                     reinterpret_cast<const int2 *>(tile_bins), unsorted,
                                                                                     total, gaussian_ids_sorted);
-    return igs::check_launch("igs_sort_intersects");
+    return igs::check_launch(who);
+}
+
+int igs_sort_intersects(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                        int tiles_y, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace, size_t workspace_bytes,
+                        void *stream) {
+    return sort_band(num_points, capacity, xys, radii, cum_tiles_hit, tiles_x, tiles_y, 0, tiles_y, gaussian_ids_sorted, tile_bins,
+                     workspace, workspace_bytes, stream, "igs_sort_intersects");
+}
+
+int igs_band_tiles_hit(int num_points, const float *xys, const int32_t *radii, int tiles_x, int tiles_y, int row_begin, int row_end,
+                       int32_t *num_tiles_hit, void *stream) {
+    IGS_REQUIRE(num_points >= 0 && tiles_x >= 0 && tiles_y >= 0, "igs_band_tiles_hit: negative size");
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "igs_band_tiles_hit: tile rows [%d, %d) outside [0, %d)",
+                row_begin, row_end, tiles_y);
+    if (num_points == 0) return IGS_OK;
+    IGS_REQUIRE(xys && radii && num_tiles_hit, "igs_band_tiles_hit: null pointer");
+    IGS_REQUIRE(igs::aligned(xys, 8), "igs_band_tiles_hit: xys must be 8-byte aligned");
+    band_hits_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
+        num_points, reinterpret_cast<const float2 *>(xys), radii, (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin,
+        (unsigned)row_end, num_tiles_hit);
+    return igs::check_launch("igs_band_tiles_hit");
+}
+
+int igs_sort_intersects_band(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                             int tiles_y, int row_begin, int row_end, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace,
+                             size_t workspace_bytes, void *stream) {
+    return sort_band(num_points, capacity, xys, radii, cum_tiles_hit, tiles_x, tiles_y, row_begin, row_end, gaussian_ids_sorted, tile_bins,
+                     workspace, workspace_bytes, stream, "igs_sort_intersects_band");
 }
 
 }  // extern "C"

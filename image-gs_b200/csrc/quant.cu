@@ -107,3 +107,45 @@ int igs_quantize_ste(int num_points, int channels, const float *xy, const float 
 }
 
 }  // extern "C"
+
+// Backward of the loss-space feature transform of the forward above (feat_t = feat T^T, model.py:963-964) with the straight-through
+// identity: v_feat = v_feat_t T (+ v_extra, e.g. the rate term's gradient with respect to the same features), one thread per Gaussian.
+namespace {
+
+template <int C>
+__global__ void __launch_bounds__(256) feat_transform_bwd_kernel(const int n, const int channels_rt, const float *__restrict__ v_feat_t,
+                                                                 const float *__restrict__ transform, const float *__restrict__ v_extra,
+                                                                 float *__restrict__ v_feat) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    const int channels = C > 0 ? C : channels_rt;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float g[kMaxC];
+#pragma unroll
+    for (int d = 0; d < kMaxC; ++d) g[d] = d < channels ? v_feat_t[(size_t)i * channels + d] : 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+        if (c >= channels) continue;
+        float acc = v_extra ? v_extra[(size_t)i * channels + c] : 0.f;
+#pragma unroll
+        for (int d = 0; d < kMaxC; ++d)
+            if (d < channels) acc = __fmaf_rn(g[d], __ldg(&transform[d * channels + c]), acc);
+        v_feat[(size_t)i * channels + c] = acc;
+    }
+}
+
+}  // namespace
+
+extern "C" int igs_feat_transform_bwd(int num_points, int channels, const float *v_feat_t, const float *feat_transform, const float *v_extra,
+                                      float *v_feat, void *stream) {
+    IGS_REQUIRE(num_points >= 0, "igs_feat_transform_bwd: negative size");
+    IGS_REQUIRE(channels >= 1 && channels <= kMaxChannels, "igs_feat_transform_bwd: 1 to %d channels", kMaxChannels);
+    if (num_points == 0) return IGS_OK;
+    IGS_REQUIRE(v_feat_t && feat_transform && v_feat, "igs_feat_transform_bwd: null pointer");
+    const int blocks = igs::ceil_div(num_points, 256);
+    if (channels == 3)
+        feat_transform_bwd_kernel<3><<<blocks, 256, 0, igs::as_stream(stream)>>>(num_points, channels, v_feat_t, feat_transform, v_extra, v_feat);
+    else
+        feat_transform_bwd_kernel<0><<<blocks, 256, 0, igs::as_stream(stream)>>>(num_points, channels, v_feat_t, feat_transform, v_extra, v_feat);
+    return igs::check_launch("igs_feat_transform_bwd");
+}

@@ -23,6 +23,8 @@
 //   * raster_bwd_kernel (the [H, W, 10] operator): each warp visits the union of its 32 pixels' top-K Gaussians in
 //     increasing key order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving
 //     reduce-scatter, and adds them into per-tile shared accumulators or directly to the outputs.
+#include <algorithm>
+
 #include "igs_common.cuh"
 
 namespace {
@@ -47,11 +49,12 @@ struct PixelCoord {
     int tid;   // thread / pixel index within the tile
 };
 
-// Warp w covers the 8x4 patch (w % 2, w / 2) of the tile; lane l its pixel (l % 8, l / 8)
-__device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x) {
+// Warp w covers the 8x4 patch (w % 2, w / 2) of the tile; lane l its pixel (l % 8, l / 8). Tiles are numbered within a band of tile rows
+// starting at row_begin (0 for the whole image); the coordinates are the image's.
+__device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_begin) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int lx = (warp & 1) * 8 + (lane & 7), ly = (warp >> 1) * 4 + (lane >> 3);
-    return {(tile / tiles_x) * kTile + ly, (tile % tiles_x) * kTile + lx, tid};
+    return {(row_begin + tile / tiles_x) * kTile + ly, (tile % tiles_x) * kTile + lx, tid};
 }
 
 // sigma of a Gaussian at a pixel, with the reference's operation order (forward.cu:309-311)
@@ -60,27 +63,15 @@ __device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, flo
     return 0.5f * (a * dx * dx + c * dy * dy) + b * dx * dy;
 }
 
-template <int C>
-__global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
-                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
-                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
-                                                              const float *__restrict__ colors, float *__restrict__ out_img,
-                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk) {
-    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
-    const int channels = C > 0 ? C : channels_rt;
-    __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
-    __shared__ float s_cc[kChunk];    // conic c
-    __shared__ int s_ids[kThreads * kTopK];
-
-    const int tile = blockIdx.x;
-    const PixelCoord pc = tile_pixel(tile, tiles_x);
-    const bool inside = pc.i < img_h && pc.j < img_w;
-    const float px = (float)pc.j, py = (float)pc.i;
-    const int2 range = tile_bins[tile];
+// The top-K selection of one pixel over its tile's list (range into ids_sorted), in list order: the slot rule of the reference (free slots
+// fill in order, then a Gaussian whose alpha exceeds the minimum replaces the first slot holding it) with a fast fill of the first ten
+// entries. The list is staged through s_geo / s_cc in chunks of kChunk entries, with CTA barriers: every thread of the CTA must call it.
+// pos[k]: list position of slot k's Gaussian (-1 empty); val[k]: its alpha.
+__device__ __forceinline__ void select_topk(const int2 range, const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
+                                            const float *__restrict__ conics, const bool inside, const float px, const float py,
+                                            float4 *s_geo, float *s_cc, int (&pos)[kTopK], float (&val)[kTopK]) {
+    const int tid = threadIdx.x;
     const int len = range.y - range.x;
-
-    int pos[kTopK];
-    float val[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
         pos[k] = -1;
@@ -92,11 +83,11 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
     for (int base = 0; base < len; base += kChunk) {
         const int count = min(kChunk, len - base);
         __syncthreads();
-        if (pc.tid < count) {
-            const int g = __ldg(&ids_sorted[range.x + base + pc.tid]);
+        if (tid < count) {
+            const int g = __ldg(&ids_sorted[range.x + base + tid]);
             const float2 xy = __ldg(&xys[g]);
-            s_geo[pc.tid] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            s_cc[pc.tid] = __ldg(&conics[3 * g + 2]);
+            s_geo[tid] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            s_cc[tid] = __ldg(&conics[3 * g + 2]);
         }
         __syncthreads();
         if (!inside) continue;
@@ -162,6 +153,31 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
             }
         }
     }
+}
+
+template <int C>
+__global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
+                                                              const int band_h, const int channels_rt,
+                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
+                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
+                                                              const float *__restrict__ colors, float *__restrict__ out_img,
+                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk) {
+    constexpr int kMaxC = C > 0 ? C : kMaxChannels;
+    const int channels = C > 0 ? C : channels_rt;
+    __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
+    __shared__ float s_cc[kChunk];    // conic c
+    __shared__ int s_ids[kThreads * kTopK];
+
+    const int tile = blockIdx.x;
+    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const float px = (float)pc.j, py = (float)pc.i;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+
+    int pos[kTopK];
+    float val[kTopK];
+    select_topk(range, ids_sorted, xys, conics, inside, px, py, s_geo, s_cc, pos, val);
 
     // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
     int gid[kTopK];
@@ -184,18 +200,20 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
         for (int c = 0; c < kMaxC; ++c)
             if (c < channels) pix[c] += __ldg(&f[c]) * vis;
     }
-    const int num_pixels = img_h * img_w;
+    const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
     if (inside) {
-        const int p = pc.i * img_w + pc.j;
+        const int p = (pc.i - row_begin * kTile) * img_w + pc.j;
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)
             if (c < channels) out_img[(size_t)c * num_pixels + p] = pix[c];
     }
 
     if (tile_topk != nullptr) {
+        // a tile whose list holds 65535 entries or more is left empty: raster_bwd_pairs_kernel selects its lists again
+        const bool addressable = len < (int)kNoSlot;
         uint16_t *dst = tile_topk + (size_t)tile * kTopK * kThreads + pc.tid;
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) dst[k * kThreads] = pos[k] >= 0 ? (uint16_t)pos[k] : kNoSlot;
+        for (int k = 0; k < kTopK; ++k) dst[k * kThreads] = (addressable && pos[k] >= 0) ? (uint16_t)pos[k] : kNoSlot;
     }
     if (pixel_topk != nullptr) {
         // stage the IDs by thread, then write each tile row of 16 pixels x 10 IDs (80 int2) with consecutive threads
@@ -279,7 +297,7 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 
     const int tile = blockIdx.x;
     const int lane = threadIdx.x & 31;
-    const PixelCoord pc = tile_pixel(tile, tiles_x);
+    const PixelCoord pc = tile_pixel(tile, tiles_x, 0);
     const bool inside = pc.i < img_h && pc.j < img_w;
     const float px = (float)pc.j, py = (float)pc.i;
     const int num_pixels = img_h * img_w;
@@ -446,7 +464,8 @@ struct PairSmem {
 };
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
+__global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
+                                                                    const int band_h, const int channels_rt,
                                                                     const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
                                                                     const float2 *__restrict__ xys, const float *__restrict__ conics,
                                                                     const float *__restrict__ colors, const float *__restrict__ v_output,
@@ -463,21 +482,28 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     const int len = range.y - range.x;
     if (len <= 0) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const PixelCoord pc = tile_pixel(tile, tiles_x);
+    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
     const bool inside = pc.i < img_h && pc.j < img_w;
     const float px = (float)pc.j, py = (float)pc.i;
-    const int num_pixels = img_h * img_w;
-    const int p = inside ? pc.i * img_w + pc.j : 0;
+    const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
+    const int p = inside ? (pc.i - row_begin * kTile) * img_w + pc.j : 0;
 
     // the pixel's loads, issued before the staging barrier so that their latency overlaps it
     float v_out[kMaxC];
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
     int key[kTopK];
+    if (len < (int)kNoSlot) {
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
-        key[k] = v == kNoSlot ? -1 : (int)v;
+        for (int k = 0; k < kTopK; ++k) {
+            const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
+            key[k] = v == kNoSlot ? -1 : (int)v;
+        }
+    } else {
+        // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
+        float val[kTopK];
+        select_topk(range, ids_sorted, xys, conics, inside, px, py, sm.geo, sm.cc, key, val);
+        __syncthreads();  // the staging arrays are reused below
     }
 
     // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
@@ -640,22 +666,27 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
 }
 
 template <int C>
-cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
-                       const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk, cudaStream_t s) {
-    raster_fwd_kernel<C><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, out, pixel_topk,
-                                                     tile_topk);
+cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids, const int2 *bins,
+                       const float2 *xys, const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk,
+                       cudaStream_t s) {
+    raster_fwd_kernel<C><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys, conics, colors, out,
+                                                     pixel_topk, tile_topk);
     return cudaGetLastError();
 }
 
-int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int channels, const int32_t *ids_sorted, const int32_t *tile_bins,
-               const float *xys, const float *conics, const float *colors, float *out_img, int32_t *pixel_topk, uint16_t *tile_topk,
-               void *stream, const char *who) {
+int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, const int32_t *ids_sorted,
+               const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, float *out_img, int32_t *pixel_topk,
+               uint16_t *tile_topk, void *stream, const char *who) {
     IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && img_h >= 0 && img_w >= 0, "%s: negative size", who);
     IGS_REQUIRE(channels >= 0 && channels <= kMaxChannels, "%s: at most %d channels (got %d)", who, kMaxChannels, channels);
     IGS_REQUIRE(tiles_x == igs::ceil_div(img_w, kTile) && tiles_y == igs::ceil_div(img_h, kTile),
                 "%s: tile grid %dx%d does not cover a %dx%d image with %dx%d tiles", who, tiles_x, tiles_y, img_w, img_h, kTile, kTile);
-    const int tiles = tiles_x * tiles_y;
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
+                row_end, tiles_y);
+    IGS_REQUIRE(pixel_topk == nullptr || (row_begin == 0 && row_end == tiles_y), "%s: [H, W, 10] lists cover the whole image", who);
+    const int tiles = tiles_x * (row_end - row_begin);
     if (tiles == 0) return IGS_OK;
+    const int band_h = std::min(img_h, row_end * kTile) - row_begin * kTile;
     IGS_REQUIRE(tile_bins && xys && conics && (colors || channels == 0) && (out_img || channels == 0), "%s: null pointer", who);
     IGS_REQUIRE(igs::aligned(tile_bins, 8) && igs::aligned(xys, 8), "%s: tile_bins and xys must be 8-byte aligned", who);
     IGS_REQUIRE(pixel_topk == nullptr || igs::aligned(pixel_topk, 8), "%s: pixel_topk must be 8-byte aligned", who);
@@ -664,10 +695,10 @@ int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int channels, con
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
     cudaError_t err;
     switch (channels) {
-        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s);
+        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
+        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s);
     }
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;
@@ -683,20 +714,21 @@ cudaError_t launch_bwd(int tiles, int tiles_x, int img_h, int img_w, int channel
 }
 
 template <int C, int NV>
-cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
-                             const float *conics, const float *colors, const float *v_output, const uint16_t *tile_topk, float *v_xy,
-                             float *v_conic, float *v_colors, cudaStream_t s) {
+cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids,
+                             const int2 *bins, const float2 *xys, const float *conics, const float *colors, const float *v_output,
+                             const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, cudaStream_t s) {
     constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
     const size_t bytes = sizeof(PairSmem<kMaxC>);
     // more than the 48 KB default of dynamic shared memory (set on every call: cheap, and correct for whichever device is current)
     cudaError_t err = cudaFuncSetAttribute(raster_bwd_pairs_kernel<C, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (err != cudaSuccess) return err;
-    raster_bwd_pairs_kernel<C, NV><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
-                                                                  tile_topk, v_xy, v_conic, v_colors);
+    raster_bwd_pairs_kernel<C, NV><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys, conics,
+                                                                  colors, v_output, tile_topk, v_xy, v_conic, v_colors);
     return cudaGetLastError();
 }
 
-int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys,
+int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, int num_points, const int32_t *ids_sorted,
+               const int32_t *tile_bins, const float *xys,
                const float *conics, const float *colors, const float *v_output, const int32_t *pixel_topk, const uint16_t *tile_topk,
                float *v_xy, float *v_conic, float *v_colors, void *stream, const char *who) {
     IGS_REQUIRE(img_h >= 0 && img_w >= 0 && num_points >= 0, "%s: negative size", who);
@@ -711,7 +743,12 @@ int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t
             return igs::check_launch(who);
     }
     const int tiles_x = igs::ceil_div(img_w, kTile), tiles_y = igs::ceil_div(img_h, kTile);
-    const int tiles = tiles_x * tiles_y;
+    if (row_end < 0) row_end = tiles_y;
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
+                row_end, tiles_y);
+    IGS_REQUIRE(pixel_topk == nullptr || (row_begin == 0 && row_end == tiles_y), "%s: [H, W, 10] lists cover the whole image", who);
+    const int tiles = tiles_x * (row_end - row_begin);
+    const int band_h = std::min(img_h, row_end * kTile) - row_begin * kTile;
     if (tiles == 0 || num_points == 0) return IGS_OK;
     IGS_REQUIRE(xys && conics && (colors || channels == 0) && (v_output || channels == 0), "%s: null pointer", who);
     IGS_REQUIRE(pixel_topk || (tile_topk && tile_bins && ids_sorted), "%s: null top-K lists", who);
@@ -722,15 +759,15 @@ int raster_bwd(int img_h, int img_w, int channels, int num_points, const int32_t
     if (tile_topk != nullptr) {
         // tiles with lists up to kPairStage entries; the union-walk kernel below takes the longer ones
         if (channels == 3)
-            err = launch_bwd_pairs<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<3, 8>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else if (channels <= 3)
-            err = launch_bwd_pairs<0, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<0, 8>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else if (channels == 9)
-            err = launch_bwd_pairs<9, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<9, 16>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else if (channels <= 11)
-            err = launch_bwd_pairs<0, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<0, 16>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         else
-            err = launch_bwd_pairs<0, 32>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
+            err = launch_bwd_pairs<0, 32>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
         if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     }
     if (tile_topk != nullptr) return IGS_OK;  // the pairs kernel handled every tile
@@ -756,25 +793,23 @@ int igs_raster_fwd_topk(int tiles_x, int tiles_y, int img_height, int img_width,
                         const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, float *out_img,
                         int32_t *pixel_topk, void *stream) {
     IGS_REQUIRE(pixel_topk != nullptr || (int64_t)img_height * img_width == 0, "igs_raster_fwd_topk: null pixel_topk");
-    return raster_fwd(tiles_x, tiles_y, img_height, img_width, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors, out_img,
-                      pixel_topk, nullptr, stream, "igs_raster_fwd_topk");
+    return raster_fwd(tiles_x, tiles_y, img_height, img_width, 0, tiles_y, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors,
+                      out_img, pixel_topk, nullptr, stream, "igs_raster_fwd_topk");
 }
 
 int igs_raster_fwd_topk_tiles(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
                               const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
                               const float *colors, float *out_img, uint16_t *tile_topk, void *stream) {
     IGS_REQUIRE(tile_topk != nullptr || tiles_x * tiles_y == 0, "igs_raster_fwd_topk_tiles: null tile_topk");
-    IGS_REQUIRE(max_list_len >= 0 && max_list_len < (int)kNoSlot,
-                "igs_raster_fwd_topk_tiles: tile lists may hold up to %d entries, more than 16-bit positions address (use igs_raster_fwd_topk)",
-                max_list_len);
-    return raster_fwd(tiles_x, tiles_y, img_height, img_width, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors, out_img,
-                      nullptr, tile_topk, stream, "igs_raster_fwd_topk_tiles");
+    IGS_REQUIRE(max_list_len >= 0, "igs_raster_fwd_topk_tiles: negative max_list_len");
+    return raster_fwd(tiles_x, tiles_y, img_height, img_width, 0, tiles_y, channels, gaussian_ids_sorted, tile_bins, xys, conics, colors,
+                      out_img, nullptr, tile_topk, stream, "igs_raster_fwd_topk_tiles");
 }
 
 int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
                         const float *colors, const float *v_output, const int32_t *pixel_topk, float *v_xy, float *v_conic,
                         float *v_colors, void *stream) {
-    return raster_bwd(img_height, img_width, channels, num_points, nullptr, nullptr, xys, conics, colors, v_output, pixel_topk, nullptr,
+    return raster_bwd(img_height, img_width, 0, -1, channels, num_points, nullptr, nullptr, xys, conics, colors, v_output, pixel_topk, nullptr,
                       v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk");
 }
 
@@ -782,8 +817,27 @@ int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int n
                               const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
                               const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream) {
     IGS_REQUIRE(tile_topk != nullptr, "igs_raster_bwd_topk_tiles: null tile_topk");
-    return raster_bwd(img_height, img_width, channels, num_points, gaussian_ids_sorted, tile_bins, xys, conics, colors, v_output, nullptr,
+    return raster_bwd(img_height, img_width, 0, -1, channels, num_points, gaussian_ids_sorted, tile_bins, xys, conics, colors, v_output, nullptr,
                       tile_topk, v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk_tiles");
+}
+
+int igs_raster_fwd_topk_tiles_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                                   int max_list_len, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                                   const float *conics, const float *colors, float *out_band, uint16_t *tile_topk, void *stream) {
+    IGS_REQUIRE(max_list_len >= 0, "igs_raster_fwd_topk_tiles_band: negative max_list_len");
+    IGS_REQUIRE(tile_topk != nullptr || row_begin == row_end, "igs_raster_fwd_topk_tiles_band: null tile_topk");
+    return raster_fwd(tiles_x, tiles_y, img_height, img_width, row_begin, row_end, channels, gaussian_ids_sorted, tile_bins, xys, conics,
+                      colors, out_band, nullptr, tile_topk, stream, "igs_raster_fwd_topk_tiles_band");
+}
+
+int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin, int row_end, int channels, int num_points,
+                                   const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                                   const float *colors, const float *v_output_band, const uint16_t *tile_topk, float *v_xy, float *v_conic,
+                                   float *v_colors, void *stream) {
+    IGS_REQUIRE(tile_topk != nullptr, "igs_raster_bwd_topk_tiles_band: null tile_topk");
+    IGS_REQUIRE(row_end >= 0, "igs_raster_bwd_topk_tiles_band: negative row_end");
+    return raster_bwd(img_height, img_width, row_begin, row_end, channels, num_points, gaussian_ids_sorted, tile_bins, xys, conics, colors,
+                      v_output_band, nullptr, tile_topk, v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk_tiles_band");
 }
 
 }  // extern "C"

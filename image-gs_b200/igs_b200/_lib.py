@@ -30,10 +30,15 @@ SIGNATURES = {
     "igs_raster_fwd_topk_tiles": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),
     "igs_raster_bwd_topk": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     "igs_raster_bwd_topk_tiles": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
+    "igs_band_tiles_hit": (c_int, [c_int, P, P, c_int, c_int, c_int, c_int, P, P]),
+    "igs_sort_intersects_band": (c_int, [c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
+    "igs_raster_fwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),
+    "igs_raster_bwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
     "igs_loo_loss_increase": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, c_int, c_float, P, P]),
     "igs_l1_workspace": (c_size_t, [c_int64]),
     "igs_l1_loss": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
     "igs_quantize_ste": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_float, P, P, P, P, P, P, P, P, P, P, P, P]),
+    "igs_feat_transform_bwd": (c_int, [c_int, c_int, P, P, P, P, P]),
     "igs_rate_workspace": (c_size_t, [c_int]),
     "igs_rate_fwd": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_float, c_float, c_float, P, P, P, P, P, c_size_t,
                              P]),

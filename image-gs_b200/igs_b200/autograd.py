@@ -7,8 +7,9 @@ Differentiable operators of the training step, with the semantics of the referen
   - rate_loss (compress/rate.py:178-202)
   - l1_loss: ratio * F.l1_loss with its gradient computed in the same pass
 
-The rasterization's autograd path keeps each pixel's top-K lists in the 16-bit tile-list form (half the bytes of [H, W, 10] int32) when
-every tile list is shorter than 65535 entries (guaranteed for fewer than 65535 Gaussians or intersections), else the reference's form.
+The rasterization's autograd path keeps each pixel's top-K lists in the 16-bit tile-list form (positions in the tile's list; a quarter of
+the bytes of the reference's [H, W, 10] int32 ids); the backward pass selects the lists of a tile again when its list reaches 65535
+entries.
 """
 from typing import Optional
 
@@ -74,15 +75,9 @@ class _RasterizeGaussiansSumTopK(Function):
             return torch.zeros(img_height, img_width, colors.shape[-1], device=xys.device, dtype=torch.float32)
         bound = min(num_points, num_intersects)
         img_size = (img_width, img_height, 1)
-        if bound <= ops.MAX_TILE_LIST:
-            out_img, tile_topk = ops.nd_rasterize_forward_topk_norm_tiles(tile_bounds, img_size, bound, ids, bins, xys, conics, colors)
-            ctx.form = "tiles"
-            ctx.save_for_backward(xys, conics, colors, ids, bins, tile_topk)
-        else:
-            out_img, pixel_topk = ops.nd_rasterize_forward_topk_norm(tile_bounds, (ops.TILE, ops.TILE, 1), img_size, ids, bins, xys, conics,
-                                                                     colors)
-            ctx.form = "pixels"
-            ctx.save_for_backward(xys, conics, colors, pixel_topk)
+        out_img, tile_topk = ops.nd_rasterize_forward_topk_norm_tiles(tile_bounds, img_size, bound, ids, bins, xys, conics, colors)
+        ctx.form = "tiles"
+        ctx.save_for_backward(xys, conics, colors, ids, bins, tile_topk)
         # channel-planar [C, H, W] returned as an [H, W, C] view (rasterize_sum.py:248-265)
         return out_img.permute(1, 2, 0)
 
@@ -92,14 +87,9 @@ class _RasterizeGaussiansSumTopK(Function):
             xys, conics, colors = ctx.saved_tensors
             return torch.zeros_like(xys), None, torch.zeros_like(conics), None, torch.zeros_like(colors), None, None, None
         v_output = v_out_img.permute(2, 0, 1).contiguous()  # channel-planar; free when the caller's gradient is [C, H, W]
-        if ctx.form == "tiles":
-            xys, conics, colors, ids, bins, tile_topk = ctx.saved_tensors
-            v_xy, v_conic, v_colors = ops.nd_rasterize_backward_topk_norm_tiles(ctx.img_height, ctx.img_width, ids, bins, xys, conics, colors,
-                                                                                v_output, tile_topk)
-        else:
-            xys, conics, colors, pixel_topk = ctx.saved_tensors
-            v_xy, v_conic, v_colors = ops.nd_rasterize_backward_topk_norm(ctx.img_height, ctx.img_width, ops.TILE, ops.TILE, xys, conics,
-                                                                          colors, v_output, pixel_topk)
+        xys, conics, colors, ids, bins, tile_topk = ctx.saved_tensors
+        v_xy, v_conic, v_colors = ops.nd_rasterize_backward_topk_norm_tiles(ctx.img_height, ctx.img_width, ids, bins, xys, conics, colors,
+                                                                            v_output, tile_topk)
         return v_xy, None, v_conic, None, v_colors, None, None, None
 
 

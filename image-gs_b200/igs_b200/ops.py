@@ -16,7 +16,6 @@ TILE = 16
 TOP_K = 10
 MAX_CHANNELS = 12
 EPS = 1e-4
-MAX_TILE_LIST = 65534  # longest tile list the 16-bit tile-list form of the top-K lists addresses
 
 
 def _check_input(t: torch.Tensor, name: str, dtype=None):

@@ -24,13 +24,28 @@ class RasterStep:
     """One image's step. Inputs are device tensors: means [N,2], scales [N,2] (pixels), rotations [N,1], features [N,C], target [C,H,W]."""
 
     def __init__(self, means, scales, rotations, features, target, capacity: Optional[int] = None, capacity_ratio: float = 2.0,
-                 l1_ratio: float = 1.0, tile_row_range=None):
+                 l1_ratio: float = 1.0, quant: Optional[dict] = None, loss_transform=None, rate: Optional[dict] = None):
+        """quant: dict(pos_steps [2], scale_step, rot_step, feat_steps [C]) puts the straight-through quantizer in front (scales must be
+        the canonical, non-negative ones); loss_transform [C,C]: render feat T^T (YUV loss space, needs quant); rate: dict(model (the
+        fields of compress.rate.RateModel), inv_rot_step, factor) adds the rate term on the raw features and rotations."""
         self.lib = _lib.load()
         self.device = means.device
         self.n, self.c = features.shape
         c, self.h, self.w = target.shape
         assert c == self.c
+        self.raw = (means, scales, rotations, features)
         self.means, self.scales, self.rotations, self.features, self.target = means, scales, rotations, features, target
+        self.quant, self.rate = quant, rate
+        self.transform = loss_transform.contiguous() if loss_transform is not None else None
+        if self.quant is not None:
+            self.q_means, self.q_scales, self.q_rot, self.q_feat = (torch.empty_like(means), torch.empty_like(scales),
+                                                                    torch.empty_like(rotations), torch.empty_like(features))
+            self.feat_t = torch.empty_like(features) if self.transform is not None else None
+            self.means, self.scales, self.rotations = self.q_means, self.q_scales, self.q_rot
+            self.features = self.feat_t if self.transform is not None else self.q_feat
+            self._quantize()
+        elif self.transform is not None:
+            raise ValueError("loss_transform is applied by the quantizer stage; pass quant as well")
         self.tb = ops.tile_grid(self.h, self.w)
         self.num_tiles = self.tb[0] * self.tb[1]
         self.l1_ratio = float(l1_ratio)
@@ -66,14 +81,55 @@ class RasterStep:
         self.sort_ws_bytes = self.lib.igs_sort_workspace(self.capacity, self.tb[0], self.tb[1])
         self.sort_ws = torch.empty(self.sort_ws_bytes, device=dev, dtype=torch.uint8)
         self.max_list = min(self.n, self.capacity)
-        self.tile_form = self.max_list <= ops.MAX_TILE_LIST
-        if self.tile_form:
-            self.topk = torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
-        else:
-            self.topk = torch.empty(self.h, self.w, TOP_K, device=dev, dtype=i32)
+        # top-K lists in the 16-bit tile-list form (tiles with 65535+ entries are selected again by the backward pass)
+        self.topk = torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        if self.rate is not None:
+            m = self.rate["model"]
+            self.rate_loss = torch.empty((), device=dev, dtype=f32)
+            self.rate_weight = torch.empty(1, device=dev, dtype=f32)
+            self.rate_own_grad = torch.empty_like(features)
+            self.rate_rot_grad = torch.empty(n, device=dev, dtype=f32)
+            self.rate_grad_feat = torch.empty_like(features)
+            self.rate_grad_rot = torch.empty(n, device=dev, dtype=f32)
+            self.rate_ws_bytes = self.lib.igs_rate_workspace(n)
+            self.rate_ws = torch.zeros(self.rate_ws_bytes, device=dev, dtype=torch.uint8)
+            self.rate_refs = ((ctypes.c_int32 * nc)(*m.color_refs), (ctypes.c_int32 * nc)(*m.pred_channels))
+            self.grad_one = torch.ones((), device=dev, dtype=f32)
+        if self.transform is not None or self.rate is not None:
+            self.v_feat = torch.empty_like(features)  # gradient of the raw features
         self.graph = None
 
     # ---- stages (each one C-ABI call on the current stream) ----
+
+    def _quantize(self):
+        q = self.quant
+        means, scales, rots, feats = self.raw
+        self._check(self.lib.igs_quantize_ste(self.n, self.c, ptr(means), ptr(scales), ptr(rots), ptr(feats), ptr(q["pos_steps"]),
+                                              float(q["scale_step"]), float(q["rot_step"]), ptr(q["feat_steps"]), ptr(self.transform),
+                                              ptr(self.q_means), ptr(self.q_scales), ptr(self.q_rot), ptr(self.q_feat), ptr(self.feat_t),
+                                              None, None, None, None, self._stream()), "quantize")
+
+    def _rate_term(self):
+        m, r = self.rate["model"], self.rate
+        _, _, rots, feats = self.raw
+        self._check(self.lib.igs_rate_fwd(self.n, self.c, m.neighbors.size(1), ptr(feats), ptr(rots), ptr(self.loss), ptr(m.neighbors),
+                                          ptr(m.weights), ptr(m.slope), ctypes.cast(self.rate_refs[0], ctypes.c_void_p),
+                                          ctypes.cast(self.rate_refs[1], ctypes.c_void_p), ptr(m.inv_steps), ptr(m.feat_coeffs),
+                                          ptr(m.inv_rot), float(r["inv_rot_step"]), self.l1_ratio, float(r["factor"]), ptr(self.rate_loss),
+                                          ptr(self.rate_weight), ptr(self.rate_own_grad), ptr(self.rate_rot_grad), ptr(self.rate_ws),
+                                          self.rate_ws_bytes, self._stream()), "rate forward")
+        self._check(self.lib.igs_rate_bwd(self.n, self.c, ptr(self.grad_one), ptr(self.rate_weight), ptr(self.rate_own_grad),
+                                          ptr(self.rate_rot_grad), ptr(m.offsets), ptr(m.sources), ptr(m.source_weights), ptr(self.rate_grad_feat),
+                                          ptr(self.rate_grad_rot), self._stream()), "rate backward")
+
+    def _feature_grads(self):
+        """Gradient of the raw features: through the loss-space transform (identity without one) plus the rate term's."""
+        extra = self.rate_grad_feat if self.rate is not None else None
+        if self.transform is not None:
+            self._check(self.lib.igs_feat_transform_bwd(self.n, self.c, ptr(self.v_colors), ptr(self.transform), ptr(extra), ptr(self.v_feat),
+                                                        self._stream()), "feature transform backward")
+        else:
+            torch.add(self.v_colors, extra, out=self.v_feat)
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -96,38 +152,37 @@ class RasterStep:
                     "bin")
 
     def _forward(self):
-        if self.tile_form:
-            st = self.lib.igs_raster_fwd_topk_tiles(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
-                                                    ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.image),
-                                                    ptr(self.topk), self._stream())
-        else:
-            st = self.lib.igs_raster_fwd_topk(self.tb[0], self.tb[1], self.h, self.w, self.c, ptr(self.ids), ptr(self.bins), ptr(self.xys),
-                                              ptr(self.conics), ptr(self.features), ptr(self.image), ptr(self.topk), self._stream())
-        self._check(st, "forward")
+        self._check(self.lib.igs_raster_fwd_topk_tiles(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
+                                                       ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.image),
+                                                       ptr(self.topk), self._stream()), "forward")
 
     def _loss(self):
         self._check(self.lib.igs_l1_loss(self.image.numel(), ptr(self.image), ptr(self.target), self.l1_ratio, ptr(self.loss),
                                          ptr(self.v_image), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "l1")
 
     def _backward(self):
-        if self.tile_form:
-            st = self.lib.igs_raster_bwd_topk_tiles(self.h, self.w, self.c, self.n, ptr(self.ids), ptr(self.bins), ptr(self.xys),
-                                                    ptr(self.conics), ptr(self.features), ptr(self.v_image), ptr(self.topk), ptr(self.v_xy),
-                                                    ptr(self.v_conic), ptr(self.v_colors), self._stream())
-        else:
-            st = self.lib.igs_raster_bwd_topk(self.h, self.w, self.c, self.n, ptr(self.xys), ptr(self.conics), ptr(self.features),
-                                              ptr(self.v_image), ptr(self.topk), ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_colors),
-                                              self._stream())
-        self._check(st, "backward")
+        self._check(self.lib.igs_raster_bwd_topk_tiles(self.h, self.w, self.c, self.n, ptr(self.ids), ptr(self.bins), ptr(self.xys),
+                                                       ptr(self.conics), ptr(self.features), ptr(self.v_image), ptr(self.topk), ptr(self.v_xy),
+                                                       ptr(self.v_conic), ptr(self.v_colors), self._stream()), "backward")
 
     def _project_backward(self):
         self._check(self.lib.igs_project_bwd(self.n, ptr(self.scales), ptr(self.rotations), self.h, self.w, ptr(self.radii), ptr(self.conics),
                                              ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                              ptr(self.v_rot), self._stream()), "project_backward")
 
-    STAGES = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward", "_project_backward")
+    BASE_STAGES = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward", "_project_backward")
     # kernels each stage launches (memsets excluded)
-    KERNELS = {"_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1}
+    KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1,
+               "_rate_term": 2, "_feature_grads": 1}
+
+    @property
+    def STAGES(self):
+        stages = (("_quantize",) if self.quant is not None else ()) + self.BASE_STAGES
+        if self.rate is not None:
+            stages += ("_rate_term",)
+        if self.rate is not None or self.transform is not None:
+            stages += ("_feature_grads",)
+        return stages
 
     def launch(self):
         for s in self.STAGES:
@@ -135,7 +190,7 @@ class RasterStep:
 
     @property
     def kernels_per_step(self):
-        return sum(self.KERNELS.values())
+        return sum(self.KERNELS[s] for s in self.STAGES)
 
     def capture(self, stages=None):
         """A CUDA graph of the step (or of the given stages)."""

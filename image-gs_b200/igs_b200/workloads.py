@@ -33,6 +33,7 @@ class Workload:
     rate_term: bool = False
     seed: int = 1000
     images: int = 1  # independent images of this shape (texture stacks)
+    sharding: str = "images"  # across GPUs: "images" (one independent image per GPU) or "bands" (tile-row bands of one image)
     notes: str = field(default="", compare=False)
 
     @property
@@ -57,7 +58,7 @@ CONFIGS = {
                               rate_term=True, seed=1002, notes="854x480 YUV, 4k Gaussians, luma-weighted L1 + rate term, feature step 1/64"),
     "cfg3_1080p": Workload("cfg3_1080p", 1080, 1920, 20000, 3, math.log(3.0), 0.6, seed=1003,
                            notes="1920x1080 RGB, 20k Gaussians; headline fwd+bwd steps/s"),
-    "cfg4_2160p": Workload("cfg4_2160p", 2160, 3840, 80000, 3, math.log(3.0), 0.7, max_anisotropy=8.0, seed=1004,
+    "cfg4_2160p": Workload("cfg4_2160p", 2160, 3840, 80000, 3, math.log(3.0), 0.7, max_anisotropy=8.0, seed=1004, sharding="bands",
                            notes="3840x2160 RGB, 80k Gaussians; tile-row bands across GPUs with a gradient all-reduce"),
     "cfg5_tex9": Workload("cfg5_tex9", 2048, 2048, 50000, 9, math.log(3.0), 0.6, seed=1005, images=64,
                           notes="64 independent 2048x2048 9-channel texture stacks, 50k Gaussians each; one image per GPU"),
@@ -154,3 +155,25 @@ def input_digest(inputs):
         h.update(key.encode())
         h.update(inputs[key].contiguous().numpy().tobytes())
     return h.hexdigest()[:16]
+
+
+def quant_settings(wl: Workload, device):
+    """Step quantization settings of the reference's defaults (cfgs/default.yaml: pos_step 0.125 px, scale_step 1/32 octave, rot_step
+    0.703125 degrees, feature step 1/64) as the tensors of model.quant_steps (model.py:300-305)."""
+    return dict(pos_steps=(0.125 / torch.tensor([wl.width, wl.height], dtype=torch.float32)).to(device),
+                scale_step=float(torch.tensor(0.03125, dtype=torch.float32)), rot_step=float(torch.tensor(math.radians(0.703125),
+                                                                                                             dtype=torch.float32)),
+                feat_steps=torch.full((wl.channels,), 0.015625, dtype=torch.float32, device=device))
+
+
+class RateModelTensors:
+    """The fields of the reference's compress.rate.RateModel that the rate operators read, from a dict of arrays."""
+
+    def __init__(self, arrays, device):
+        t = lambda k, dt=torch.float32: torch.as_tensor(arrays[k]).to(device=device, dtype=dt).contiguous()  # noqa: E731
+        self.neighbors = t("neighbors", torch.int32)
+        self.weights, self.slope, self.inv_steps = t("weights"), t("slope"), t("inv_steps")
+        self.feat_coeffs, self.inv_rot = t("feat_coeffs"), t("inv_rot")
+        self.offsets, self.sources, self.source_weights = t("offsets", torch.int32), t("sources", torch.int32), t("source_weights")
+        self.color_refs = tuple(int(v) for v in arrays["color_refs"])
+        self.pred_channels = tuple(int(v) for v in arrays["pred_channels"])

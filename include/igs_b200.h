@@ -88,8 +88,8 @@ int igs_raster_fwd_topk(int tiles_x, int tiles_y, int img_height, int img_width,
 
 /* The same forward pass for the training step (rasterize_sum.py:169-267's autograd path): instead of pixel_topk, tile_topk
  * [T,10,256] uint16 holds each pixel's slots as positions in its tile's Gaussian list (0xFFFF empty), indexed by the pixel's lane in
- * the tile (warp w covers the 8x4 patch (w%2, w/2), lane l its pixel (l%8, l/8)). max_list_len bounds every tile list
- * (e.g. min(num_points, capacity)) and must be below 65535. */
+ * the tile (warp w covers the 8x4 patch (w%2, w/2), lane l its pixel (l%8, l/8)). Tiles whose list holds 65535 entries or more are left
+ * empty there; igs_raster_bwd_topk_tiles selects their lists again. max_list_len: an upper bound of the list lengths (informational). */
 int igs_raster_fwd_topk_tiles(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
                               const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
                               const float *colors, float *out_img, uint16_t *tile_topk, void *stream);
@@ -104,6 +104,31 @@ int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_poi
 int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int num_points, const int32_t *gaussian_ids_sorted,
                               const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
                               const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream);
+
+/* ---- tile-row bands (one image split over several GPUs; no counterpart in the reference, which renders on one GPU) ------------------ */
+
+/* The tiles of rows [row_begin, row_end) that each Gaussian's rectangle covers: the band's num_tiles_hit, to prefix-sum for its binning */
+int igs_band_tiles_hit(int num_points, const float *xys, const int32_t *radii, int tiles_x, int tiles_y, int row_begin, int row_end,
+                       int32_t *num_tiles_hit, void *stream);
+
+/* igs_sort_intersects restricted to tile rows [row_begin, row_end): cum_tiles_hit is the prefix sum of igs_band_tiles_hit; tile_bins
+ * [tiles_x * (row_end - row_begin), 2] numbers the band's tiles from its first row; workspace igs_sort_workspace(capacity, tiles_x,
+ * row_end - row_begin). The lists equal the matching slice of the whole image's. */
+int igs_sort_intersects_band(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
+                             int tiles_y, int row_begin, int row_end, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
+/* igs_raster_fwd_topk_tiles for a band: out_band [C, band_h, W] with band_h = min(H, 16 row_end) - 16 row_begin, the band's tile lists;
+ * pixel coordinates are the image's, so every value equals the whole image's. */
+int igs_raster_fwd_topk_tiles_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                                   int max_list_len, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                                   const float *conics, const float *colors, float *out_band, uint16_t *tile_topk, void *stream);
+
+/* igs_raster_bwd_topk_tiles for a band: v_output_band [C, band_h, W]; the gradients are this band's share (sum them over the bands) */
+int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin, int row_end, int channels, int num_points,
+                                   const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                                   const float *colors, const float *v_output_band, const uint16_t *tile_topk, float *v_xy, float *v_conic,
+                                   float *v_colors, void *stream);
 
 /* topk_norm_loo_loss_increase (bindings.cu:895-936, kernel forward.cu:667-738): per Gaussian, the increase of the absolute (squared
  * when `squared`) error summed over pixels and channels when it alone leaves the top-K lists; targets [C,H,W]. */
@@ -129,6 +154,11 @@ int igs_quantize_ste(int num_points, int channels, const float *xy, const float 
                      const float *pos_steps, float scale_step, float rot_step, const float *feat_steps, const float *feat_transform,
                      float *out_xy, float *out_scale, float *out_rot, float *out_feat, float *out_feat_t, float *q_xy, float *q_scale,
                      float *q_rot, float *q_feat, void *stream);
+
+/* Backward of the loss-space feature transform (autograd of `feat @ loss_transform.T`, model.py:963-964) through the straight-through
+ * quantizer: v_feat [N,C] = v_feat_t [N,C] T [C,C] + v_extra (may be NULL; e.g. the rate term's feature gradient). */
+int igs_feat_transform_bwd(int num_points, int channels, const float *v_feat_t, const float *feat_transform, const float *v_extra,
+                           float *v_feat, void *stream);
 
 /* rate_loss_forward (gsplat/gsplat/cuda/csrc/rate.cu:201-279; definition compress/rate.py:167-175 rate_bits): loss (device scalar)
  * = factor / max(l1_loss / l1_ratio, 1e-4) * (sum_{g,c} feat_coeffs[c] (sqrt(r^2 + 1/4) - 1/2) + sum_g rot_coeffs[g] (sqrt(t^2 + 1/4) - 1/2)),

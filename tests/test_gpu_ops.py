@@ -202,3 +202,35 @@ def test_pipeline_graph_matches_autograd(device):
     for p, mine in zip(params, (step.v_mean2d, step.v_scale, step.v_rot, step.v_colors)):
         assert_close_grad(mine, p.grad.reshape(mine.shape), what="pipeline grad")
     assert int(step.num_intersects.item()) <= step.capacity
+
+
+def test_pipeline_rate_step_matches_autograd(device):
+    """The 480p YUV step (quantizer, loss-space transform, L1, rate term), graph-captured, against the same step composed from the
+    autograd operators and ATen."""
+    z = py_fixture("cfg2_480p_yuv")
+    wl = workloads.get_workload("cfg2_480p_yuv")
+    inp = workloads.make_inputs(wl)
+    d = to_dev(inp, device)
+    model = workloads.RateModelTensors(z, device)
+    q = workloads.quant_settings(wl, device)
+    T = workloads.loss_transform_yuv().to(device)
+    rate = dict(model=model, inv_rot_step=float(z["inv_rot_step"]), factor=float(z["factor"]))
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["loss_target"], quant=q, loss_transform=T,
+                               rate=rate)
+    step.replay()
+    torch.cuda.synchronize()
+    raw = [d[k].clone().requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+    m, s_, r, f = ag.quantize_ste(*raw, q["pos_steps"], q["scale_step"], q["rot_step"], q["feat_steps"])
+    ft = f @ T.T
+    h, w = wl.height, wl.width
+    xys, radii, conics, hits = ag.project_gaussians_2d_scale_rot(m, s_, r, h, w, ops.tile_grid(h, w))
+    img = ag.rasterize_gaussians_sum_topk(xys, radii, conics, hits, ft, h, w, capacity=step.capacity)
+    l1 = ag.l1_loss(img.permute(2, 0, 1), d["loss_target"])
+    total = l1 + ag.rate_loss(raw[3], raw[2], l1, model, rate["inv_rot_step"], 1.0, rate["factor"])
+    total.backward()
+    assert float(step.loss) == float(l1)
+    assert abs(float(step.rate_loss) - float(total - l1)) <= 1e-5 * abs(float(total - l1))
+    assert_close_grad(step.v_mean2d, raw[0].grad, what="means")
+    assert_close_grad(step.v_scale, raw[1].grad, what="scales")
+    assert_close_grad(step.v_rot.view(-1) + step.rate_grad_rot, raw[2].grad.view(-1), what="rotations")
+    assert_close_grad(step.v_feat, raw[3].grad, what="features")

@@ -148,6 +148,35 @@ def test_tile_list_path_matches_pixel_path(name, device):
         assert_close_grad(a, b, what=nm)
 
 
+def test_tile_lists_beyond_16_bit_positions(device, ref_module):
+    """Tile lists of 70,000 entries (more than 16-bit positions address): the forward pass leaves those tiles' 16-bit lists empty and the
+    backward pass selects them again. Top-K lists equal the reference kernels' bit for bit (with 70,000 candidates nearly every pixel has
+    near-ties in alpha, so the IEEE-exp oracle is not the pin for the selection); gradients agree with the [H, W, 10] path and with the
+    reference kernels' backward over the same lists (the quotient rule cancels heavily here: ten weights near 1 per pixel)."""
+    wl, inp = make_case(40, 24, 70000, log_scale_mean=math.log(40.0), log_scale_std=0.1, seed=23)
+    dinp = to_dev(inp, device)
+    h, w = wl.height, wl.width
+    ours = ours_stages(dinp, h, w)
+    bins = np_(ours["tile_bins"])
+    assert (bins[:, 1] - bins[:, 0]).min() >= 65535
+    ref = reference_stages(ref_module, dinp, h, w, v_output=ours["v_output"], xys=ours["xys"], radii=ours["radii"], conics=ours["conics"],
+                           hits=ours["num_tiles_hit"])
+    np.testing.assert_array_equal(np_(ours["gaussian_ids_sorted"]), np_(ref["gaussian_ids_sorted"]))
+    np.testing.assert_array_equal(np_(ours["pixel_topk"]), np_(ref["pixel_topk"]))
+    assert_close_render(ours["image"], ref["image"], what="image")
+    tb = ops.tile_grid(h, w)
+    img, tile_topk = ops.nd_rasterize_forward_topk_norm_tiles(tb, (w, h, 1), ours["capacity"], ours["gaussian_ids_sorted"],
+                                                              ours["tile_bins"], ours["xys"], ours["conics"], dinp["features"])
+    assert torch.equal(img, ours["image"])
+    assert bool((tile_topk == -1).all())  # 0xFFFF everywhere: re-selected in the backward pass
+    v = ops.nd_rasterize_backward_topk_norm_tiles(h, w, ours["gaussian_ids_sorted"], ours["tile_bins"], ours["xys"], ours["conics"],
+                                                  dinp["features"], ours["v_output"], tile_topk)
+    for nm in ("v_xy", "v_conic", "v_colors"):
+        a = v[("v_xy", "v_conic", "v_colors").index(nm)]
+        assert_close_grad(a, ours[nm], what=nm)
+        assert_close_grad(a, ref[nm], what=nm + " vs reference")
+
+
 def test_capacity_drops_like_reference(device):
     """Fixed capacity below the intersection count: the excess (in Gaussian-major order) is dropped exactly as the reference does."""
     wl, inp, dinp = build_case("cfg1_256", device)
