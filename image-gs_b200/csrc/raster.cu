@@ -63,18 +63,20 @@ __device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, flo
     return 0.5f * (a * dx * dx + c * dy * dy) + b * dx * dy;
 }
 
-// The top-K selection of one pixel over its tile's list (range into ids_sorted), in list order: the slot rule of the reference (free slots
-// fill in order, then a Gaussian whose alpha exceeds the minimum replaces the first slot holding it) with a fast fill of the first ten
-// entries. The list is staged through s_geo / s_cc in chunks of kChunk entries, with CTA barriers: every thread of the CTA must call it.
-// pos[k]: list position of slot k's Gaussian (-1 empty); val[k]: its alpha.
+// The top-K selection of one pixel over its tile's list (range into ids_sorted), in list order, with the slot rule of the reference: free
+// slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it. The first ten
+// entries fill the slots with fixed indices when all of them are valid for the pixel (what the rule does while slots are free). The list
+// is staged through s_geo / s_cc in chunks of kChunk entries, with CTA barriers: every thread of the CTA must call it. The slots' list
+// positions are kept in shared memory (s_pos, [kTopK][kThreads] ints: one dynamic store per insertion instead of a select over ten
+// registers) and returned in pos[k] (-1 empty); val[k] is slot k's alpha.
 __device__ __forceinline__ void select_topk(const int2 range, const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
                                             const float *__restrict__ conics, const bool inside, const float px, const float py,
-                                            float4 *s_geo, float *s_cc, int (&pos)[kTopK], float (&val)[kTopK]) {
+                                            float4 *s_geo, float *s_cc, int *s_pos, int (&pos)[kTopK], float (&val)[kTopK]) {
     const int tid = threadIdx.x;
     const int len = range.y - range.x;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        pos[k] = -1;
+        s_pos[k * kThreads + tid] = -1;
         val[k] = 0.f;
     }
     int filled = 0, min_slot = 0;
@@ -93,8 +95,7 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         if (!inside) continue;
         int e = 0;
         if (base == 0 && count >= kTopK) {
-            // Fast fill: when none of the list's first ten entries is skipped for this pixel they take slots 0..9 in order, exactly
-            // what the insertion rule does while slots are free, so they are written with fixed slot indices; otherwise start over.
+            // fast fill: all of the first ten entries valid -> slots 0..9 in order; otherwise the general rule below
             bool all_valid = true;
 #pragma unroll
             for (int k = 0; k < kTopK; ++k) {
@@ -102,9 +103,10 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[k], px, py);
                 all_valid = all_valid && !(sigma < 0.f || isnan(sigma) || isinf(sigma));
                 val[k] = __expf(-sigma);
-                pos[k] = k;
             }
             if (all_valid) {
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) s_pos[k * kThreads + tid] = k;
                 filled = kTopK;
                 e = kTopK;
                 min_slot = 0;
@@ -118,28 +120,20 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 }
             } else {
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    pos[k] = -1;
-                    val[k] = 0.f;
-                }
+                for (int k = 0; k < kTopK; ++k) val[k] = 0.f;
             }
         }
-        for (; e < count; ++e) {
+        // filling: free slots take the valid entries in order
+        for (; e < count && filled < kTopK; ++e) {
             const float4 q = s_geo[e];
             const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
             if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
             const float alpha = __expf(-sigma);
-            if (!(alpha > min_val)) continue;
-            // free slots fill in order; once full, the first slot holding the minimum is replaced
-            const int slot = filled < kTopK ? filled : min_slot;
 #pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                if (k == slot) {
-                    pos[k] = base + e;
-                    val[k] = alpha;
-                }
-            }
-            filled += filled < kTopK;
+            for (int k = 0; k < kTopK; ++k)
+                if (k == filled) val[k] = alpha;
+            s_pos[filled * kThreads + tid] = base + e;
+            ++filled;
             if (filled == kTopK) {
                 min_slot = 0;
                 min_val = val[0];
@@ -152,7 +146,32 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 }
             }
         }
+        // full: an entry whose alpha exceeds the minimum replaces the first slot holding it; the new minimum (first slot on ties) is
+        // found in the same pass that writes the value
+        for (; e < count; ++e) {
+            const float4 q = s_geo[e];
+            const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
+            if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
+            const float alpha = __expf(-sigma);
+            if (!(alpha > min_val)) continue;
+            s_pos[min_slot * kThreads + tid] = base + e;
+            const int slot = min_slot;
+            min_slot = 0;
+            min_val = slot == 0 ? alpha : val[0];
+            val[0] = min_val;
+#pragma unroll
+            for (int k = 1; k < kTopK; ++k) {
+                const float v = k == slot ? alpha : val[k];
+                val[k] = v;
+                if (v < min_val) {
+                    min_slot = k;
+                    min_val = v;
+                }
+            }
+        }
     }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pos[k] = s_pos[k * kThreads + tid];
 }
 
 template <int C>
@@ -166,7 +185,7 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
     const int channels = C > 0 ? C : channels_rt;
     __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
     __shared__ float s_cc[kChunk];    // conic c
-    __shared__ int s_ids[kThreads * kTopK];
+    __shared__ int s_ids[kThreads * kTopK];  // the slots' list positions during the selection, then the IDs of [H, W, 10] lists
 
     const int tile = blockIdx.x;
     const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
@@ -177,7 +196,7 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
 
     int pos[kTopK];
     float val[kTopK];
-    select_topk(range, ids_sorted, xys, conics, inside, px, py, s_geo, s_cc, pos, val);
+    select_topk(range, ids_sorted, xys, conics, inside, px, py, s_geo, s_cc, s_ids, pos, val);
 
     // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
     int gid[kTopK];
@@ -217,6 +236,7 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
     }
     if (pixel_topk != nullptr) {
         // stage the IDs by thread, then write each tile row of 16 pixels x 10 IDs (80 int2) with consecutive threads
+        __syncthreads();  // every thread has read its positions from s_ids
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) s_ids[pc.tid * kTopK + k] = gid[k];
         __syncthreads();
@@ -444,8 +464,8 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 // One CTA of 256 threads (one per pixel) per tile; lists longer than kPairStage entries go through steps 2-3 in chunks of kPairStage:
 //   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
 //      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
-//   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory (per-pair shared atomics
-//      count each entry's pairs; a one-warp scan gives the segments; a returning atomic per pair takes a place in its segment);
+//   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory (warp-aggregated shared
+//      atomics count each entry's pairs; a one-warp scan gives the segments; one returning atomic per group of lanes takes places);
 //   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
 //      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v dx, v dy and w v_out (dx, dy from the Gaussian's center), then one
 //      reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the
@@ -464,7 +484,7 @@ struct PairSmem {
 };
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
+__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
                                                                     const int band_h, const int channels_rt,
                                                                     const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
                                                                     const float2 *__restrict__ xys, const float *__restrict__ conics,
@@ -502,8 +522,8 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
     } else {
         // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
         float val[kTopK];
-        select_topk(range, ids_sorted, xys, conics, inside, px, py, sm.geo, sm.cc, key, val);
-        __syncthreads();  // the staging arrays are reused below
+        select_topk(range, ids_sorted, xys, conics, inside, px, py, sm.geo, sm.cc, reinterpret_cast<int *>(&sm.vw[0][0]), key, val);
+        __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
     }
 
     // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
@@ -577,12 +597,16 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
             stage(chunk);
             __syncthreads();
         }
-        // 2. counting sort of this chunk's pairs by entry (shared-memory atomics; lanes adding to the same counter are merged by the
-        //    hardware)
+        // 2. counting sort of this chunk's pairs by entry: per slot, the lanes of a warp holding the same entry (neighbouring pixels
+        //    mostly keep the same Gaussians) are grouped with __match_any_sync and their leader adds the group's count, then takes the
+        //    group's places in the entry's segment with one returning atomic
+        unsigned peers[kTopK];
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             const int e = key[k] - chunk;
-            if (key[k] >= 0 && e >= 0 && e < n_entries) atomicAdd(&sm.start[e], 1);
+            const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
+            peers[k] = __match_any_sync(0xffffffffu, mine ? e : -1);
+            if (mine && (peers[k] & ((1u << lane) - 1u)) == 0u) atomicAdd(&sm.start[e], __popc(peers[k]));
         }
         __syncthreads();
         if (warp == 0) {
@@ -613,7 +637,12 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_pairs_kernel(const int ti
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             const int e = key[k] - chunk;
-            if (key[k] >= 0 && e >= 0 && e < n_entries) sm.pairs[atomicAdd(&sm.cursor[e], 1)] = (uint16_t)((k << 8) | tid);
+            const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
+            const unsigned below = peers[k] & ((1u << lane) - 1u);
+            int first = 0;
+            if (mine && below == 0u) first = atomicAdd(&sm.cursor[e], __popc(peers[k]));
+            first = __shfl_sync(0xffffffffu, first, __ffs(peers[k]) - 1);
+            if (mine) sm.pairs[first + __popc(below)] = (uint16_t)((k << 8) | tid);
         }
         __syncthreads();
 
