@@ -4,7 +4,7 @@ Benchmark of Image-GS's rasterization training step on B200: forward + L1 backwa
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3_1080p] [--impl ours|reference]
 
 A step (default workload: 1920x1080 RGB target, 20,000 Gaussians, 16x16 tiles, top-10) is projection -> prefix sum -> tile binning ->
-top-K forward -> L1 loss and gradient -> top-K backward -> projection backward, replayed from one CUDA graph with inputs resident in HBM
+top-K forward with the L1 loss and its gradient fused -> top-K backward -> projection backward, replayed from one CUDA graph with inputs resident in HBM
 (`value`). With N GPUs (torchrun, one process per GPU, NCCL for the barrier and the max over ranks) every rank renders its own independent
 image (weak scaling, no data-path communication). `e2e` runs the same step through the drop-in gsplat API with autograd, copying the
 Gaussian parameters host->device from pinned memory and reading the loss back every step. The L2 cache is flushed (a 256 MB write)
@@ -246,7 +246,8 @@ def run_ours(args, wl):
         stage_ms = {"forward": ms_per_step, "backward": 0.0}
     hbm_peak, peak_kind = peaks()
     p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
-    fwd_bytes = p * (4 * c + 4 * k) + num_isect * 4 + n * 4 * (5 + c)
+    # the forward kernel renders and takes the L1 loss: image write, [H, W, 10] lists of the operator surface, target read, gradient write
+    fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + num_isect * 4 + n * 4 * (5 + c)
     bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
     dominant = max(("forward", "backward"), key=lambda s: stage_ms[s])
     dom_ms = stage_ms[dominant]
@@ -378,7 +379,7 @@ def run_bands(args, wl):
         p = step.band_h * wl.width
         roofline = None
         if stage_ms:
-            fwd_bytes = p * (4 * c + 4 * k) + band_isect * 4 + n * 4 * (5 + c)
+            fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + band_isect * 4 + n * 4 * (5 + c)
             bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
             dominant = max(("forward", "backward"), key=lambda s_: stage_ms[s_])
             dom_bytes = fwd_bytes if dominant == "forward" else bwd_bytes

@@ -24,6 +24,7 @@
 //     increasing key order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving
 //     reduce-scatter, and adds them into per-tile shared accumulators or directly to the outputs.
 #include <algorithm>
+#include <cstddef>
 
 #include "igs_common.cuh"
 
@@ -174,13 +175,56 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
     for (int k = 0; k < kTopK; ++k) pos[k] = s_pos[k * kThreads + tid];
 }
 
+// The L1 loss of the rendered pixels fused into the forward pass (the training loss of model.py:1224-1227, ratio * F.l1_loss(image,
+// target), and its gradient sign(image - target) * ratio / numel): each CTA writes the gradient of its pixels and the sum of their
+// |image - target| (in a fixed order) to partials[tile]; l1_finish_kernel, launched next, adds the partials in tile order, so the loss
+// is deterministic. (Forming the loss in the last CTA to finish would make every CTA wait for a returning atomic before it exits: at
+// 8,160 tiles that costs more than the second launch.) target == nullptr: no loss.
+struct FusedL1 {
+    const float *target;  // [C, rows, W] like the image (the band's rows for a band)
+    float *v_output;      // gradient of the loss with respect to the image, same layout
+    float grad_value;     // ratio / numel (numel of the whole image)
+    float *partials;      // one per tile of the launch
+};
+
+__device__ __forceinline__ float l1_sign(float d) { return d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f); }
+
+// Sum of one value per thread over the CTA (blockDim.x threads, a multiple of 32) in a fixed order; the result is valid in thread 0.
+// scratch: blockDim.x / 32 floats.
+__device__ __forceinline__ float cta_sum(float v, float *scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // scratch may still be read by a previous use
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float total = 0.f;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total += scratch[w];
+    return total;
+}
+
+constexpr int kFinishThreads = 1024;
+
+// loss = ratio * (sum of the partials in tile order) / numel, one CTA
+__global__ void __launch_bounds__(kFinishThreads) l1_finish_kernel(const float *__restrict__ partials, const int count, const float ratio,
+                                                                   const float numel, float *__restrict__ loss) {
+    __shared__ float scratch[kFinishThreads / 32];
+    float sum = 0.f;
+#pragma unroll 8
+    for (int t = threadIdx.x; t < count; t += kFinishThreads) sum += __ldg(&partials[t]);
+    const float all = cta_sum(sum, scratch);
+    if (threadIdx.x == 0) *loss = ratio * (all / numel);
+}
+
 template <int C>
-__global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
+__global__ void __launch_bounds__(kThreads, (C == 1 || C == 3) ? 5 : 4) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
                                                               const int band_h, const int channels_rt,
                                                               const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
                                                               const float2 *__restrict__ xys, const float *__restrict__ conics,
                                                               const float *__restrict__ colors, float *__restrict__ out_img,
-                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk) {
+                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk,
+                                                              const FusedL1 l1) {
     constexpr int kMaxC = C > 0 ? C : kMaxChannels;
     const int channels = C > 0 ? C : channels_rt;
     __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
@@ -220,11 +264,25 @@ __global__ void __launch_bounds__(kThreads) raster_fwd_kernel(const int tiles_x,
             if (c < channels) pix[c] += __ldg(&f[c]) * vis;
     }
     const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
+    const int p = (pc.i - row_begin * kTile) * img_w + pc.j;
     if (inside) {
-        const int p = (pc.i - row_begin * kTile) * img_w + pc.j;
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)
             if (c < channels) out_img[(size_t)c * num_pixels + p] = pix[c];
+    }
+    if (l1.target != nullptr) {
+        float acc = 0.f;
+        if (inside) {
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) {
+                if (c >= channels) continue;
+                const float d = pix[c] - __ldcs(&l1.target[(size_t)c * num_pixels + p]);
+                acc += fabsf(d);
+                __stcs(&l1.v_output[(size_t)c * num_pixels + p], l1_sign(d) * l1.grad_value);
+            }
+        }
+        const float total = cta_sum(acc, reinterpret_cast<float *>(s_cc));
+        if (threadIdx.x == 0) l1.partials[tile] = total;
     }
 
     if (tile_topk != nullptr) {
@@ -697,15 +755,15 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_ke
 template <int C>
 cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids, const int2 *bins,
                        const float2 *xys, const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk,
-                       cudaStream_t s) {
+                       const FusedL1 &l1, cudaStream_t s) {
     raster_fwd_kernel<C><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys, conics, colors, out,
-                                                     pixel_topk, tile_topk);
+                                                     pixel_topk, tile_topk, l1);
     return cudaGetLastError();
 }
 
 int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, const int32_t *ids_sorted,
                const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, float *out_img, int32_t *pixel_topk,
-               uint16_t *tile_topk, void *stream, const char *who) {
+               uint16_t *tile_topk, void *stream, const char *who, FusedL1 l1 = FusedL1{}) {
     IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && img_h >= 0 && img_w >= 0, "%s: negative size", who);
     IGS_REQUIRE(channels >= 0 && channels <= kMaxChannels, "%s: at most %d channels (got %d)", who, kMaxChannels, channels);
     IGS_REQUIRE(tiles_x == igs::ceil_div(img_w, kTile) && tiles_y == igs::ceil_div(img_h, kTile),
@@ -724,10 +782,10 @@ int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, in
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
     cudaError_t err;
     switch (channels) {
-        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s); break;
-        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, s);
+        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
+        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
+        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
+        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s);
     }
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;
@@ -857,6 +915,45 @@ int igs_raster_fwd_topk_tiles_band(int tiles_x, int tiles_y, int img_height, int
     IGS_REQUIRE(tile_topk != nullptr || row_begin == row_end, "igs_raster_fwd_topk_tiles_band: null tile_topk");
     return raster_fwd(tiles_x, tiles_y, img_height, img_width, row_begin, row_end, channels, gaussian_ids_sorted, tile_bins, xys, conics,
                       colors, out_band, nullptr, tile_topk, stream, "igs_raster_fwd_topk_tiles_band");
+}
+
+size_t igs_raster_l1_workspace(int num_tiles) { return sizeof(float) * (size_t)(num_tiles > 0 ? num_tiles : 1); }
+
+int igs_raster_fwd_topk_tiles_l1_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                                      int max_list_len, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                                      const float *conics, const float *colors, const float *target, float ratio, float *out_img,
+                                      uint16_t *tile_topk, float *loss, float *v_output, void *workspace, size_t workspace_bytes,
+                                      void *stream) {
+    const char *who = "igs_raster_fwd_topk_tiles_l1";
+    IGS_REQUIRE(max_list_len >= 0, "%s: negative max_list_len", who);
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y && tiles_x >= 0, "%s: bad tile rows", who);
+    const int tiles = tiles_x * (row_end - row_begin);
+    if (tiles == 0) return IGS_OK;
+    IGS_REQUIRE(channels >= 1, "%s: the loss needs at least one channel", who);
+    IGS_REQUIRE(tile_topk && target && loss && v_output && workspace, "%s: null pointer", who);
+    IGS_REQUIRE(workspace_bytes >= igs_raster_l1_workspace(tiles), "%s: workspace too small (%zu bytes, need %zu)", who, workspace_bytes,
+                igs_raster_l1_workspace(tiles));
+    IGS_REQUIRE(igs::aligned(workspace, 16), "%s: workspace must be 16-byte aligned", who);
+    const float numel = (float)((int64_t)channels * img_height * img_width);
+    FusedL1 l1;
+    l1.target = target;
+    l1.v_output = v_output;
+    l1.grad_value = ratio / numel;
+    l1.partials = static_cast<float *>(workspace);
+    const int status = raster_fwd(tiles_x, tiles_y, img_height, img_width, row_begin, row_end, channels, gaussian_ids_sorted, tile_bins, xys,
+                                  conics, colors, out_img, nullptr, tile_topk, stream, who, l1);
+    if (status != IGS_OK) return status;
+    l1_finish_kernel<<<1, kFinishThreads, 0, igs::as_stream(stream)>>>(l1.partials, tiles, ratio, numel, loss);
+    return igs::check_launch(who);
+}
+
+int igs_raster_fwd_topk_tiles_l1(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
+                                 const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                                 const float *colors, const float *target, float ratio, float *out_img, uint16_t *tile_topk, float *loss,
+                                 float *v_output, void *workspace, size_t workspace_bytes, void *stream) {
+    return igs_raster_fwd_topk_tiles_l1_band(tiles_x, tiles_y, img_height, img_width, 0, tiles_y, channels, max_list_len,
+                                             gaussian_ids_sorted, tile_bins, xys, conics, colors, target, ratio, out_img, tile_topk, loss,
+                                             v_output, workspace, workspace_bytes, stream);
 }
 
 int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin, int row_end, int channels, int num_points,

@@ -98,9 +98,9 @@ class BandStep:
         self.cum_ws = torch.empty(self.cum_ws_bytes, device=dev, dtype=torch.uint8)
         self.image = torch.empty(nc, self.band_h, img_w, device=dev, dtype=f32)
         self.v_image = torch.empty_like(self.image)
-        # the band's loss with the whole image's normalisation: ratio * sum|d| / (C H W)
-        self.l1_scale = float(l1_ratio) * self.image.numel() / float(nc * img_h * img_w) if self.image.numel() else 0.0
-        self.l1_ws_bytes = self.lib.igs_l1_workspace(max(1, self.image.numel()))
+        # the band's loss is its share of the whole image's, ratio * sum over the band |d| / (C H W), computed by the forward kernel
+        self.l1_ratio = float(l1_ratio)
+        self.l1_ws_bytes = self.lib.igs_raster_l1_workspace(max(1, self.num_tiles))
         self.l1_ws = torch.zeros(self.l1_ws_bytes, device=dev, dtype=torch.uint8)
         # one buffer for the all-reduce: the partial gradients, then the partial loss
         self.reduced = torch.empty(n * (5 + nc) + 1, device=dev, dtype=f32)
@@ -145,16 +145,14 @@ class BandStep:
                                                      self.sort_ws_bytes, self._stream()), "bin")
 
     def _forward(self):
-        _lib.check(self.lib.igs_raster_fwd_topk_tiles_band(self.tb[0], self.tb[1], self.h, self.w, self.r0, self.r1, self.c, self.max_list,
-                                                           ptr(self.ids), ptr(self.bins), ptr(self.xys), ptr(self.conics),
-                                                           ptr(self.features), ptr(self.image), ptr(self.topk), self._stream()), "forward")
-
-    def _loss(self):
-        if self.image.numel() == 0:
+        if self.num_tiles == 0:
             self.loss.zero_()
             return
-        _lib.check(self.lib.igs_l1_loss(self.image.numel(), ptr(self.image), ptr(self.target), self.l1_scale, ptr(self.loss),
-                                        ptr(self.v_image), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "l1")
+        _lib.check(self.lib.igs_raster_fwd_topk_tiles_l1_band(self.tb[0], self.tb[1], self.h, self.w, self.r0, self.r1, self.c, self.max_list,
+                                                              ptr(self.ids), ptr(self.bins), ptr(self.xys), ptr(self.conics),
+                                                              ptr(self.features), ptr(self.target), self.l1_ratio, ptr(self.image),
+                                                              ptr(self.topk), ptr(self.loss), ptr(self.v_image), ptr(self.l1_ws),
+                                                              self.l1_ws_bytes, self._stream()), "forward")
 
     def _backward(self):
         _lib.check(self.lib.igs_raster_bwd_topk_tiles_band(self.h, self.w, self.r0, self.r1, self.c, self.n, ptr(self.ids), ptr(self.bins),
@@ -167,8 +165,8 @@ class BandStep:
                                             ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                             ptr(self.v_rot), self._stream()), "project_backward")
 
-    LOCAL = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward")
-    KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1}
+    LOCAL = ("_project", "_cumsum", "_bin", "_forward", "_backward")
+    KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_forward": 2, "_backward": 1, "_project_backward": 1}
 
     def all_reduce(self):
         if self.group is not None:

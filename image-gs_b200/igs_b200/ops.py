@@ -156,6 +156,31 @@ def nd_rasterize_forward_topk_norm_tiles(tile_bounds, img_size, max_list_len, ga
     return out_img, tile_topk
 
 
+def nd_rasterize_forward_topk_norm_tiles_l1(tile_bounds, img_size, max_list_len, gaussian_ids_sorted, tile_bins, xys, conics, colors,
+                                            target, ratio=1.0):
+    """The training-step forward with the L1 loss fused: (out_img [C,H,W], tile_topk, loss = ratio * mean|out_img - target|,
+    v_output = its gradient with respect to out_img); target [C,H,W] float32."""
+    h, w = _check_raster_geometry(tile_bounds, (TILE, TILE, 1), img_size)
+    channels = colors.size(1)
+    _check_input(target, "target", torch.float32)
+    if tuple(target.shape) != (channels, h, w):
+        raise RuntimeError(f"target must be [{channels}, {h}, {w}]")
+    dev = xys.device
+    num_tiles = int(tile_bounds[0]) * int(tile_bounds[1])
+    lib = _lib.load()
+    out_img = torch.empty(channels, h, w, device=dev, dtype=torch.float32)
+    v_output = torch.empty_like(out_img)
+    loss = torch.empty((), device=dev, dtype=torch.float32)
+    tile_topk = torch.empty(num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+    ws_bytes = lib.igs_raster_l1_workspace(num_tiles)
+    ws = torch.zeros(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib_call("igs_raster_fwd_topk_tiles_l1", int(tile_bounds[0]), int(tile_bounds[1]), h, w, channels, int(max_list_len),
+                  ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors), ptr(target), float(ratio), ptr(out_img),
+                  ptr(tile_topk), ptr(loss), ptr(v_output), ptr(ws), ws_bytes, stream_of(dev))
+    return out_img, tile_topk, loss, v_output
+
+
 def nd_rasterize_backward_topk_norm(img_height, img_width, BLOCK_H, BLOCK_W, xys, conics, colors, v_output, pixel_topk):
     """-> v_xy [N,2], v_conic [N,3], v_colors [N,C] (bindings.cu:444-502); v_output channel-planar [C,H,W]."""
     for t, n in ((xys, "xys"), (conics, "conics"), (colors, "colors"), (v_output, "v_output")):

@@ -62,7 +62,7 @@ class RasterStep:
         self.image = torch.empty(nc, self.h, self.w, device=dev, dtype=f32)
         self.v_image = torch.empty_like(self.image)
         self.loss = torch.empty((), device=dev, dtype=f32)
-        self.l1_ws_bytes = self.lib.igs_l1_workspace(self.image.numel())
+        self.l1_ws_bytes = self.lib.igs_raster_l1_workspace(self.num_tiles)
         self.l1_ws = torch.zeros(self.l1_ws_bytes, device=dev, dtype=torch.uint8)
         self.grads = torch.empty(n * (5 + nc), device=dev, dtype=f32)
         self.v_xy, self.v_conic, self.v_colors = self.grads[:2 * n].view(n, 2), self.grads[2 * n:5 * n].view(n, 3), self.grads[5 * n:].view(n, nc)
@@ -152,13 +152,11 @@ class RasterStep:
                     "bin")
 
     def _forward(self):
-        self._check(self.lib.igs_raster_fwd_topk_tiles(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
-                                                       ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.image),
-                                                       ptr(self.topk), self._stream()), "forward")
-
-    def _loss(self):
-        self._check(self.lib.igs_l1_loss(self.image.numel(), ptr(self.image), ptr(self.target), self.l1_ratio, ptr(self.loss),
-                                         ptr(self.v_image), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "l1")
+        """Render, with the L1 loss and its gradient with respect to the image computed in the same kernel."""
+        self._check(self.lib.igs_raster_fwd_topk_tiles_l1(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
+                                                          ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features),
+                                                          ptr(self.target), self.l1_ratio, ptr(self.image), ptr(self.topk), ptr(self.loss),
+                                                          ptr(self.v_image), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "forward")
 
     def _backward(self):
         self._check(self.lib.igs_raster_bwd_topk_tiles(self.h, self.w, self.c, self.n, ptr(self.ids), ptr(self.bins), ptr(self.xys),
@@ -170,9 +168,9 @@ class RasterStep:
                                              ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                              ptr(self.v_rot), self._stream()), "project_backward")
 
-    BASE_STAGES = ("_project", "_cumsum", "_bin", "_forward", "_loss", "_backward", "_project_backward")
+    BASE_STAGES = ("_project", "_cumsum", "_bin", "_forward", "_backward", "_project_backward")
     # kernels each stage launches (memsets excluded)
-    KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 1, "_loss": 1, "_backward": 1, "_project_backward": 1,
+    KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 2, "_backward": 1, "_project_backward": 1,
                "_rate_term": 2, "_feature_grads": 1}
 
     @property

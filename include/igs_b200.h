@@ -94,6 +94,17 @@ int igs_raster_fwd_topk_tiles(int tiles_x, int tiles_y, int img_height, int img_
                               const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
                               const float *colors, float *out_img, uint16_t *tile_topk, void *stream);
 
+/* igs_raster_fwd_topk_tiles with the training loss fused into its epilogue (model.py:1224-1227: loss = ratio * F.l1_loss(image,
+ * target), whose gradient is sign(image - target) * ratio / numel): also reads target [C,H,W] and writes *loss and v_output [C,H,W], the
+ * gradient the backward pass takes, so the image is not read again by a separate loss pass. The loss is summed per tile, then in tile
+ * order by a second one-CTA kernel (deterministic). workspace: igs_raster_l1_workspace(tiles_x * tiles_y) bytes (per-tile partial sums),
+ * 16-byte aligned, no initialization needed. No counterpart in the reference, which calls F.l1_loss on the returned image. */
+size_t igs_raster_l1_workspace(int num_tiles);
+int igs_raster_fwd_topk_tiles_l1(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int max_list_len,
+                                 const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                                 const float *colors, const float *target, float ratio, float *out_img, uint16_t *tile_topk, float *loss,
+                                 float *v_output, void *workspace, size_t workspace_bytes, void *stream);
+
 /* nd_rasterize_backward_topk_norm (bindings.cu:444-502, kernel backward.cu:187-335): v_output [C,H,W]; outputs v_xy [N,2],
  * v_conic [N,3], v_colors [N,C] are zeroed and accumulated (float atomics: the last bits vary run to run). */
 int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
@@ -123,6 +134,15 @@ int igs_sort_intersects_band(int num_points, int capacity, const float *xys, con
 int igs_raster_fwd_topk_tiles_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
                                    int max_list_len, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
                                    const float *conics, const float *colors, float *out_band, uint16_t *tile_topk, void *stream);
+
+/* igs_raster_fwd_topk_tiles_l1 for a band: target and v_output hold the band's rows [C, band_h, W]; *loss is the band's share of the
+ * whole image's loss (ratio * sum over the band of |image - target| / (C H W)), so the bands' losses sum to the image's; workspace
+ * igs_raster_l1_workspace(tiles_x * (row_end - row_begin)). */
+int igs_raster_fwd_topk_tiles_l1_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                                      int max_list_len, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                                      const float *conics, const float *colors, const float *target, float ratio, float *out_img,
+                                      uint16_t *tile_topk, float *loss, float *v_output, void *workspace, size_t workspace_bytes,
+                                      void *stream);
 
 /* igs_raster_bwd_topk_tiles for a band: v_output_band [C, band_h, W]; the gradients are this band's share (sum them over the bands) */
 int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin, int row_end, int channels, int num_points,

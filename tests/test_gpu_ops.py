@@ -49,6 +49,32 @@ def test_l1_loss_matches_torch(numel_shape, device):
     assert float(loss2) == float(loss)
 
 
+@pytest.mark.parametrize("case", [dict(h=88, w=120, n=300, seed=11), dict(h=64, w=80, n=200, c=9, seed=13), dict(h=50, w=70, n=150, c=1, seed=12)])
+def test_forward_with_fused_l1_matches_separate_loss(case, device):
+    """The forward kernel's fused L1 loss: render and lists identical to the plain forward, gradient identical to the L1 kernel's (and to
+    torch's), loss within float summation order of torch's, repeatable."""
+    kw = dict(case)
+    h, w = kw.pop("h"), kw.pop("w")
+    wl, inp = make_case(h, w, **kw)
+    d = to_dev(inp, device)
+    ours = ours_stages(d, h, w)
+    tb = ops.tile_grid(h, w)
+    bound = min(len(inp["means"]), ours["capacity"])
+    args = (tb, (w, h, 1), bound, ours["gaussian_ids_sorted"], ours["tile_bins"], ours["xys"], ours["conics"], d["features"])
+    img, topk = ops.nd_rasterize_forward_topk_norm_tiles(*args)
+    img2, topk2, loss, v_out = ops.nd_rasterize_forward_topk_norm_tiles_l1(*args, d["target"], ratio=0.8)
+    assert torch.equal(img, img2) and torch.equal(topk, topk2)
+    loss_ref, grad_ref = ops.l1_loss_and_grad(img, d["target"], ratio=0.8)
+    torch.testing.assert_close(v_out, grad_ref, rtol=0, atol=0)
+    x = img.clone().requires_grad_(True)
+    ref = 0.8 * F.l1_loss(x, d["target"])
+    ref.backward()
+    torch.testing.assert_close(v_out, x.grad, rtol=0, atol=0)
+    assert abs(float(loss) - float(ref)) <= 2e-6 * abs(float(ref))
+    _, _, loss2, _ = ops.nd_rasterize_forward_topk_norm_tiles_l1(*args, d["target"], ratio=0.8)
+    assert float(loss2) == float(loss)
+
+
 @pytest.mark.parametrize("name", PY_CASES)
 def test_quantize_ste_symbols_bit_exact(name, device):
     z = py_fixture(name)
@@ -198,7 +224,8 @@ def test_pipeline_graph_matches_autograd(device):
     loss = ag.l1_loss(img.permute(2, 0, 1), d["target"])
     loss.backward()
     assert torch.equal(step.image, img.permute(2, 0, 1).detach())
-    assert float(step.loss) == float(loss)
+    # the step's loss is summed per tile inside the forward kernel, the autograd one by the separate L1 kernel: summation order only
+    assert abs(float(step.loss) - float(loss)) <= 2e-6 * float(loss)
     for p, mine in zip(params, (step.v_mean2d, step.v_scale, step.v_rot, step.v_colors)):
         assert_close_grad(mine, p.grad.reshape(mine.shape), what="pipeline grad")
     assert int(step.num_intersects.item()) <= step.capacity
@@ -228,7 +255,7 @@ def test_pipeline_rate_step_matches_autograd(device):
     l1 = ag.l1_loss(img.permute(2, 0, 1), d["loss_target"])
     total = l1 + ag.rate_loss(raw[3], raw[2], l1, model, rate["inv_rot_step"], 1.0, rate["factor"])
     total.backward()
-    assert float(step.loss) == float(l1)
+    assert abs(float(step.loss) - float(l1)) <= 2e-6 * float(l1)
     assert abs(float(step.rate_loss) - float(total - l1)) <= 1e-5 * abs(float(total - l1))
     assert_close_grad(step.v_mean2d, raw[0].grad, what="means")
     assert_close_grad(step.v_scale, raw[1].grad, what="scales")
