@@ -239,6 +239,27 @@ def topk_norm_loo_loss_increase(img_height, img_width, xys, conics, colors, pixe
     return out
 
 
+def topk_feature_weights_fixed(img_height, img_width, xys, conics, pixel_topk, eps=EPS):
+    """Per-Gaussian sum over pixels of the squared normalized top-K weight as int64 fixed point with 40 fractional bits: the integer sums
+    of compress.quantization.feature_weights (quantization.py:218-230) over model._iter_topk_weights (model.py:1404-1421)."""
+    for t, n in ((xys, "xys"), (conics, "conics")):
+        _check_input(t, n, torch.float32)
+    _check_input(pixel_topk, "pixel_topk", torch.int32)
+    if pixel_topk.numel() != img_height * img_width * TOP_K:
+        raise RuntimeError("pixel_topk must be [H, W, TOP_K]")
+    dev = xys.device
+    out = torch.empty(xys.size(0), device=dev, dtype=torch.int64)
+    with torch.cuda.device(dev):
+        _lib_call("igs_feature_weights", int(img_height), int(img_width), xys.size(0), ptr(xys), ptr(conics), ptr(pixel_topk), float(eps),
+                  ptr(out), stream_of(dev))
+    return out
+
+
+def topk_feature_weights(img_height, img_width, xys, conics, pixel_topk, eps=EPS):
+    """compress.quantization.feature_weights(model._iter_topk_weights(...)) -> [N] float64."""
+    return topk_feature_weights_fixed(img_height, img_width, xys, conics, pixel_topk, eps).to(torch.float64) / 2.0**40
+
+
 # ---- losses, quantization, rate term -------------------------------------------------------------------------------------------------
 
 def l1_loss_and_grad(image: torch.Tensor, target: torch.Tensor, ratio: float = 1.0, workspace: Optional[torch.Tensor] = None):

@@ -156,6 +156,14 @@ int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_p
                           const float *colors, const int32_t *pixel_topk, const float *targets, int squared, float eps,
                           float *loss_increase, void *stream);
 
+/* feature_weights over _iter_topk_weights (compress/quantization.py:218-230, model.py:1404-1421): per Gaussian, the sum over pixels of
+ * its squared normalized top-K weight as 64-bit fixed point with 40 fractional bits (fixed_point [N] int64, zeroed here; the weights are
+ * fixed_point / 2^40). The slot weights exp(-sigma) are recomputed with the reference's IEEE float32 arithmetic from pixel_topk [H,W,10]
+ * (of igs_raster_fwd_topk), normalized in double with eps (1e-4 in the reference) and rounded half to even; integer atomics make the sums
+ * independent of the order of the additions. */
+int igs_feature_weights(int img_height, int img_width, int num_points, const float *xys, const float *conics, const int32_t *pixel_topk,
+                        double eps, int64_t *fixed_point, void *stream);
+
 /* ---- training-step losses and quantization -------------------------------------------------------------------------------------- */
 
 /* L1 loss and its gradient in one pass (model.py:1224-1227, F.l1_loss): loss = ratio * mean|image - target| (device scalar) and

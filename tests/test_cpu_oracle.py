@@ -165,3 +165,14 @@ def test_oracle_rate_matches_reference_python(name):
     assert abs(loss.item() - float(z["loss"])) <= 1e-6 * abs(float(z["loss"]))
     assert_close_grad(feat.grad.numpy(), z["grad_feat"], what="grad_feat")
     assert_close_grad(rot.grad.numpy(), z["grad_rot"], what="grad_rot")
+
+
+@pytest.mark.parametrize("name", ["weights_ragged_120x88", "weights_big_64x64", "weights_cfg1_256"])
+def test_feature_weights_oracle_matches_reference_fixture(name):
+    """oracle/weights.py restates feature_weights over _iter_topk_weights; on the CPU it reproduces the reference's own code bit for bit."""
+    from oracle import weights as ow
+
+    z = np.load(os.path.join(GOLDEN, f"py_{name}.npz"))
+    h, w, n = (int(v) for v in z["meta"])
+    got = ow.feature_weights(torch.from_numpy(z["xys"]), torch.from_numpy(z["conics"]), torch.from_numpy(z["pixel_topk"]), h, w)
+    np.testing.assert_array_equal(got.numpy(), z["weights"])

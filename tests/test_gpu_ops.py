@@ -75,6 +75,24 @@ def test_forward_with_fused_l1_matches_separate_loss(case, device):
     assert float(loss2) == float(loss)
 
 
+@pytest.mark.parametrize("name", ["weights_ragged_120x88", "weights_big_64x64", "weights_cfg1_256"])
+def test_feature_weights_vs_reference(name, device):
+    """igs_feature_weights against the reference's feature_weights over _iter_topk_weights: bit-identical int64 fixed-point sums to its
+    code run by ATen on the GPU (oracle/weights.py, the reference's operations), and the reference's own CPU results (fixture) within the
+    float32 exp differences of the two machines."""
+    from oracle import weights as ow
+
+    z = py_fixture(name)
+    h, w, n = (int(v) for v in z["meta"])
+    xys, conics, topk = (torch.from_numpy(z[k]).to(device) for k in ("xys", "conics", "pixel_topk"))
+    fixed = ops.topk_feature_weights_fixed(h, w, xys, conics, topk)
+    ref = ow.feature_weights_fixed(ow.iter_topk_weights(xys, conics, topk, h, w), n, 1e-4, device)
+    assert torch.equal(fixed, ref)
+    got = fixed.double() / 2.0 ** 40
+    np.testing.assert_allclose(got.cpu().numpy(), z["weights"], rtol=1e-6, atol=1e-9)
+    torch.testing.assert_close(ops.topk_feature_weights(h, w, xys, conics, topk), got, rtol=0, atol=0)
+
+
 @pytest.mark.parametrize("name", PY_CASES)
 def test_quantize_ste_symbols_bit_exact(name, device):
     z = py_fixture(name)
