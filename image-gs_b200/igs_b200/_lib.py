@@ -40,6 +40,8 @@ SIGNATURES = {
     "igs_raster_bwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
     "igs_loo_loss_increase": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, c_int, c_float, P, P]),
     "igs_feature_weights": (c_int, [c_int, c_int, c_int, P, P, P, c_double, P, P]),
+    "igs_neighbors_workspace": (c_size_t, [c_int]),
+    "igs_nearest_neighbors": (c_int, [c_int, P, c_int, P, P, P, c_size_t, P]),
     "igs_l1_workspace": (c_size_t, [c_int64]),
     "igs_l1_loss": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
     "igs_quantize_ste": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_float, P, P, P, P, P, P, P, P, P, P, P, P]),

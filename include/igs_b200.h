@@ -164,6 +164,15 @@ int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_p
 int igs_feature_weights(int img_height, int img_width, int num_points, const float *xys, const float *conics, const int32_t *pixel_topk,
                         double eps, int64_t *fixed_point, void *stream);
 
+/* nearest_neighbors / causal_neighbors of the rate model's preparation (compress/csrc/prediction.cpp:69-166, called by
+ * compress/rate.py:56-66 bitstream_neighbors): for integer positions [P, 2] (int64, 16-byte aligned), the 8 nearest earlier Gaussians
+ * (causal != 0: indices below the Gaussian's own, i.e. earlier in bitstream order) or the 8 nearest other Gaussians, ordered by squared
+ * distance and then by index; neighbors [P, 8] int64 and, unless null, dist2 [P, 8] int64, -1 where there are fewer. workspace:
+ * igs_neighbors_workspace(P) bytes, 16-byte aligned. Nothing is read back to the host. */
+size_t igs_neighbors_workspace(int num_points);
+int igs_nearest_neighbors(int num_points, const int64_t *positions, int causal, int64_t *neighbors, int64_t *dist2, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
 /* ---- training-step losses and quantization -------------------------------------------------------------------------------------- */
 
 /* L1 loss and its gradient in one pass (model.py:1224-1227, F.l1_loss): loss = ratio * mean|image - target| (device scalar) and

@@ -176,3 +176,15 @@ def test_feature_weights_oracle_matches_reference_fixture(name):
     h, w, n = (int(v) for v in z["meta"])
     got = ow.feature_weights(torch.from_numpy(z["xys"]), torch.from_numpy(z["conics"]), torch.from_numpy(z["pixel_topk"]), h, w)
     np.testing.assert_array_equal(got.numpy(), z["weights"])
+
+
+@pytest.mark.parametrize("name", ["cfg2_480p_yuv", "rgb_subgreen_320x200"])
+def test_neighbors_oracle_matches_reference_fixture(name):
+    """oracle/neighbors.py (brute force, bitstream order restated) reproduces the neighbours the reference's rate_model computed with its
+    C++ search (stored clamped to 0, with zero weights where there is no neighbour)."""
+    from oracle import neighbors as on
+
+    z = np.load(os.path.join(GOLDEN, f"py_{name}.npz"))
+    got = on.bitstream_neighbors(z["q_xy"].astype(np.int64), 3)
+    np.testing.assert_array_equal(got.clip(min=0), z["neighbors"])
+    np.testing.assert_array_equal(got >= 0, z["weights"] > 0)

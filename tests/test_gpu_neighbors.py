@@ -1,0 +1,53 @@
+"""
+The GPU neighbour search of the rate model's preparation (igs_nearest_neighbors; compress/csrc/prediction.cpp:69-166 and
+compress/rate.py:56-66): exact equality with the brute-force oracle on random, duplicate-heavy, degenerate and wide-range positions, causal
+and not, and with the neighbours the reference's own rate_model computed for the 480p YUV workload and a small RGB one.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from igs_b200 import neighbors as nb
+from oracle import neighbors as on
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def cases():
+    rng = np.random.default_rng(5)
+    yield "tiny", rng.integers(0, 50, size=(5, 2))
+    yield "nine", rng.integers(0, 50, size=(9, 2))
+    yield "random", rng.integers(0, 4000, size=(3000, 2))
+    yield "duplicates", rng.integers(0, 12, size=(1500, 2))  # many equal positions and distances: ties by index
+    yield "line", np.stack([rng.integers(0, 10 ** 6, size=1200), np.full(1200, 7)], axis=1)
+    yield "wide", rng.integers(-2 ** 29, 2 ** 29, size=(1000, 2))  # squared distances up to 2^61: no int64 overflow
+    yield "clustered", np.concatenate([rng.integers(0, 20, size=(800, 2)), rng.integers(10 ** 5, 10 ** 5 + 3000, size=(800, 2))])
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_nearest_neighbors_match_brute_force(causal, device):
+    for name, pos in cases():
+        pos = pos.astype(np.int64)
+        ids, d2 = nb.nearest_neighbors(torch.from_numpy(pos).to(device), causal=causal, return_dist2=True)
+        ref_ids, ref_d2 = on.nearest_neighbors(pos, causal=causal)
+        np.testing.assert_array_equal(ids.cpu().numpy(), ref_ids, err_msg=name)
+        np.testing.assert_array_equal(d2.cpu().numpy(), ref_d2, err_msg=name)
+
+
+@pytest.mark.parametrize("name", ["cfg2_480p_yuv", "rgb_subgreen_320x200"])
+def test_bitstream_neighbors_match_reference(name, device):
+    z = np.load(os.path.join(GOLDEN, f"py_{name}.npz"))
+    q = z["q_xy"].astype(np.int64)
+    got = nb.bitstream_neighbors(q, 3, device=device)
+    np.testing.assert_array_equal(got, on.bitstream_neighbors(q, 3))
+    np.testing.assert_array_equal(got.clip(min=0), z["neighbors"])  # the reference's rate model stores them clamped to 0
+    np.testing.assert_array_equal(got >= 0, z["weights"] > 0)
+
+
+def test_empty_and_single(device):
+    assert nb.bitstream_neighbors(np.zeros((0, 2), np.int64), device=device).shape == (0, 8)
+    one = nb.nearest_neighbors(torch.zeros(1, 2, dtype=torch.int64, device=device))
+    assert bool((one == -1).all())
