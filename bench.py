@@ -503,6 +503,71 @@ def run_e2e(args, wl, inp, device, capacity, world):
                    (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward"}
 
 
+def run_aux(args):
+    """The rows around the step, each timed on the GPU and beside the reference's CPU code where it has one: the neighbour search of the
+    rate model's preparation at 80,000 Gaussians (vs the reference's C++ causal_neighbors, built from source into oracle/_ref, on all host
+    threads), the per-Gaussian feature weights and the leave-one-out loss increase at 1080p/20k. One JSON line."""
+    from igs_b200 import neighbors as nb
+    from igs_b200 import ops
+
+    device = torch.device("cuda", 0)
+    out = {"aux": True, "unit": "ms"}
+
+    def gpu_ms(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    # neighbour search: the 2160p/80k workload's positions quantized with the default 1/8-pixel step, in bitstream order
+    wl4 = workloads.get_workload("cfg4_2160p")
+    inp4 = workloads.make_inputs(wl4)
+    q = torch.round(inp4["means"].double() * torch.tensor([wl4.width, wl4.height], dtype=torch.float64) / 0.125).long().numpy()
+    order = nb.bitstream_order(q, 3)
+    sq = torch.from_numpy(np.ascontiguousarray(q[order])).to(device)
+    ms = gpu_ms(lambda: nb.causal_neighbors(sq))
+    entry = {"gaussians": len(q), "gpu_ms": ms}
+    sys.path.insert(0, ROOT)
+    try:
+        from oracle import build_ref
+
+        ref = build_ref.load_prediction()
+        host = np.ascontiguousarray(q[order])
+        ref.causal_neighbors(host)
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            ref_out = ref.causal_neighbors(host)
+        entry["reference_cpu_ms"] = 1e3 * (time.perf_counter() - t0) / reps
+        entry["reference_cpu_threads"] = len(os.sched_getaffinity(0))
+        entry["identical"] = bool(np.array_equal(nb.causal_neighbors(sq).cpu().numpy(), ref_out))
+    except ImportError as e:
+        entry["reference_cpu_ms"] = None
+        entry["reference_note"] = str(e)
+    out["causal_neighbors"] = entry
+
+    # feature weights and leave-one-out at 1080p/20k from the step's top-K lists
+    wl = workloads.get_workload("cfg3_1080p")
+    inp = workloads.make_inputs(wl)
+    d = {k: v.to(device) for k, v in inp.items()}
+    h, w, n = wl.height, wl.width, wl.num_gaussians
+    tb = ops.tile_grid(h, w)
+    xys, radii, conics, hits = ops.project_gaussians_2d_scale_rot_forward(n, d["means"], d["scales"], d["rotations"], h, w, tb)
+    cum, total = ops.cumulative_intersects(hits)
+    ids, bins = ops.sort_intersects_by_tile(n, int(total.item()), xys, radii, cum, tb)
+    _, topk = ops.nd_rasterize_forward_topk_norm(tb, (16, 16, 1), (w, h, 1), ids, bins, xys, conics, d["features"])
+    out["feature_weights_1080p"] = {"gpu_ms": gpu_ms(lambda: ops.topk_feature_weights_fixed(h, w, xys, conics, topk))}
+    out["loo_1080p"] = {"gpu_ms": gpu_ms(lambda: ops.topk_norm_loo_loss_increase(h, w, xys, conics, d["features"], topk, d["target"],
+                                                                                  False, 1e-4))}
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -513,9 +578,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
     ap.add_argument("--no-stages", action="store_true", help="skip the per-stage timing")
+    ap.add_argument("--aux", action="store_true", help="time the rows around the step (neighbour search, feature weights, LOO) instead")
     args = ap.parse_args()
     wl = workloads.get_workload(args.workload)
-    if args.impl == "reference":
+    if args.aux:
+        run_aux(args)
+    elif args.impl == "reference":
         run_reference(args, wl)
     elif wl.sharding == "bands":
         run_bands(args, wl)

@@ -62,6 +62,52 @@ def load_module():
     return module
 
 
+PREDICTION = "igs_prediction"
+
+
+def prediction_module_path():
+    """Path of the reference's C++ prediction module built into oracle/_ref, or None."""
+    hits = glob.glob(os.path.join(OUT, PREDICTION + "*.so"))
+    return hits[0] if hits else None
+
+
+def build_prediction(reference_root="/root/reference"):
+    """Compiles the reference's compress/csrc/prediction.cpp (its neighbour search and predictor; a pybind11 module) where it lies, with
+    g++ (-O3 -ffp-contract=off -pthread, and the source hash define that compress/common.py:13-27 checks), into oracle/_ref/. It is the
+    CPU baseline and checker of the GPU neighbour search."""
+    import hashlib
+    import subprocess
+    import sysconfig
+
+    from torch.utils.cpp_extension import include_paths
+
+    src = os.path.join(reference_root, "compress", "csrc", "prediction.cpp")
+    if not os.path.exists(src):
+        raise FileNotFoundError(src)
+    os.makedirs(OUT, exist_ok=True)
+    with open(src, "rb") as f:
+        digest = hashlib.sha256(f.read()).hexdigest()[:16]
+    out = os.path.join(OUT, PREDICTION + sysconfig.get_config_var("EXT_SUFFIX"))
+    gxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
+    subprocess.run([gxx, "-O3", "-std=c++17", "-shared", "-fPIC", "-pthread", "-ffp-contract=off", f'-DSOURCE_HASH="{digest}"', "-I",
+                    include_paths()[0], "-I", sysconfig.get_paths()["include"], src, "-o", out], check=True)
+    return out
+
+
+def load_prediction():
+    """Import the built prediction module (raises ImportError when it has not been built)."""
+    path = prediction_module_path()
+    if path is None:
+        raise ImportError("reference prediction module not built (python oracle/build_ref.py)")
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(PREDICTION, path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
 if __name__ == "__main__":
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     print(build(root, verbose=True))
+    print(build_prediction(root))
