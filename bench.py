@@ -183,6 +183,11 @@ def time_graph(graph, reps, flush):
 
 RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the raster kernels, from one ncu capture of this workload
+# (`ncu --set full --clock-control none -k regex:"raster_(fwd|bwd_pairs)" -s 3 -c 3 python bench.py --steps 2 --warmup 3 --no-cpu
+# --no-e2e --no-stages`, caches flushed before each pass); None where no capture was taken
+NCU_TRAFFIC = {"cfg3_1080p": {"forward": 26.44e6 + 41.33e6, "backward": 68.46e6 + 1.19e6}}
+
 
 def step_options(wl, device):
     """Extra stages of the workload's step: for the 480p YUV configuration the straight-through quantizer, the luma-weighted loss
@@ -277,7 +282,8 @@ def run_ours(args, wl):
             "gaussian_pixel_evals_per_step": evals, "gaussian_pixel_evals_per_s": evals * value,
             "stages_ms": stage_ms,
             "roofline": {"bound": "hbm", "kernel": f"raster_{dominant}", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": dom_bytes,
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC.get(wl.name, {}).get(dominant), "algorithmic_bytes": dom_bytes,
                          "kernel_ms": dom_ms},
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
