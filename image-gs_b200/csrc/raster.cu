@@ -522,8 +522,9 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 // One CTA of 256 threads (one per pixel) per tile; lists longer than kPairStage entries go through steps 2-3 in chunks of kPairStage:
 //   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
 //      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
-//   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory (warp-aggregated shared
-//      atomics count each entry's pairs; a one-warp scan gives the segments; one returning atomic per group of lanes takes places);
+//   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory without atomics: per slot the
+//      lanes of a warp holding the same entry are grouped (__match_any_sync) and the group's leader counts it in the warp's own row of
+//      counters; a CTA-wide scan turns the (warp, entry) counts into places; each pair is stored at its place;
 //   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
 //      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v dx, v dy and w v_out (dx, dy from the Gaussian's center), then one
 //      reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the
@@ -537,8 +538,9 @@ struct PairSmem {
     float vout[kMaxC][kThreads];       // dL/dout per channel and pixel
     float2 pxy[kThreads];              // pixel coordinates
     uint16_t pairs[kPairs];            // (slot << 8) | pixel, grouped by entry
-    int start[kPairStage + 1];         // pairs per entry, then segment starts
-    int cursor[kPairStage];
+    int start[kPairStage + 1];         // segment starts
+    uint16_t wcnt[kThreads / 32][kPairStage];  // pairs per (warp, entry), then each warp's first place in the entry's segment
+    int wsum[kThreads / 32];
 };
 
 template <int C, int NV>
@@ -596,7 +598,6 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_ke
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c)
                 if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
-            sm.start[e] = 0;
         }
     };
     stage(0);
@@ -605,45 +606,56 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_ke
     for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
     __syncthreads();
 
-    // 1. per-pixel gradients with respect to sigma and the colour weights
-    float d[kTopK];
+    // 1. per-pixel gradients with respect to sigma and the colour weights (the reference's algebra, backward.cu:219-265, its divisions
+    //    by denom written as products with two reciprocals computed once)
+    float d[kTopK], s[kTopK];
     float denom = (float)igs::kNormEps;
+    if (len <= kPairStage) {
+        // the whole list is staged: every slot reads shared memory
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        d[k] = 0.f;
-        if (key[k] < 0) continue;
-        float gx, gy, a, b, c;
-        if (key[k] < kPairStage) {
-            const float4 q = sm.geo[key[k]];
-            gx = q.x, gy = q.y, a = q.z, b = q.w, c = sm.cc[key[k]];
-        } else {
-            const int g = __ldg(&ids_sorted[range.x + key[k]]);
-            const float2 xy = __ldg(&xys[g]);
-            gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
+        for (int k = 0; k < kTopK; ++k) {
+            d[k] = 0.f, s[k] = 0.f;
+            if (key[k] < 0) continue;
+            const int e = key[k];
+            const float4 q = sm.geo[e];
+            d[k] = __expf(-gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[e], px, py));
+            denom += d[k];
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += sm.col[e * kMaxC + c] * v_out[c];
         }
-        d[k] = __expf(-gaussian_sigma(gx, gy, a, b, c, px, py));
-        denom += d[k];
+    } else {
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            d[k] = 0.f, s[k] = 0.f;
+            if (key[k] < 0) continue;
+            float gx, gy, a, b, c;
+            if (key[k] < kPairStage) {
+                const float4 q = sm.geo[key[k]];
+                gx = q.x, gy = q.y, a = q.z, b = q.w, c = sm.cc[key[k]];
+#pragma unroll
+                for (int ch = 0; ch < kMaxC; ++ch)
+                    if (ch < channels) s[k] += sm.col[key[k] * kMaxC + ch] * v_out[ch];
+            } else {
+                const int g = __ldg(&ids_sorted[range.x + key[k]]);
+                const float2 xy = __ldg(&xys[g]);
+                gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
+#pragma unroll
+                for (int ch = 0; ch < kMaxC; ++ch)
+                    if (ch < channels) s[k] += __ldg(&colors[(size_t)g * channels + ch]) * v_out[ch];
+            }
+            d[k] = __expf(-gaussian_sigma(gx, gy, a, b, c, px, py));
+            denom += d[k];
+        }
     }
-    float s[kTopK];
+    // fast-math division is a product with the approximate reciprocal, so the reference's x / denom and x / (denom * denom) are these
+    // products, in its order of operations
+    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
     float shared = 0.f;
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        s[k] = 0.f;
-        if (key[k] < 0) continue;
-        if (key[k] < kPairStage) {
+    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
 #pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
-        } else {
-            const int g = __ldg(&ids_sorted[range.x + key[k]]);
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += __ldg(&colors[(size_t)g * channels + c]) * v_out[c];
-        }
-        shared += -d[k] / (denom * denom) * s[k];
-    }
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] / denom + shared), d[k] / denom);
+    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
 
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
@@ -655,52 +667,65 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_ke
             stage(chunk);
             __syncthreads();
         }
-        // 2. counting sort of this chunk's pairs by entry: per slot, the lanes of a warp holding the same entry (neighbouring pixels
-        //    mostly keep the same Gaussians) are grouped with __match_any_sync and their leader adds the group's count, then takes the
-        //    group's places in the entry's segment with one returning atomic
-        unsigned peers[kTopK];
+        // 2. counting sort of this chunk's pairs by entry without atomics: per slot, the lanes of a warp holding the same entry are grouped
+        //    with __match_any_sync; each warp counts its pairs per entry in its own row of wcnt (a group's leader adds the group, so no
+        //    two lanes write one counter), which also gives each pair its place among the warp's pairs of that entry (< 32: 5 bits)
+        for (int e = lane; e < n_entries; e += 32) sm.wcnt[warp][e] = 0;
+        __syncwarp();
+        unsigned off_lo = 0u, off_hi = 0u;  // the pairs' places, 5 bits per slot
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             const int e = key[k] - chunk;
             const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
-            peers[k] = __match_any_sync(0xffffffffu, mine ? e : -1);
-            if (mine && (peers[k] & ((1u << lane) - 1u)) == 0u) atomicAdd(&sm.start[e], __popc(peers[k]));
+            const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
+            const unsigned below = peers & ((1u << lane) - 1u);
+            const int base = mine ? (int)sm.wcnt[warp][e] : 0;
+            __syncwarp();
+            if (mine && below == 0u) sm.wcnt[warp][e] = (uint16_t)(base + __popc(peers));
+            __syncwarp();
+            const unsigned off = (unsigned)(base + __popc(below)) & 31u;
+            if (k < 6) off_lo |= off << (5 * k);
+            else off_hi |= off << (5 * (k - 6));
         }
         __syncthreads();
-        if (warp == 0) {
-            constexpr int kPer = kPairStage / 32;  // exclusive scan of the counts by one warp
-            int local[kPer], run = 0;
+        {
+            // per entry (one thread each): the warps' counts into running places, the entry's total into a CTA-wide exclusive scan
+            const int e = tid;
+            int total = 0;
+            if (e < n_entries) {
 #pragma unroll
-            for (int j = 0; j < kPer; ++j) {
-                const int e = lane * kPer + j;
-                local[j] = e < n_entries ? sm.start[e] : 0;
-                run += local[j];
+                for (int w = 0; w < kThreads / 32; ++w) {
+                    const int c = sm.wcnt[w][e];
+                    sm.wcnt[w][e] = (uint16_t)total;
+                    total += c;
+                }
             }
-            int incl = run;
+            int incl = total;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int n = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= o) incl += n;
             }
-            int start = incl - run;
+            if (lane == 31) sm.wsum[warp] = incl;
+            __syncthreads();
+            int before = 0;
 #pragma unroll
-            for (int j = 0; j < kPer; ++j) {
-                const int e = lane * kPer + j;
-                if (e < n_entries) sm.start[e] = sm.cursor[e] = start;
-                start += local[j];
+            for (int w = 0; w < kThreads / 32; ++w) before += w < warp ? sm.wsum[w] : 0;
+            const int start = before + incl - total;
+            if (e < n_entries) {
+                sm.start[e] = start;
+#pragma unroll
+                for (int w = 0; w < kThreads / 32; ++w) sm.wcnt[w][e] = (uint16_t)(sm.wcnt[w][e] + start);
             }
-            if (lane == 31) sm.start[n_entries] = incl;
+            if (e == n_entries - 1) sm.start[n_entries] = start + total;
         }
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             const int e = key[k] - chunk;
             const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
-            const unsigned below = peers[k] & ((1u << lane) - 1u);
-            int first = 0;
-            if (mine && below == 0u) first = atomicAdd(&sm.cursor[e], __popc(peers[k]));
-            first = __shfl_sync(0xffffffffu, first, __ffs(peers[k]) - 1);
-            if (mine) sm.pairs[first + __popc(below)] = (uint16_t)((k << 8) | tid);
+            const unsigned off = (k < 6 ? off_lo >> (5 * k) : off_hi >> (5 * (k - 6))) & 31u;
+            if (mine) sm.pairs[sm.wcnt[warp][e] + off] = (uint16_t)((k << 8) | tid);
         }
         __syncthreads();
 
