@@ -4,11 +4,13 @@ Benchmark of Image-GS's rasterization training step on B200: forward + L1 backwa
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3_1080p] [--impl ours|reference]
 
 A step (default workload: 1920x1080 RGB target, 20,000 Gaussians, 16x16 tiles, top-10) is projection -> prefix sum -> tile binning ->
-top-K forward with the L1 loss and its gradient fused -> top-K backward -> projection backward, replayed from one CUDA graph with inputs resident in HBM
-(`value`). With N GPUs (torchrun, one process per GPU, NCCL for the barrier and the max over ranks) every rank renders its own independent
-image (weak scaling, no data-path communication). `e2e` runs the same step through the drop-in gsplat API with autograd, copying the
-Gaussian parameters host->device from pinned memory and reading the loss back every step. The L2 cache is flushed (a 256 MB write)
-between timed steps, outside the per-step CUDA-event intervals.
+top-K forward with the L1 loss and its gradient fused -> top-K backward -> projection backward, replayed from one CUDA graph with inputs
+resident in HBM (`value`). With N GPUs (torchrun, one process per GPU, NCCL for the barrier and the max over ranks) every rank renders its
+own independent image (weak scaling, no data-path communication); `--workload cfg4_2160p` splits one image into tile-row bands (strong
+scaling, one NCCL all-reduce per step). `e2e` runs the same step through the C ABI with host buffers: the Gaussian parameters copied
+host->device from pinned memory and the loss read back every step; `e2e_autograd` does the same through the drop-in gsplat API with
+autograd and F.l1_loss (what Image-GS's model.py calls). The L2 cache is flushed (a 256 MB write) between timed steps, outside the
+per-step CUDA-event intervals.
 
 `--impl reference` times the CPU restatement of the reference's path (the reference has no CPU implementation of its own) on the host's
 cores, on rank 0 only.
@@ -261,8 +263,12 @@ def run_ours(args, wl):
     step_bytes = (p * (8 * c + 8 * k) + n * 4 * (5 + 7 + 2 * (5 + c) + (5 + c) + 5 + 5) + num_isect * 4 * 5 + wl.num_tiles * 16)
     loss_bytes = 12 * c * p
 
-    # end to end through the drop-in gsplat API (autograd), host -> device parameters and device -> host loss every step
-    e2e = run_e2e(args, wl, inp, device, step.capacity, world) if not args.no_e2e else None
+    # end to end with host buffers: through the C ABI (the step as above, parameters copied in and the loss read back every step), and
+    # through the drop-in gsplat API with autograd (what model.py calls)
+    e2e = e2e_autograd = None
+    if not args.no_e2e:
+        e2e = run_step_e2e(args, step, step.raw, inp, device, world, "step")
+        e2e_autograd = run_e2e(args, wl, inp, device, step.capacity, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -288,7 +294,8 @@ def run_ours(args, wl):
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
-            "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps, "clocks": clk,
+            "e2e": e2e, "e2e_autograd": e2e_autograd, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
+            "clocks": clk,
         }
         print(json.dumps(out))
     if world > 1:
@@ -371,7 +378,7 @@ def run_bands(args, wl):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_band_e2e(args, step, inp, device, world)
+        e2e = run_step_e2e(args, step, (step.means, step.scales, step.rotations, step.features), inp, device, world, "bands")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -414,16 +421,17 @@ def run_bands(args, wl):
         torch.distributed.destroy_process_group()
 
 
-def run_band_e2e(args, step, inp, device, world):
-    """The band step through the C ABI with host buffers: the Gaussian parameters copied host -> device from pinned memory and the loss
-    read back every step."""
-    host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
-    dev = {"means": step.means, "scales": step.scales, "rotations": step.rotations, "features": step.features}
+def run_step_e2e(args, step, dev_params, inp, device, world, api):
+    """The step through the C ABI with host buffers: the Gaussian parameters copied host -> device from pinned memory into the step's
+    input tensors and the loss read back to the host every step."""
+    keys = ("means", "scales", "rotations", "features")
+    host = [inp[k].pin_memory() for k in keys]
+    dev = list(dev_params)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
     def one():
-        for k in dev:
-            dev[k].copy_(host[k], non_blocking=True)
+        for d, h in zip(dev, host):
+            d.copy_(h, non_blocking=True)
         step.replay()
         loss_host.copy_(step.loss, non_blocking=True)
 
@@ -443,9 +451,11 @@ def run_band_e2e(args, step, inp, device, world):
     t = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    return {"value": args.steps / (float(t.item()) / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
-            "d2h_bytes_per_step": 4 * world, "api": "igs_b200.bands.BandStep over the C ABI (host parameters copied in every step)"}
+    h2d = sum(v.numel() * v.element_size() for v in host)
+    return {"value": world * args.steps / (float(t.item()) / 1e3) if api != "bands" else args.steps / (float(t.item()) / 1e3),
+            "unit": "steps/s", "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world,
+            "api": ("igs_b200.bands.BandStep" if api == "bands" else "igs_b200.pipeline.RasterStep") +
+                   " over the C ABI (host parameters copied in and the loss read back every step)"}
 
 
 def run_e2e(args, wl, inp, device, capacity, world):

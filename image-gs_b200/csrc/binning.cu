@@ -125,6 +125,7 @@ __device__ __forceinline__ unsigned block_sum_u32(unsigned v, unsigned *scratch)
 }
 
 __global__ void __launch_bounds__(kCumThreads) cumsum_partials_kernel(const int n, const int *__restrict__ in, unsigned *__restrict__ partials) {
+    igs::wait_for_predecessor();
     __shared__ unsigned scratch[kCumThreads / 32];
     unsigned v[kCumItems], run = 0u;
     load_items(in, n, blockIdx.x * kCumBlock + threadIdx.x * kCumItems, v);
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kCumThreads) cumsum_partials_kernel(const int 
 
 __global__ void __launch_bounds__(kCumThreads) cumsum_scan_kernel(const int n, const int *__restrict__ in, const unsigned *__restrict__ partials,
                                                                   int *__restrict__ out, int *__restrict__ total_out) {
+    igs::wait_for_predecessor();
     __shared__ unsigned scratch[kCumThreads / 32];
     unsigned before = 0u;
     for (int b = threadIdx.x; b < (int)blockIdx.x; b += kCumThreads) before += partials[b];
@@ -197,6 +199,7 @@ __global__ void __launch_bounds__(256) count_kernel(const int n, const int capac
                                                     const unsigned tiles_y, const unsigned row_begin, const unsigned row_end,
                                                     int *__restrict__ tile_count, int2 *__restrict__ slot_tile_rank,
                                                     int *__restrict__ slot_gaussian) {
+    igs::wait_for_predecessor();
     const int slots = min(__ldg(&cum[n - 1]), capacity);
     const unsigned num_tiles = tiles_x * (row_end - row_begin);
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < slots; idx += gridDim.x * blockDim.x) {
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(256) count_kernel(const int n, const int capac
 __global__ void __launch_bounds__(256) band_hits_kernel(const int n, const float2 *__restrict__ xys, const int *__restrict__ radii,
                                                         const unsigned tiles_x, const unsigned tiles_y, const unsigned row_begin,
                                                         const unsigned row_end, int *__restrict__ hits) {
+    igs::wait_for_predecessor();
     const int g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n) return;
     int count = 0;
@@ -239,6 +243,7 @@ __global__ void __launch_bounds__(256) band_hits_kernel(const int n, const float
 // Exclusive scan of the tile counts by one CTA: tile_bins[t] = (start, end), (0, 0) for empty tiles
 __global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const int num_tiles, const int *__restrict__ tile_count,
                                                                  int2 *__restrict__ tile_bins, int *__restrict__ total_out) {
+    igs::wait_for_predecessor();
     const unsigned total = chunked_scan(tile_count, num_tiles, [&](int t, unsigned excl, unsigned v) {
         tile_bins[t] = v > 0u ? make_int2((int)excl, (int)(excl + v)) : make_int2(0, 0);
     });
@@ -249,6 +254,7 @@ __global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const int num_t
 __global__ void __launch_bounds__(256) place_kernel(const int n, const int capacity, const int *__restrict__ cum, const unsigned num_tiles,
                                                     const int2 *__restrict__ tile_bins, const int2 *__restrict__ slot_tile_rank,
                                                     const int *__restrict__ slot_gaussian, int *__restrict__ unsorted) {
+    igs::wait_for_predecessor();
     const int slots = min(__ldg(&cum[n - 1]), capacity);
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < slots; idx += gridDim.x * blockDim.x) {
         const int2 tr = slot_tile_rank[idx];
@@ -265,6 +271,7 @@ constexpr int kOrderStage = 1024;  // entries per warp staged in shared memory
 __global__ void __launch_bounds__(kOrderWarps * 32) order_kernel(const int num_tiles, const int capacity, const int2 *__restrict__ tile_bins,
                                                                  const int *__restrict__ unsorted, const int *__restrict__ total_in,
                                                                  int *__restrict__ sorted) {
+    igs::wait_for_predecessor();
     __shared__ int stage[kOrderWarps][kOrderStage];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tile = blockIdx.x * kOrderWarps + warp;
@@ -330,8 +337,8 @@ int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int3
     IGS_REQUIRE(workspace_bytes >= igs_cumsum_workspace(n), "igs_cumsum: workspace too small");
     const int blocks = igs::ceil_div(n, kCumBlock);
     unsigned *partials = static_cast<unsigned *>(workspace);
-    cumsum_partials_kernel<<<blocks, kCumThreads, 0, s>>>(n, num_tiles_hit, partials);
-    cumsum_scan_kernel<<<blocks, kCumThreads, 0, s>>>(n, num_tiles_hit, partials, cum_tiles_hit, total);
+    igs::launch(cumsum_partials_kernel, blocks, kCumThreads, 0, s, n, num_tiles_hit, partials);
+    igs::launch(cumsum_scan_kernel, blocks, kCumThreads, 0, s, n, num_tiles_hit, partials, cum_tiles_hit, total);
     return igs::check_launch("igs_cumsum");
 }
 
@@ -374,18 +381,17 @@ static int sort_band(int num_points, int capacity, const float *xys, const int32
     // slots are bounded by the capacity; a grid-stride loop over them reads the true count on the device
     const int slot_blocks = std::min(igs::ceil_div(capacity, 256), 148 * 16);
     if (num_points > 0) {
-        count_kernel<<<slot_blocks, 256, 0, s>>>(num_points, capacity, reinterpret_cast<const float2 *>(xys), radii, cum_tiles_hit,
-                                                 (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin, (unsigned)row_end, tile_count,
-                                                 slot_tile_rank, slot_gaussian);
+        igs::launch(count_kernel, slot_blocks, 256, 0, s, num_points, capacity, reinterpret_cast<const float2 *>(xys), radii,
+                    cum_tiles_hit, (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin, (unsigned)row_end, tile_count, slot_tile_rank,
+                    slot_gaussian);
     }
-    tile_scan_kernel<<<1, kScanThreads, 0, s>>>(num_tiles, tile_count, reinterpret_cast<int2 *>(tile_bins), total);
+    igs::launch(tile_scan_kernel, 1, kScanThreads, 0, s, num_tiles, tile_count, reinterpret_cast<int2 *>(tile_bins), total);
     if (num_points > 0) {
-        place_kernel<<<slot_blocks, 256, 0, s>>>(num_points, capacity, cum_tiles_hit, (unsigned)num_tiles,
-                                                 reinterpret_cast<const int2 *>(tile_bins), slot_tile_rank, slot_gaussian, unsorted);
+        igs::launch(place_kernel, slot_blocks, 256, 0, s, num_points, capacity, cum_tiles_hit, (unsigned)num_tiles,
+                    reinterpret_cast<const int2 *>(tile_bins), slot_tile_rank, slot_gaussian, unsorted);
     }
-    order_kernel<<<igs::ceil_div(num_tiles, kOrderWarps), kOrderWarps * 32, 0, s>>>(num_tiles, capacity,
-                                                                                    reinterpret_cast<const int2 *>(tile_bins), unsorted,
-                                                                                    total, gaussian_ids_sorted);
+    igs::launch(order_kernel, igs::ceil_div(num_tiles, kOrderWarps), kOrderWarps * 32, 0, s, num_tiles, capacity,
+                reinterpret_cast<const int2 *>(tile_bins), unsorted, total, gaussian_ids_sorted);
     return igs::check_launch(who);
 }
 
@@ -404,9 +410,9 @@ int igs_band_tiles_hit(int num_points, const float *xys, const int32_t *radii, i
     if (num_points == 0) return IGS_OK;
     IGS_REQUIRE(xys && radii && num_tiles_hit, "igs_band_tiles_hit: null pointer");
     IGS_REQUIRE(igs::aligned(xys, 8), "igs_band_tiles_hit: xys must be 8-byte aligned");
-    band_hits_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
-        num_points, reinterpret_cast<const float2 *>(xys), radii, (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin,
-        (unsigned)row_end, num_tiles_hit);
+    igs::launch(band_hits_kernel, igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream), num_points,
+                reinterpret_cast<const float2 *>(xys), radii, (unsigned)tiles_x, (unsigned)tiles_y, (unsigned)row_begin, (unsigned)row_end,
+                num_tiles_hit);
     return igs::check_launch("igs_band_tiles_hit");
 }
 

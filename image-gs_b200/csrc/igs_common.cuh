@@ -7,6 +7,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/igs_b200.h"
 
 namespace igs {
@@ -29,6 +31,27 @@ inline cudaStream_t as_stream(void *stream) { return reinterpret_cast<cudaStream
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 inline bool aligned(const void *p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// Programmatic dependent launch (sm_90 and later): the kernels of the training step are launched with programmatic stream serialization,
+// so a kernel is scheduled while its predecessor on the stream drains instead of after it; each of them begins with
+// wait_for_predecessor() (griddepcontrol.wait: returns once the predecessor has completed and its writes are visible; a no-op for a
+// kernel launched without the attribute) before it reads or writes memory.
+__device__ __forceinline__ void wait_for_predecessor() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace igs
 

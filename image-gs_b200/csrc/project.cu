@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(256) project_fwd_kernel(const int n, const flo
                                                           const float *__restrict__ rotations, const float img_w, const float img_h,
                                                           const unsigned tiles_x, const unsigned tiles_y, float2 *__restrict__ xys,
                                                           int *__restrict__ radii, float *__restrict__ conics, int *__restrict__ hits) {
+    igs::wait_for_predecessor();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float2 mean = __ldg(&means[i]);
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) project_bwd_kernel(const int n, const flo
                                                           const float *__restrict__ v_conic, float *__restrict__ v_cov2d,
                                                           float2 *__restrict__ v_mean2d, float2 *__restrict__ v_scale,
                                                           float *__restrict__ v_rot) {
+    igs::wait_for_predecessor();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     if (__ldg(&radii[i]) <= 0) {
@@ -159,9 +161,9 @@ int igs_project_fwd(int num_points, const float *means2d, const float *scales2d,
     IGS_REQUIRE(means2d && scales2d && rotation && xys && radii && conics && num_tiles_hit, "igs_project_fwd: null pointer");
     IGS_REQUIRE(igs::aligned(means2d, 8) && igs::aligned(scales2d, 8) && igs::aligned(xys, 8),
                 "igs_project_fwd: means2d, scales2d and xys must be 8-byte aligned [N, 2] float32");
-    project_fwd_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
-        num_points, reinterpret_cast<const float2 *>(means2d), reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width,
-        (float)img_height, (unsigned)tiles_x, (unsigned)tiles_y, reinterpret_cast<float2 *>(xys), radii, conics, num_tiles_hit);
+    igs::launch(project_fwd_kernel, igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream), num_points,
+                reinterpret_cast<const float2 *>(means2d), reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width,
+                (float)img_height, (unsigned)tiles_x, (unsigned)tiles_y, reinterpret_cast<float2 *>(xys), radii, conics, num_tiles_hit);
     return igs::check_launch("igs_project_fwd");
 }
 
@@ -174,10 +176,10 @@ int igs_project_bwd(int num_points, const float *scales2d, const float *rotation
                 "igs_project_bwd: null pointer");
     IGS_REQUIRE(igs::aligned(scales2d, 8) && igs::aligned(v_xy, 8) && igs::aligned(v_mean2d, 8) && igs::aligned(v_scale, 8),
                 "igs_project_bwd: [N, 2] tensors must be 8-byte aligned");
-    project_bwd_kernel<<<igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream)>>>(
-        num_points, reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width, (float)img_height, radii, conics,
-        reinterpret_cast<const float2 *>(v_xy), v_conic, v_cov2d, reinterpret_cast<float2 *>(v_mean2d), reinterpret_cast<float2 *>(v_scale),
-        v_rot);
+    igs::launch(project_bwd_kernel, igs::ceil_div(num_points, 256), 256, 0, igs::as_stream(stream), num_points,
+                reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width, (float)img_height, radii, conics,
+                reinterpret_cast<const float2 *>(v_xy), v_conic, v_cov2d, reinterpret_cast<float2 *>(v_mean2d),
+                reinterpret_cast<float2 *>(v_scale), v_rot);
     return igs::check_launch("igs_project_bwd");
 }
 

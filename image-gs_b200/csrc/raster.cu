@@ -209,6 +209,7 @@ constexpr int kFinishThreads = 1024;
 // loss = ratio * (sum of the partials in tile order) / numel, one CTA
 __global__ void __launch_bounds__(kFinishThreads) l1_finish_kernel(const float *__restrict__ partials, const int count, const float ratio,
                                                                    const float numel, float *__restrict__ loss) {
+    igs::wait_for_predecessor();
     __shared__ float scratch[kFinishThreads / 32];
     float sum = 0.f;
 #pragma unroll 8
@@ -218,13 +219,12 @@ __global__ void __launch_bounds__(kFinishThreads) l1_finish_kernel(const float *
 }
 
 template <int C>
-__global__ void __launch_bounds__(kThreads, (C == 1 || C == 3) ? 5 : 4) raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
-                                                              const int band_h, const int channels_rt,
-                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
-                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
-                                                              const float *__restrict__ colors, float *__restrict__ out_img,
-                                                              int *__restrict__ pixel_topk, uint16_t *__restrict__ tile_topk,
-                                                              const FusedL1 l1) {
+__global__ void __launch_bounds__(kThreads, (C == 1 || C == 3) ? 5 : 4)
+    raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h, const int channels_rt,
+        const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
+        const float *__restrict__ conics, const float *__restrict__ colors, float *__restrict__ out_img, int *__restrict__ pixel_topk,
+        uint16_t *__restrict__ tile_topk, const FusedL1 l1) {
+    igs::wait_for_predecessor();
     constexpr int kMaxC = C > 0 ? C : kMaxChannels;
     const int channels = C > 0 ? C : channels_rt;
     __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
@@ -544,13 +544,12 @@ struct PairSmem {
 };
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin,
-                                                                    const int band_h, const int channels_rt,
-                                                                    const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
-                                                                    const float2 *__restrict__ xys, const float *__restrict__ conics,
-                                                                    const float *__restrict__ colors, const float *__restrict__ v_output,
-                                                                    const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy,
-                                                                    float *__restrict__ v_conic, float *__restrict__ v_colors) {
+__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3)
+    raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h,
+        const int channels_rt, const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
+        const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
+        const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
+    igs::wait_for_predecessor();
     constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
     static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry sums and the channels");
     const int channels = C > 0 ? C : channels_rt;
@@ -781,9 +780,8 @@ template <int C>
 cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids, const int2 *bins,
                        const float2 *xys, const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk,
                        const FusedL1 &l1, cudaStream_t s) {
-    raster_fwd_kernel<C><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys, conics, colors, out,
-                                                     pixel_topk, tile_topk, l1);
-    return cudaGetLastError();
+    return igs::launch(raster_fwd_kernel<C>, tiles, kThreads, 0, s, tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys,
+                       conics, colors, out, pixel_topk, tile_topk, l1);
 }
 
 int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, const int32_t *ids_sorted,
@@ -805,13 +803,10 @@ int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, in
     cudaStream_t s = igs::as_stream(stream);
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
-    cudaError_t err;
-    switch (channels) {
-        case 1: err = launch_fwd<1>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
-        case 3: err = launch_fwd<3>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
-        case 9: err = launch_fwd<9>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s); break;
-        default: err = launch_fwd<0>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img, pixel_topk, tile_topk, l1, s);
-    }
+    // channel counts with a specialised kernel, else the generic one
+    const auto launch = channels == 1 ? launch_fwd<1> : channels == 3 ? launch_fwd<3> : channels == 9 ? launch_fwd<9> : launch_fwd<0>;
+    const cudaError_t err = launch(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, out_img,
+                                   pixel_topk, tile_topk, l1, s);
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;
 }
@@ -834,9 +829,8 @@ cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int r
     // more than the 48 KB default of dynamic shared memory (set on every call: cheap, and correct for whichever device is current)
     cudaError_t err = cudaFuncSetAttribute(raster_bwd_pairs_kernel<C, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (err != cudaSuccess) return err;
-    raster_bwd_pairs_kernel<C, NV><<<tiles, kThreads, bytes, s>>>(tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys, conics,
-                                                                  colors, v_output, tile_topk, v_xy, v_conic, v_colors);
-    return cudaGetLastError();
+    return igs::launch(raster_bwd_pairs_kernel<C, NV>, tiles, kThreads, bytes, s, tiles_x, img_h, img_w, row_begin, band_h, channels, ids,
+                       bins, xys, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors);
 }
 
 int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, int num_points, const int32_t *ids_sorted,
@@ -848,11 +842,18 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
     cudaStream_t s = igs::as_stream(stream);
     if (num_points > 0) {
         IGS_REQUIRE(v_xy && v_conic && (v_colors || channels == 0), "%s: null gradient pointer", who);
-        // the kernel accumulates with atomics
-        if (cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * (size_t)num_points, s) != cudaSuccess ||
-            cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * (size_t)num_points, s) != cudaSuccess ||
-            (channels > 0 && cudaMemsetAsync(v_colors, 0, sizeof(float) * (size_t)channels * num_points, s) != cudaSuccess))
-            return igs::check_launch(who);
+        // the kernel accumulates with atomics; one memset when the three gradients are one block (v_xy, v_conic, v_colors back to back)
+        const size_t n = (size_t)num_points;
+        const bool block = v_conic == v_xy + 2 * n && (channels == 0 || v_colors == v_conic + 3 * n);
+        cudaError_t e;
+        if (block) {
+            e = cudaMemsetAsync(v_xy, 0, sizeof(float) * (5 + (size_t)channels) * n, s);
+        } else {
+            e = cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * n, s);
+            if (e == cudaSuccess) e = cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * n, s);
+            if (e == cudaSuccess && channels > 0) e = cudaMemsetAsync(v_colors, 0, sizeof(float) * (size_t)channels * n, s);
+        }
+        if (e != cudaSuccess) return igs::check_launch(who);
     }
     const int tiles_x = igs::ceil_div(img_w, kTile), tiles_y = igs::ceil_div(img_h, kTile);
     if (row_end < 0) row_end = tiles_y;
@@ -867,32 +868,25 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
     IGS_REQUIRE(igs::aligned(xys, 8), "%s: xys must be 8-byte aligned", who);
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
-    cudaError_t err = cudaSuccess;
+    // specialised kernels for 3 and 9 channels; otherwise the generic kernel with room for 5 + C sums (NV of 8, 16 or 32)
+    cudaError_t err;
     if (tile_topk != nullptr) {
-        // tiles with lists up to kPairStage entries; the union-walk kernel below takes the longer ones
-        if (channels == 3)
-            err = launch_bwd_pairs<3, 8>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        else if (channels <= 3)
-            err = launch_bwd_pairs<0, 8>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        else if (channels == 9)
-            err = launch_bwd_pairs<9, 16>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        else if (channels <= 11)
-            err = launch_bwd_pairs<0, 16>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        else
-            err = launch_bwd_pairs<0, 32>(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors, s);
-        if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+        const auto launch = channels == 3    ? launch_bwd_pairs<3, 8>
+                            : channels <= 3  ? launch_bwd_pairs<0, 8>
+                            : channels == 9  ? launch_bwd_pairs<9, 16>
+                            : channels <= 11 ? launch_bwd_pairs<0, 16>
+                                             : launch_bwd_pairs<0, 32>;
+        err = launch(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk,
+                     v_xy, v_conic, v_colors, s);
+    } else {
+        const auto launch = channels == 3    ? launch_bwd<3, 8>
+                            : channels <= 3  ? launch_bwd<0, 8>
+                            : channels == 9  ? launch_bwd<9, 16>
+                            : channels <= 11 ? launch_bwd<0, 16>
+                                             : launch_bwd<0, 32>;
+        err = launch(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy,
+                     v_conic, v_colors, s);
     }
-    if (tile_topk != nullptr) return IGS_OK;  // the pairs kernel handled every tile
-    if (channels == 3)
-        err = launch_bwd<3, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
-    else if (channels <= 3)
-        err = launch_bwd<0, 8>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
-    else if (channels == 9)
-        err = launch_bwd<9, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
-    else if (channels <= 11)
-        err = launch_bwd<0, 16>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
-    else
-        err = launch_bwd<0, 32>(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy, v_conic, v_colors, s);
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;
 }
@@ -968,7 +962,7 @@ int igs_raster_fwd_topk_tiles_l1_band(int tiles_x, int tiles_y, int img_height, 
     const int status = raster_fwd(tiles_x, tiles_y, img_height, img_width, row_begin, row_end, channels, gaussian_ids_sorted, tile_bins, xys,
                                   conics, colors, out_img, nullptr, tile_topk, stream, who, l1);
     if (status != IGS_OK) return status;
-    l1_finish_kernel<<<1, kFinishThreads, 0, igs::as_stream(stream)>>>(l1.partials, tiles, ratio, numel, loss);
+    igs::launch(l1_finish_kernel, 1, kFinishThreads, 0, igs::as_stream(stream), l1.partials, tiles, ratio, numel, loss);
     return igs::check_launch(who);
 }
 
