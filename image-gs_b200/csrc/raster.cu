@@ -50,129 +50,169 @@ struct PixelCoord {
     int tid;   // thread / pixel index within the tile
 };
 
-// Warp w covers the 8x4 patch (w % 2, w / 2) of the tile; lane l its pixel (l % 8, l / 8). Tiles are numbered within a band of tile rows
-// starting at row_begin (0 for the whole image); the coordinates are the image's.
-__device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_begin) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// Warp w covers the 8x4 patch (w % 2, w / 2) of the tile; lane l its pixel (l % 8, l / 8). lid is the pixel's index in this layout
+// (0..255). Tiles are numbered within a band of tile rows starting at row_begin (0 for the whole image); the coordinates are the image's.
+__device__ __forceinline__ PixelCoord tile_pixel_of(int tile, int tiles_x, int row_begin, int lid) {
+    const int lane = lid & 31, warp = lid >> 5;
     const int lx = (warp & 1) * 8 + (lane & 7), ly = (warp >> 1) * 4 + (lane >> 3);
-    return {(row_begin + tile / tiles_x) * kTile + ly, (tile % tiles_x) * kTile + lx, tid};
+    return {(row_begin + tile / tiles_x) * kTile + ly, (tile % tiles_x) * kTile + lx, lid};
+}
+
+// one pixel per thread
+__device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_begin) {
+    return tile_pixel_of(tile, tiles_x, row_begin, threadIdx.x);
 }
 
 // sigma of a Gaussian at a pixel, with the reference's operation order (forward.cu:309-311)
 __device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, float b, float c, float px, float py) {
-    const float dx = gx - px, dy = gy - py;
-    return 0.5f * (a * dx * dx + c * dy * dy) + b * dx * dy;
+    // spelled with explicit roundings so that every kernel computes it alike whatever the compiler could share between pixels: the
+    // contraction of the reference's fast-math build, 0.5 * fma(a dx, dx, (c dy) dy) fused into fma(b dx, dy, .)
+    const float dx = __fsub_rn(gx, px), dy = __fsub_rn(gy, py);
+    const float quad = __fmaf_rn(__fmul_rn(a, dx), dx, __fmul_rn(__fmul_rn(c, dy), dy));
+    return __fmaf_rn(__fmul_rn(b, dx), dy, __fmul_rn(0.5f, quad));
 }
 
-// The top-K selection of one pixel over its tile's list (range into ids_sorted), in list order, with the slot rule of the reference: free
-// slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it. The first ten
-// entries fill the slots with fixed indices when all of them are valid for the pixel (what the rule does while slots are free). The list
-// is staged through s_geo / s_cc in chunks of kChunk entries, with CTA barriers: every thread of the CTA must call it. The slots' list
-// positions are kept in shared memory (s_pos, [kTopK][kThreads] ints: one dynamic store per insertion instead of a select over ten
-// registers) and returned in pos[k] (-1 empty); val[k] is slot k's alpha.
+// The reference skips an entry whose sigma is negative, NaN or infinite (forward.cu:301)
+__device__ __forceinline__ bool sigma_valid(const float sigma) { return !(sigma < 0.f || isnan(sigma) || isinf(sigma)); }
+
+// The top-K selection of PPT pixels per thread over their tile's list (range into ids_sorted), in list order, with the slot rule of the
+// reference: free slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it.
+// The first ten entries fill the slots with fixed indices when all of them are valid for a pixel (what the rule does while slots are
+// free). The list is staged through s_geo / s_cc in chunks of kChunk entries by the CTA's kThreads / PPT threads, with CTA barriers:
+// every thread must call it. Each pixel's slot values stay in registers (val[q][k], its alpha); their list positions go to shared memory
+// (s_pos[k * kThreads + lid], -1 empty: one dynamic store per insertion instead of a select over ten registers). With two pixels per
+// thread the staged parameters and the loop are shared by both. Pixels outside the image (inside[q] false) take no entries.
+template <int PPT>
 __device__ __forceinline__ void select_topk(const int2 range, const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
-                                            const float *__restrict__ conics, const bool inside, const float px, const float py,
-                                            float4 *s_geo, float *s_cc, int *s_pos, int (&pos)[kTopK], float (&val)[kTopK]) {
+                                            const float *__restrict__ conics, const PixelCoord (&pc)[PPT], const bool (&inside)[PPT],
+                                            float4 *s_geo, float *s_cc, int *s_pos, float (&val)[PPT][kTopK]) {
+    constexpr int kStagers = kThreads / PPT;
     const int tid = threadIdx.x;
     const int len = range.y - range.x;
+    float px[PPT], py[PPT], min_val[PPT];
+    int filled[PPT], min_slot[PPT];
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        s_pos[k * kThreads + tid] = -1;
-        val[k] = 0.f;
+    for (int q = 0; q < PPT; ++q) {
+        px[q] = (float)pc[q].j, py[q] = (float)pc[q].i;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            s_pos[k * kThreads + pc[q].tid] = -1;
+            val[q][k] = 0.f;
+        }
+        filled[q] = inside[q] ? 0 : kTopK;  // a pixel outside the image counts as full with an unbeatable minimum
+        min_slot[q] = 0;
+        min_val[q] = inside[q] ? -1.f : INFINITY;
     }
-    int filled = 0, min_slot = 0;
-    float min_val = -1.f;
+    auto rescan = [&](const int q) {
+        min_slot[q] = 0;
+        min_val[q] = val[q][0];
+#pragma unroll
+        for (int k = 1; k < kTopK; ++k)
+            if (val[q][k] < min_val[q]) min_slot[q] = k, min_val[q] = val[q][k];
+    };
+    // replace the first slot holding the minimum; the new minimum (first slot on ties) is found in the pass that writes the value
+    auto insert = [&](const int q, const float alpha, const int position) {
+        s_pos[min_slot[q] * kThreads + pc[q].tid] = position;
+        const int slot = min_slot[q];
+        min_slot[q] = 0;
+        min_val[q] = slot == 0 ? alpha : val[q][0];
+        val[q][0] = min_val[q];
+#pragma unroll
+        for (int k = 1; k < kTopK; ++k) {
+            const float v = k == slot ? alpha : val[q][k];
+            val[q][k] = v;
+            if (v < min_val[q]) min_slot[q] = k, min_val[q] = v;
+        }
+    };
+    auto all_full = [&]() {
+        bool full = true;
+#pragma unroll
+        for (int q = 0; q < PPT; ++q) full = full && filled[q] == kTopK;
+        return full;
+    };
 
     for (int base = 0; base < len; base += kChunk) {
         const int count = min(kChunk, len - base);
         __syncthreads();
-        if (tid < count) {
-            const int g = __ldg(&ids_sorted[range.x + base + tid]);
+        for (int i = tid; i < count; i += kStagers) {
+            const int g = __ldg(&ids_sorted[range.x + base + i]);
             const float2 xy = __ldg(&xys[g]);
-            s_geo[tid] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            s_cc[tid] = __ldg(&conics[3 * g + 2]);
+            s_geo[i] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            s_cc[i] = __ldg(&conics[3 * g + 2]);
         }
         __syncthreads();
-        if (!inside) continue;
-        int e = 0;
+        int start[PPT];  // first entry of the chunk each pixel still has to consider
+#pragma unroll
+        for (int q = 0; q < PPT; ++q) start[q] = 0;
         if (base == 0 && count >= kTopK) {
-            // fast fill: all of the first ten entries valid -> slots 0..9 in order; otherwise the general rule below
-            bool all_valid = true;
+            // fast fill, per pixel: all of the first ten entries valid -> slots 0..9 in order
+            float sig[PPT][kTopK];
 #pragma unroll
             for (int k = 0; k < kTopK; ++k) {
-                const float4 q = s_geo[k];
-                const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[k], px, py);
-                all_valid = all_valid && !(sigma < 0.f || isnan(sigma) || isinf(sigma));
-                val[k] = __expf(-sigma);
+                const float4 g4 = s_geo[k];
+                const float cc = s_cc[k];
+#pragma unroll
+                for (int q = 0; q < PPT; ++q) sig[q][k] = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
             }
-            if (all_valid) {
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) s_pos[k * kThreads + tid] = k;
-                filled = kTopK;
-                e = kTopK;
-                min_slot = 0;
-                min_val = val[0];
-#pragma unroll
-                for (int k = 1; k < kTopK; ++k) {
-                    if (val[k] < min_val) {
-                        min_slot = k;
-                        min_val = val[k];
-                    }
+            for (int q = 0; q < PPT; ++q) {
+                if (!inside[q]) {
+                    start[q] = kTopK;  // never inserts: keeps the pixels' starts equal in the common case below
+                    continue;
                 }
-            } else {
+                bool all_valid = true;
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) val[k] = 0.f;
+                for (int k = 0; k < kTopK; ++k) all_valid = all_valid && sigma_valid(sig[q][k]);
+                if (!all_valid) continue;
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) {
+                    val[q][k] = __expf(-sig[q][k]);
+                    s_pos[k * kThreads + pc[q].tid] = k;
+                }
+                filled[q] = kTopK;
+                start[q] = kTopK;
+                rescan(q);
             }
         }
-        // filling: free slots take the valid entries in order
-        for (; e < count && filled < kTopK; ++e) {
-            const float4 q = s_geo[e];
-            const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
-            if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
-            const float alpha = __expf(-sigma);
+        int e = start[0];
 #pragma unroll
-            for (int k = 0; k < kTopK; ++k)
-                if (k == filled) val[k] = alpha;
-            s_pos[filled * kThreads + tid] = base + e;
-            ++filled;
-            if (filled == kTopK) {
-                min_slot = 0;
-                min_val = val[0];
+        for (int q = 1; q < PPT; ++q) e = min(e, start[q]);
+        if (all_full()) {
+            // the common case: every pixel full (all starts equal), only the replacement rule
+            for (; e < count; ++e) {
+                const float4 g4 = s_geo[e];
+                const float cc = s_cc[e];
 #pragma unroll
-                for (int k = 1; k < kTopK; ++k) {
-                    if (val[k] < min_val) {
-                        min_slot = k;
-                        min_val = val[k];
-                    }
+                for (int q = 0; q < PPT; ++q) {
+                    const float sigma = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                    if (!sigma_valid(sigma)) continue;
+                    const float alpha = __expf(-sigma);
+                    if (alpha > min_val[q]) insert(q, alpha, base + e);
                 }
             }
-        }
-        // full: an entry whose alpha exceeds the minimum replaces the first slot holding it; the new minimum (first slot on ties) is
-        // found in the same pass that writes the value
-        for (; e < count; ++e) {
-            const float4 q = s_geo[e];
-            const float sigma = gaussian_sigma(q.x, q.y, q.z, q.w, s_cc[e], px, py);
-            if (sigma < 0.f || isnan(sigma) || isinf(sigma)) continue;
-            const float alpha = __expf(-sigma);
-            if (!(alpha > min_val)) continue;
-            s_pos[min_slot * kThreads + tid] = base + e;
-            const int slot = min_slot;
-            min_slot = 0;
-            min_val = slot == 0 ? alpha : val[0];
-            val[0] = min_val;
+        } else {
+            for (; e < count; ++e) {
+                const float4 g4 = s_geo[e];
+                const float cc = s_cc[e];
 #pragma unroll
-            for (int k = 1; k < kTopK; ++k) {
-                const float v = k == slot ? alpha : val[k];
-                val[k] = v;
-                if (v < min_val) {
-                    min_slot = k;
-                    min_val = v;
+                for (int q = 0; q < PPT; ++q) {
+                    if (e < start[q]) continue;
+                    const float sigma = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                    if (!sigma_valid(sigma)) continue;
+                    const float alpha = __expf(-sigma);
+                    if (filled[q] < kTopK) {
+#pragma unroll
+                        for (int k = 0; k < kTopK; ++k)
+                            if (k == filled[q]) val[q][k] = alpha;
+                        s_pos[filled[q] * kThreads + pc[q].tid] = base + e;
+                        if (++filled[q] == kTopK) rescan(q);
+                    } else if (alpha > min_val[q]) {
+                        insert(q, alpha, base + e);
+                    }
                 }
             }
         }
     }
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) pos[k] = s_pos[k * kThreads + tid];
 }
 
 // The L1 loss of the rendered pixels fused into the forward pass (the training loss of model.py:1224-1227, ratio * F.l1_loss(image,
@@ -218,8 +258,13 @@ __global__ void __launch_bounds__(kFinishThreads) l1_finish_kernel(const float *
     if (threadIdx.x == 0) *loss = ratio * (all / numel);
 }
 
+// Pixels per thread of the forward pass: two (a thread takes the pixels of lane ids t and t + 128 of the tile layout), sharing the staged
+// Gaussians' loads and the loop, and 128 threads per tile.
+constexpr int kFwdPixels = 2;
+constexpr int kFwdThreads = kThreads / kFwdPixels;
+
 template <int C>
-__global__ void __launch_bounds__(kThreads, (C == 1 || C == 3) ? 5 : 4)
+__global__ void __launch_bounds__(kFwdThreads, 8)
     raster_fwd_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h, const int channels_rt,
         const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
         const float *__restrict__ conics, const float *__restrict__ colors, float *__restrict__ out_img, int *__restrict__ pixel_topk,
@@ -227,80 +272,96 @@ __global__ void __launch_bounds__(kThreads, (C == 1 || C == 3) ? 5 : 4)
     igs::wait_for_predecessor();
     constexpr int kMaxC = C > 0 ? C : kMaxChannels;
     const int channels = C > 0 ? C : channels_rt;
-    __shared__ float4 s_geo[kChunk];  // x, y, conic a, conic b
-    __shared__ float s_cc[kChunk];    // conic c
+    __shared__ float4 s_geo[kChunk];         // x, y, conic a, conic b
+    __shared__ float s_cc[kChunk];           // conic c
     __shared__ int s_ids[kThreads * kTopK];  // the slots' list positions during the selection, then the IDs of [H, W, 10] lists
 
     const int tile = blockIdx.x;
-    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
-    const bool inside = pc.i < img_h && pc.j < img_w;
-    const float px = (float)pc.j, py = (float)pc.i;
+    PixelCoord pc[kFwdPixels];
+    bool inside[kFwdPixels];
+#pragma unroll
+    for (int q = 0; q < kFwdPixels; ++q) {
+        pc[q] = tile_pixel_of(tile, tiles_x, row_begin, threadIdx.x + q * kFwdThreads);
+        inside[q] = pc[q].i < img_h && pc[q].j < img_w;
+    }
     const int2 range = tile_bins[tile];
     const int len = range.y - range.x;
 
-    int pos[kTopK];
-    float val[kTopK];
-    select_topk(range, ids_sorted, xys, conics, inside, px, py, s_geo, s_cc, s_ids, pos, val);
+    float val[kFwdPixels][kTopK];
+    select_topk<kFwdPixels>(range, ids_sorted, xys, conics, pc, inside, s_geo, s_cc, s_ids, val);
 
-    // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
-    int gid[kTopK];
-    float sum = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        gid[k] = pos[k] >= 0 ? __ldg(&ids_sorted[range.x + pos[k]]) : -1;
-        if (pos[k] >= 0) sum += val[k];
-    }
-    const double inv = 1.0 / ((double)sum + igs::kNormEps);
-    float pix[kMaxC];
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        if (gid[k] < 0) continue;
-        const float vis = (float)((double)val[k] * inv);
-        const float *f = colors + (size_t)gid[k] * channels;
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) pix[c] += __ldg(&f[c]) * vis;
-    }
     const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
-    const int p = (pc.i - row_begin * kTile) * img_w + pc.j;
-    if (inside) {
+    const bool addressable = len < (int)kNoSlot;
+    float acc = 0.f;  // the CTA's part of the L1 loss
 #pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) out_img[(size_t)c * num_pixels + p] = pix[c];
-    }
-    if (l1.target != nullptr) {
-        float acc = 0.f;
-        if (inside) {
+    for (int q = 0; q < kFwdPixels; ++q) {
+        int pos[kTopK], gid[kTopK];
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) pos[k] = s_ids[k * kThreads + pc[q].tid];
+        // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            gid[k] = pos[k] >= 0 ? __ldg(&ids_sorted[range.x + pos[k]]) : -1;
+            if (pos[k] >= 0) sum += val[q][k];
+        }
+        const double inv = 1.0 / ((double)sum + igs::kNormEps);
+        float pix[kMaxC];
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            if (gid[k] < 0) continue;
+            const float vis = (float)((double)val[q][k] * inv);
+            const float *f = colors + (size_t)gid[k] * channels;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+        }
+        const int p = (pc[q].i - row_begin * kTile) * img_w + pc[q].j;
+        if (inside[q]) {
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c) {
                 if (c >= channels) continue;
-                const float d = pix[c] - __ldcs(&l1.target[(size_t)c * num_pixels + p]);
-                acc += fabsf(d);
-                __stcs(&l1.v_output[(size_t)c * num_pixels + p], l1_sign(d) * l1.grad_value);
+                out_img[(size_t)c * num_pixels + p] = pix[c];
+                if (l1.target != nullptr) {
+                    const float d = pix[c] - __ldcs(&l1.target[(size_t)c * num_pixels + p]);
+                    acc += fabsf(d);
+                    __stcs(&l1.v_output[(size_t)c * num_pixels + p], l1_sign(d) * l1.grad_value);
+                }
             }
         }
+        if (tile_topk != nullptr) {
+            // a tile whose list holds 65535 entries or more is left empty: raster_bwd_pairs_kernel selects its lists again
+            uint16_t *dst = tile_topk + (size_t)tile * kTopK * kThreads + pc[q].tid;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) dst[k * kThreads] = (addressable && pos[k] >= 0) ? (uint16_t)pos[k] : kNoSlot;
+        }
+    }
+    if (l1.target != nullptr) {
         const float total = cta_sum(acc, reinterpret_cast<float *>(s_cc));
         if (threadIdx.x == 0) l1.partials[tile] = total;
     }
-
-    if (tile_topk != nullptr) {
-        // a tile whose list holds 65535 entries or more is left empty: raster_bwd_pairs_kernel selects its lists again
-        const bool addressable = len < (int)kNoSlot;
-        uint16_t *dst = tile_topk + (size_t)tile * kTopK * kThreads + pc.tid;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) dst[k * kThreads] = (addressable && pos[k] >= 0) ? (uint16_t)pos[k] : kNoSlot;
-    }
     if (pixel_topk != nullptr) {
-        // stage the IDs by thread, then write each tile row of 16 pixels x 10 IDs (80 int2) with consecutive threads
-        __syncthreads();  // every thread has read its positions from s_ids
+        // the IDs by pixel into shared memory (positions read first, then overwritten), then each tile row of 16 pixels x 10 IDs (80
+        // int2) written with consecutive threads
+        int ids[kFwdPixels][kTopK];
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) s_ids[pc.tid * kTopK + k] = gid[k];
+        for (int q = 0; q < kFwdPixels; ++q)
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const int position = s_ids[k * kThreads + pc[q].tid];
+                ids[q][k] = position >= 0 ? __ldg(&ids_sorted[range.x + position]) : -1;
+            }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < kFwdPixels; ++q)
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) s_ids[pc[q].tid * kTopK + k] = ids[q][k];
         __syncthreads();
         const int i0 = (tile / tiles_x) * kTile, j0 = (tile % tiles_x) * kTile;
         const int row_pairs = kTile * kTopK / 2;
-        for (int idx = threadIdx.x; idx < kTile * row_pairs; idx += kThreads) {
+        for (int idx = threadIdx.x; idx < kTile * row_pairs; idx += kFwdThreads) {
             const int ly = idx / row_pairs, rem = idx % row_pairs;
             const int lx = rem / (kTopK / 2), pair = rem % (kTopK / 2);
             const int i = i0 + ly, j = j0 + lx;
@@ -544,7 +605,7 @@ struct PairSmem {
 };
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3)
+__global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h,
         const int channels_rt, const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
         const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
@@ -580,8 +641,13 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3)
         }
     } else {
         // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
-        float val[kTopK];
-        select_topk(range, ids_sorted, xys, conics, inside, px, py, sm.geo, sm.cc, reinterpret_cast<int *>(&sm.vw[0][0]), key, val);
+        const PixelCoord pcs[1] = {pc};
+        const bool ins[1] = {inside};
+        float val[1][kTopK];
+        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);
+        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, val);
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
         __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
     }
 
@@ -780,7 +846,7 @@ template <int C>
 cudaError_t launch_fwd(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids, const int2 *bins,
                        const float2 *xys, const float *conics, const float *colors, float *out, int *pixel_topk, uint16_t *tile_topk,
                        const FusedL1 &l1, cudaStream_t s) {
-    return igs::launch(raster_fwd_kernel<C>, tiles, kThreads, 0, s, tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys,
+    return igs::launch(raster_fwd_kernel<C>, tiles, kFwdThreads, 0, s, tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins, xys,
                        conics, colors, out, pixel_topk, tile_topk, l1);
 }
 
