@@ -32,6 +32,15 @@ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 inline bool aligned(const void *p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
+// sigma of a Gaussian (center gx, gy; conic a, b, c) at a pixel, with the reference's operation order (forward.cu:309-311)
+__device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, float b, float c, float px, float py) {
+    // spelled with explicit roundings so that every kernel computes it alike whatever the compiler could share between pixels: the
+    // contraction of the reference's fast-math build, 0.5 * fma(a dx, dx, (c dy) dy) fused into fma(b dx, dy, .)
+    const float dx = __fsub_rn(gx, px), dy = __fsub_rn(gy, py);
+    const float quad = __fmaf_rn(__fmul_rn(a, dx), dx, __fmul_rn(__fmul_rn(c, dy), dy));
+    return __fmaf_rn(__fmul_rn(b, dx), dy, __fmul_rn(0.5f, quad));
+}
+
 // Programmatic dependent launch (sm_90 and later): the kernels of the training step are launched with programmatic stream serialization,
 // so a kernel is scheduled while its predecessor on the stream drains instead of after it; each of them begins with
 // wait_for_predecessor() (griddepcontrol.wait: returns once the predecessor has completed and its writes are visible; a no-op for a

@@ -39,8 +39,7 @@ __global__ void __launch_bounds__(256) loo_kernel(const int img_w, const int num
         if (g < 0) continue;
         const float2 xy = __ldg(&xys[g]);
         const float a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), cc = __ldg(&conics[3 * g + 2]);
-        const float dx = xy.x - px, dy = xy.y - py;
-        w[k] = __expf(-(0.5f * (a * dx * dx + cc * dy * dy) + b * dx * dy));
+        w[k] = __expf(-igs::gaussian_sigma(xy.x, xy.y, a, b, cc, px, py));
         sum_w += w[k];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)

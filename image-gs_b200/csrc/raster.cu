@@ -63,14 +63,6 @@ __device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_
     return tile_pixel_of(tile, tiles_x, row_begin, threadIdx.x);
 }
 
-// sigma of a Gaussian at a pixel, with the reference's operation order (forward.cu:309-311)
-__device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, float b, float c, float px, float py) {
-    // spelled with explicit roundings so that every kernel computes it alike whatever the compiler could share between pixels: the
-    // contraction of the reference's fast-math build, 0.5 * fma(a dx, dx, (c dy) dy) fused into fma(b dx, dy, .)
-    const float dx = __fsub_rn(gx, px), dy = __fsub_rn(gy, py);
-    const float quad = __fmaf_rn(__fmul_rn(a, dx), dx, __fmul_rn(__fmul_rn(c, dy), dy));
-    return __fmaf_rn(__fmul_rn(b, dx), dy, __fmul_rn(0.5f, quad));
-}
 
 // The reference skips an entry whose sigma is negative, NaN or infinite (forward.cu:301)
 __device__ __forceinline__ bool sigma_valid(const float sigma) { return !(sigma < 0.f || isnan(sigma) || isinf(sigma)); }
@@ -152,7 +144,7 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 const float4 g4 = s_geo[k];
                 const float cc = s_cc[k];
 #pragma unroll
-                for (int q = 0; q < PPT; ++q) sig[q][k] = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                for (int q = 0; q < PPT; ++q) sig[q][k] = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
             }
 #pragma unroll
             for (int q = 0; q < PPT; ++q) {
@@ -184,7 +176,7 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 const float cc = s_cc[e];
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
-                    const float sigma = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                    const float sigma = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
                     if (!sigma_valid(sigma)) continue;
                     const float alpha = __expf(-sigma);
                     if (alpha > min_val[q]) insert(q, alpha, base + e);
@@ -197,7 +189,7 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
                     if (e < start[q]) continue;
-                    const float sigma = gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                    const float sigma = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
                     if (!sigma_valid(sigma)) continue;
                     const float alpha = __expf(-sigma);
                     if (filled[q] < kTopK) {
@@ -500,7 +492,7 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
         d[k] = 0.f;
         if (kk == kNone) continue;
         const Params q = params_of(kk);
-        d[k] = __expf(-gaussian_sigma(q.x, q.y, q.a, q.b, q.c, px, py));
+        d[k] = __expf(-igs::gaussian_sigma(q.x, q.y, q.a, q.b, q.c, px, py));
         denom += d[k];
     }
     // dL/dd_k = s_k / D - sum_j d_j s_j / D^2 with s_k = f_k . v_out
@@ -683,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
             if (key[k] < 0) continue;
             const int e = key[k];
             const float4 q = sm.geo[e];
-            d[k] = __expf(-gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[e], px, py));
+            d[k] = __expf(-igs::gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[e], px, py));
             denom += d[k];
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c)
@@ -709,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
                 for (int ch = 0; ch < kMaxC; ++ch)
                     if (ch < channels) s[k] += __ldg(&colors[(size_t)g * channels + ch]) * v_out[ch];
             }
-            d[k] = __expf(-gaussian_sigma(gx, gy, a, b, c, px, py));
+            d[k] = __expf(-igs::gaussian_sigma(gx, gy, a, b, c, px, py));
             denom += d[k];
         }
     }
