@@ -186,9 +186,9 @@ def time_graph(graph, reps, flush):
 RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the raster kernels, from one ncu capture of this workload
-# (`ncu --set full --clock-control none -k regex:"raster_(fwd|bwd_pairs)" -s 3 -c 3 python bench.py --steps 2 --warmup 3 --no-cpu
+# (`ncu --set full --clock-control none -k regex:"raster_(fwd|bwd_pairs)" -s 2 -c 2 python bench.py --steps 2 --warmup 3 --no-cpu
 # --no-e2e --no-stages`, caches flushed before each pass); None where no capture was taken
-NCU_TRAFFIC = {"cfg3_1080p": {"forward": 26.44e6 + 41.33e6, "backward": 68.46e6 + 1.19e6}}
+NCU_TRAFFIC = {"cfg3_1080p": {"forward": 26.49e6 + 37.97e6, "backward": 68.47e6 + 1.12e6}}
 
 
 def step_options(wl, device):
