@@ -110,7 +110,7 @@ def dist_setup(gpus):
     return world, rank, local
 
 
-def cpu_step_rate(wl, inp, min_seconds=10.0, max_steps=5):
+def cpu_step_rate(wl, inp, min_seconds=10.0, max_steps=1000):
     """Steps/s of the CPU oracle (all host threads) over whole steps of the workload: (rate, threads, steps)."""
     sys.path.insert(0, ROOT)
     from oracle import cpu

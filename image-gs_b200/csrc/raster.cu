@@ -7,9 +7,11 @@
 // accumulated over the slots in slot order. Slot order and contents are part of the output (pixel_topk), so the insertion rule is kept
 // exactly.
 //
-// B200 layout: one CTA of 256 threads per tile (grid = tiles, so the hardware balances uneven list lengths over the 148 SMs); each warp
-// owns a compact 8x4 pixel patch; the tile's list is staged in shared memory in chunks of 256 entries (one 16-byte and one 4-byte
-// broadcast load per Gaussian and pixel). Two output forms of the top-K lists:
+// B200 layout: one CTA per tile (grid = tiles, so the hardware balances uneven list lengths over the 148 SMs); pixels are numbered so
+// that 32 consecutive ones form a compact 8x4 patch; the forward's 128 threads take two pixels each (patches t and t + 128), the
+// backward's 256 threads one; the tile's list is staged in shared memory in chunks of 256 entries (one 16-byte and one 4-byte broadcast
+// load per Gaussian, shared by a thread's pixels). The training step's forward also takes the L1 loss of its pixels and writes the
+// loss's gradient with respect to the image. Two output forms of the top-K lists:
 //   * pixel_topk [H, W, 10] int32 Gaussian IDs (the reference's operator output), written through shared memory as coalesced 8-byte rows;
 //   * tile lists (autograd path): per tile, slot-major [10][256] uint16 positions in the tile's Gaussian list, 20 bytes per pixel instead
 //     of 40, written as coalesced 64-byte warp rows, and read back by the backward pass, which stages the same list in shared memory.
@@ -36,7 +38,7 @@ using igs::kTile;
 using igs::kTilePixels;
 using igs::kTopK;
 
-constexpr int kThreads = kTilePixels;  // one thread per pixel of the tile
+constexpr int kThreads = kTilePixels;  // pixels of a tile (and threads of the backward's CTA)
 constexpr int kChunk = 256;            // list entries staged per round in the forward pass
 constexpr int kPairStage = 256;        // longest tile list of the pairs-grouped backward pass
 constexpr int kPairs = kThreads * kTopK;
