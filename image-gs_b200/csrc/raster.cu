@@ -411,7 +411,7 @@ struct Params {
 };
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
+__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
                                                               const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
                                                               const float2 *__restrict__ xys, const float *__restrict__ conics,
                                                               const float *__restrict__ colors, const float *__restrict__ v_output,
@@ -497,7 +497,8 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
         d[k] = __expf(-igs::gaussian_sigma(q.x, q.y, q.a, q.b, q.c, px, py));
         denom += d[k];
     }
-    // dL/dd_k = s_k / D - sum_j d_j s_j / D^2 with s_k = f_k . v_out
+    // dL/dd_k = s_k / D - sum_j d_j s_j / D^2 with s_k = f_k . v_out (fast-math division: products with the reciprocals)
+    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
     float s[kTopK];
     float shared = 0.f;
 #pragma unroll
@@ -507,13 +508,13 @@ __global__ void __launch_bounds__(kThreads) raster_bwd_kernel(const int tiles_x,
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)
             if (c < channels) s[k] += color_of(key[k], c) * v_out[c];
-        shared += -d[k] / (denom * denom) * s[k];
+        shared += -d[k] * inv2 * s[k];
     }
     float w[kTopK], vsig[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        w[k] = d[k] / denom;
-        vsig[k] = -d[k] * (s[k] / denom + shared);
+        w[k] = d[k] * inv;
+        vsig[k] = -d[k] * (s[k] * inv + shared);
     }
 
     // union walk over the warp's entries in increasing key order
