@@ -22,9 +22,9 @@
 // v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Two kernels:
 //   * raster_bwd_pairs_kernel (training step, from the tile lists): the tile's (pixel, slot) pairs grouped by Gaussian in shared memory,
 //     one warp per Gaussian summing its pairs, then one global atomic per (tile, Gaussian, value); see the comment above it;
-//   * raster_bwd_kernel (the [H, W, 10] operator): each warp visits the union of its 32 pixels' top-K Gaussians in
-//     increasing key order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving
-//     reduce-scatter, and adds them into per-tile shared accumulators or directly to the outputs.
+//   * raster_bwd_ids_kernel (the [H, W, 10] operator): each warp visits the union of its 32 pixels' top-K Gaussian IDs in increasing
+//     order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving reduce-scatter, and
+//     adds them with one global atomic per value.
 #include <algorithm>
 #include <cstddef>
 
@@ -42,11 +42,6 @@ constexpr int kThreads = kTilePixels;  // pixels of a tile (and threads of the b
 constexpr int kChunk = 256;            // list entries staged per round in the forward pass
 constexpr int kPairStage = 256;        // longest tile list of the pairs-grouped backward pass
 constexpr int kPairs = kThreads * kTopK;
-// list entries staged by the backward pass (fewer for the widest value vectors, to stay within 48 KB of static shared memory); longer
-// lists read the Gaussians from global memory and accumulate with global atomics
-template <int NV>
-constexpr int bwd_stage() { return NV <= 16 ? 256 : 128; }
-
 struct PixelCoord {
     int i, j;  // row, column in the image
     int tid;   // thread / pixel index within the tile
@@ -403,111 +398,56 @@ __device__ __forceinline__ int halving_index(int lane) {
     return index;
 }
 
-constexpr int kNone = 0x7fffffff;
-
-// Gaussian parameters for the backward pass: from the staged tile list, or from global memory by ID
-struct Params {
-    float x, y, a, b, c;
-};
+// ---- backward pass of the [H, W, 10] operator --------------------------------------------------------------------------------------
+//
+// The operator's lists hold Gaussian IDs, with no tile list to index, so each warp (an 8x4 patch) walks the union of its pixels' IDs in
+// increasing order (a warp-wide minimum per step); lanes whose pixel holds the current Gaussian contribute their values, the others
+// zeros; the warp sums the 5 + C values with one recursive-halving reduce-scatter and one global atomic per value. Nothing is staged:
+// the few Gaussians of a warp's union are read through the L1 cache.
+constexpr int kNoId = 0x7fffffff;
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt,
-                                                              const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins,
-                                                              const float2 *__restrict__ xys, const float *__restrict__ conics,
-                                                              const float *__restrict__ colors, const float *__restrict__ v_output,
-                                                              const int *__restrict__ pixel_topk, const uint16_t *__restrict__ tile_topk,
-                                                              float *__restrict__ v_xy, float *__restrict__ v_conic,
-                                                              float *__restrict__ v_colors) {
-    // channel registers: C when fixed, else as many as the NV-wide value vector holds
+__global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
+    raster_bwd_ids_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt, const float2 *__restrict__ xys,
+        const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
+        const int *__restrict__ pixel_topk, float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
     constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
     static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry values and the channels");
     const int channels = C > 0 ? C : channels_rt;
-    constexpr int kBwdStage = bwd_stage<NV>();
-    __shared__ float4 s_geo[kBwdStage];
-    __shared__ float s_cc[kBwdStage];
-    __shared__ float s_col[kBwdStage * kMaxC];
-    __shared__ float s_acc[kBwdStage * NV];
-
-    const int tile = blockIdx.x;
     const int lane = threadIdx.x & 31;
-    const PixelCoord pc = tile_pixel(tile, tiles_x, 0);
+    const PixelCoord pc = tile_pixel(blockIdx.x, tiles_x, 0);
     const bool inside = pc.i < img_h && pc.j < img_w;
     const float px = (float)pc.j, py = (float)pc.i;
     const int num_pixels = img_h * img_w;
     const int p = inside ? pc.i * img_w + pc.j : 0;
 
-    // Keys of the pixel's entries: list positions (tile lists) or Gaussian IDs (pixel_topk); kNone for empty slots and outside pixels
-    const bool by_position = tile_topk != nullptr;
-    int2 range = make_int2(0, 0);
-    if (by_position) range = tile_bins[tile];
-    const int len = range.y - range.x;
-    const bool staged = by_position && len <= kBwdStage;
-    if (staged) {
-        for (int e = threadIdx.x; e < len; e += kThreads) {
-            const int g = __ldg(&ids_sorted[range.x + e]);
-            const float2 xy = __ldg(&xys[g]);
-            s_geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            s_cc[e] = __ldg(&conics[3 * g + 2]);
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s_col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
-        }
-        for (int e = threadIdx.x; e < len * NV; e += kThreads) s_acc[e] = 0.f;
-        __syncthreads();
-    }
-
-    auto params_of = [&](int key) -> Params {
-        if (staged) {
-            const float4 q = s_geo[key];
-            return {q.x, q.y, q.z, q.w, s_cc[key]};
-        }
-        const int g = by_position ? __ldg(&ids_sorted[range.x + key]) : key;
-        const float2 xy = __ldg(&xys[g]);
-        return {xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2])};
-    };
-    auto color_of = [&](int key, int c) -> float {
-        if (staged) return s_col[key * kMaxC + c];
-        const int g = by_position ? __ldg(&ids_sorted[range.x + key]) : key;
-        return __ldg(&colors[(size_t)g * channels + c]);
-    };
-
     float v_out[kMaxC];
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
-
-    int key[kTopK];
+    int id[kTopK];
     float d[kTopK];
     float denom = (float)igs::kNormEps;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        int kk = kNone;
-        if (inside) {
-            if (by_position) {
-                const uint16_t v = __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + pc.tid]);
-                kk = v == kNoSlot ? kNone : (int)v;
-            } else {
-                const int g = __ldg(&pixel_topk[(size_t)p * kTopK + k]);
-                kk = g < 0 ? kNone : g;
-            }
-        }
-        key[k] = kk;
+        const int g = inside ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        id[k] = g < 0 ? kNoId : g;
         d[k] = 0.f;
-        if (kk == kNone) continue;
-        const Params q = params_of(kk);
-        d[k] = __expf(-igs::gaussian_sigma(q.x, q.y, q.a, q.b, q.c, px, py));
+        if (g < 0) continue;
+        const float2 xy = __ldg(&xys[g]);
+        d[k] = __expf(-igs::gaussian_sigma(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2]), px, py));
         denom += d[k];
     }
-    // dL/dd_k = s_k / D - sum_j d_j s_j / D^2 with s_k = f_k . v_out (fast-math division: products with the reciprocals)
+    // the reference's algebra with its divisions by denom as products with two reciprocals (fast-math division)
     const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
     float s[kTopK];
     float shared = 0.f;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
         s[k] = 0.f;
-        if (key[k] == kNone) continue;
+        if (id[k] == kNoId) continue;
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) s[k] += color_of(key[k], c) * v_out[c];
+            if (c < channels) s[k] += __ldg(&colors[(size_t)id[k] * channels + c]) * v_out[c];
         shared += -d[k] * inv2 * s[k];
     }
     float w[kTopK], vsig[kTopK];
@@ -517,59 +457,38 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3) raster_bwd_kernel(c
         vsig[k] = -d[k] * (s[k] * inv + shared);
     }
 
-    // union walk over the warp's entries in increasing key order
     const int value_index = halving_index<NV>(lane);
-    const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    const bool adds = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    float *const target = value_index < 3 ? v_conic + value_index : value_index < 5 ? v_xy + (value_index - 3) : v_colors + (value_index - 5);
+    const int stride = value_index < 3 ? 3 : value_index < 5 ? 2 : channels;
     while (true) {
-        int head = key[0];
+        int head = id[0];
 #pragma unroll
-        for (int k = 1; k < kTopK; ++k) head = min(head, key[k]);
+        for (int k = 1; k < kTopK; ++k) head = min(head, id[k]);
         const int cur = __reduce_min_sync(0xffffffffu, head);
-        if (cur == kNone) break;
+        if (cur == kNoId) break;
         float ws = 0.f, vs = 0.f;
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
-            if (key[k] == cur) {
+            if (id[k] == cur) {
                 ws = w[k];
                 vs = vsig[k];
-                key[k] = kNone;
+                id[k] = kNoId;
             }
         }
-        const Params q = params_of(cur);
-        const float dx = q.x - px, dy = q.y - py;
+        const float2 xy = __ldg(&xys[cur]);
+        const float a = __ldg(&conics[3 * cur]), b = __ldg(&conics[3 * cur + 1]), c = __ldg(&conics[3 * cur + 2]);
+        const float dx = xy.x - px, dy = xy.y - py;
         float val[NV];
         val[0] = 0.5f * vs * dx * dx;
         val[1] = vs * dx * dy;
         val[2] = 0.5f * vs * dy * dy;
-        val[3] = vs * (q.a * dx + q.b * dy);
-        val[4] = vs * (q.b * dx + q.c * dy);
+        val[3] = vs * (a * dx + b * dy);
+        val[4] = vs * (b * dx + c * dy);
 #pragma unroll
-        for (int c = 0; c < NV - 5; ++c) val[5 + c] = c < kMaxC ? ws * v_out[c < kMaxC ? c : 0] : 0.f;
+        for (int ch = 0; ch < NV - 5; ++ch) val[5 + ch] = ch < kMaxC ? ws * v_out[ch < kMaxC ? ch : 0] : 0.f;
         const float total = warp_sum_scatter<NV>(val, lane);
-        if (holds_total) {
-            if (staged) {
-                atomicAdd(&s_acc[cur * NV + value_index], total);
-            } else {
-                const int g = by_position ? __ldg(&ids_sorted[range.x + cur]) : cur;
-                float *target = value_index < 3   ? v_conic + 3 * (size_t)g + value_index
-                                : value_index < 5 ? v_xy + 2 * (size_t)g + (value_index - 3)
-                                                  : v_colors + (size_t)g * channels + (value_index - 5);
-                atomicAdd(target, total);
-            }
-        }
-    }
-
-    if (staged) {
-        __syncthreads();
-        const int nvals = 5 + channels;
-        for (int e = threadIdx.x; e < len * nvals; e += kThreads) {
-            const int entry = e / nvals, v = e % nvals;
-            const float total = s_acc[entry * NV + v];
-            if (total == 0.f) continue;
-            const int g = __ldg(&ids_sorted[range.x + entry]);
-            float *target = v < 3 ? v_conic + 3 * (size_t)g + v : v < 5 ? v_xy + 2 * (size_t)g + (v - 3) : v_colors + (size_t)g * channels + (v - 5);
-            atomicAdd(target, total);
-        }
+        if (adds) atomicAdd(target + (size_t)stride * cur, total);
     }
 }
 
@@ -873,12 +792,11 @@ int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, in
 }
 
 template <int C, int NV>
-cudaError_t launch_bwd(int tiles, int tiles_x, int img_h, int img_w, int channels, const int *ids, const int2 *bins, const float2 *xys,
-                       const float *conics, const float *colors, const float *v_output, const int *pixel_topk, const uint16_t *tile_topk,
-                       float *v_xy, float *v_conic, float *v_colors, cudaStream_t s) {
-    raster_bwd_kernel<C, NV><<<tiles, kThreads, 0, s>>>(tiles_x, img_h, img_w, channels, ids, bins, xys, conics, colors, v_output,
-                                                         pixel_topk, tile_topk, v_xy, v_conic, v_colors);
-    return cudaGetLastError();
+cudaError_t launch_bwd_ids(int tiles, int tiles_x, int img_h, int img_w, int channels, const float2 *xys, const float *conics,
+                           const float *colors, const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors,
+                           cudaStream_t s) {
+    return igs::launch(raster_bwd_ids_kernel<C, NV>, tiles, kThreads, 0, s, tiles_x, img_h, img_w, channels, xys, conics, colors,
+                       v_output, pixel_topk, v_xy, v_conic, v_colors);
 }
 
 template <int C, int NV>
@@ -940,13 +858,12 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
         err = launch(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted, bins, xy2, conics, colors, v_output, tile_topk,
                      v_xy, v_conic, v_colors, s);
     } else {
-        const auto launch = channels == 3    ? launch_bwd<3, 8>
-                            : channels <= 3  ? launch_bwd<0, 8>
-                            : channels == 9  ? launch_bwd<9, 16>
-                            : channels <= 11 ? launch_bwd<0, 16>
-                                             : launch_bwd<0, 32>;
-        err = launch(tiles, tiles_x, img_h, img_w, channels, ids_sorted, bins, xy2, conics, colors, v_output, pixel_topk, tile_topk, v_xy,
-                     v_conic, v_colors, s);
+        const auto launch = channels == 3    ? launch_bwd_ids<3, 8>
+                            : channels <= 3  ? launch_bwd_ids<0, 8>
+                            : channels == 9  ? launch_bwd_ids<9, 16>
+                            : channels <= 11 ? launch_bwd_ids<0, 16>
+                                             : launch_bwd_ids<0, 32>;
+        err = launch(tiles, tiles_x, img_h, img_w, channels, xy2, conics, colors, v_output, pixel_topk, v_xy, v_conic, v_colors, s);
     }
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;

@@ -2,8 +2,7 @@
 The reference's own CUDA kernels (its gsplat extension, built from source into oracle/_ref) beside ours on the same B200 and the same
 1080p/20k inputs: the top-K forward and backward kernels one to one, and the whole step as model.py drives it (projection, prefix sum,
 binning with the exact count read back, forward, ATen's L1 loss and its gradient, backward, projection backward). Times are CUDA-event
-medians of eager launches after warm-up, L2 flushed before each; ours must not be slower on the forward and on the step. Run with -s
-to see the table.
+medians of eager launches after warm-up, L2 flushed before each; ours must not be slower. Run with -s to see the table.
 """
 import pytest
 import torch
@@ -75,8 +74,8 @@ def test_faster_than_reference_kernels(device, ref_module):
     print(f"{'1080p/20k on B200':40s} {'reference ms':>13s} {'ours ms':>9s} {'speed-up':>9s}")
     for name, (ref_ms, ours_ms) in rows.items():
         print(f"{name:40s} {ref_ms:13.3f} {ours_ms:9.3f} {ref_ms / ours_ms:8.2f}x")
-    # the training step and the forward kernel must not be slower; the [H, W, 10] backward operator (the reference's own union-walk
-    # design, kept for API callers; the step uses the pairs-grouped kernel) is reported only
-    for name in ("top-K forward, [H,W,10] lists", "whole step, eager", "whole step (ours as one CUDA graph)"):
-        ref_ms, ours_ms = rows[name]
-        assert ours_ms <= ref_ms, f"{name}: ours {ours_ms:.3f} ms, reference {ref_ms:.3f} ms"
+    # none may be slower; the [H, W, 10] backward operator walks the same warp unions as the reference's kernel and is only a few percent
+    # faster, so it gets 5 % of room for timing noise (the training step's backward uses the pairs-grouped kernel)
+    for name, (ref_ms, ours_ms) in rows.items():
+        room = 1.05 if name.startswith("top-K backward") else 1.0
+        assert ours_ms <= room * ref_ms, f"{name}: ours {ours_ms:.3f} ms, reference {ref_ms:.3f} ms"
