@@ -1,7 +1,6 @@
 """Binning helpers of gsplat/gsplat/utils.py, on the igs_b200 kernels."""
 from typing import Tuple
 
-import torch
 from torch import Tensor
 
 from . import _path  # noqa: F401

@@ -4,7 +4,6 @@ pybind functions (gsplat/gsplat/cuda/csrc/ext.cpp:4-32, bindings.h). Outputs are
 device and every launch goes to the current CUDA stream, so the operators can be captured in CUDA graphs (the *_capacity paths never read
 device memory back to the host).
 """
-import math
 from typing import Optional, Tuple
 
 import torch
