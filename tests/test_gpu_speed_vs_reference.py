@@ -1,13 +1,15 @@
 """
 The reference's own CUDA kernels (its gsplat extension, built from source into oracle/_ref) beside ours on the same B200 and the same
-1080p/20k inputs: the top-K forward and backward kernels one to one, and the whole step as model.py drives it (projection, prefix sum,
-binning with the exact count read back, forward, ATen's L1 loss and its gradient, backward, projection backward). Times are CUDA-event
+1080p/20k inputs: the top-K forward and backward kernels one to one, the leave-one-out pruning kernel, the feature weights (ATen
+operations in the reference), and the whole step as model.py drives it (projection, prefix sum, binning with the exact count read back,
+forward, ATen's L1 loss and its gradient, backward, projection backward). Times are CUDA-event
 medians of eager launches after warm-up, L2 flushed before each; ours must not be slower. Run with -s to see the table.
 """
 import pytest
 import torch
 
 from igs_b200 import ops, pipeline, workloads
+from oracle import weights as ow
 
 pytestmark = pytest.mark.gpu
 
@@ -51,6 +53,15 @@ def test_faster_than_reference_kernels(device, ref_module):
     rows["top-K backward, [H,W,10] lists"] = (
         median_ms(lambda: ref_module.nd_rasterize_backward_topk_norm(h, w, 16, 16, xys, conics, feats, v_out, topk)),
         median_ms(lambda: ops.nd_rasterize_backward_topk_norm(h, w, 16, 16, xys, conics, feats, v_out, topk)))
+
+    rows["leave-one-out loss increase (pruning)"] = (
+        median_ms(lambda: ref_module.topk_norm_loo_loss_increase(h, w, xys, conics, feats, topk, d["target"], False, 1e-4)),
+        median_ms(lambda: ops.topk_norm_loo_loss_increase(h, w, xys, conics, feats, topk, d["target"], False, 1e-4)))
+    # the reference computes the feature weights with ATen operations (model.py:1404-1421, quantization.py:218-230), restated in
+    # oracle/weights.py and run here on the GPU
+    rows["feature weights (ATen in the reference)"] = (
+        median_ms(lambda: ow.feature_weights(xys, conics, topk, h, w), reps=5),
+        median_ms(lambda: ops.topk_feature_weights(h, w, xys, conics, topk)))
 
     def reference_step():
         x, r, c, t = ref_module.project_gaussians_2d_scale_rot_forward(n, d["means"], d["scales"], d["rotations"], h, w, tb)
