@@ -45,7 +45,7 @@ def peaks():
 
 
 class ClockSampler:
-    """SM clocks and throttle reasons of one GPU sampled through NVML every ~2 ms while running (the timed region can be a few ms)."""
+    """SM clocks and throttle reasons of one GPU sampled through NVML every ~0.5 ms while running (the timed region can be a few ms)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
@@ -79,7 +79,7 @@ class ClockSampler:
                 self.samples.append((mhz, reasons))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.0005)
 
     def __exit__(self, *exc):
         self.stop.set()
@@ -91,7 +91,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         reasons = sorted({name for _, r in self.samples for name, bit in self.REASONS.items() if r & bit})
         return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.samples), "source": "NVML, 2 ms polling during the timed steps"}
+                "samples": len(self.samples), "source": "NVML, polled every 0.5 ms during the timed steps"}
 
 
 def dist_setup(gpus):
