@@ -51,3 +51,21 @@ def test_empty_and_single(device):
     assert nb.bitstream_neighbors(np.zeros((0, 2), np.int64), device=device).shape == (0, 8)
     one = nb.nearest_neighbors(torch.zeros(1, 2, dtype=torch.int64, device=device))
     assert bool((one == -1).all())
+
+
+def test_matches_reference_search_at_80k(device):
+    """The 2160p workload's 80,000 positions (1/8-pixel steps, bitstream order): identical to the reference's own C++ causal_neighbors
+    (compress/csrc/prediction.cpp, built from source into oracle/_ref)."""
+    from igs_b200 import workloads
+    from oracle import build_ref
+
+    try:
+        ref = build_ref.load_prediction()
+    except ImportError as e:
+        pytest.skip(str(e))
+    wl = workloads.get_workload("cfg4_2160p")
+    inp = workloads.make_inputs(wl)
+    q = torch.round(inp["means"].double() * torch.tensor([wl.width, wl.height], dtype=torch.float64) / 0.125).long().numpy()
+    ordered = np.ascontiguousarray(q[nb.bitstream_order(q, 3)])
+    got = nb.causal_neighbors(torch.from_numpy(ordered).to(device)).cpu().numpy()
+    np.testing.assert_array_equal(got, ref.causal_neighbors(ordered))

@@ -93,6 +93,19 @@ def test_feature_weights_vs_reference(name, device):
     torch.testing.assert_close(ops.topk_feature_weights(h, w, xys, conics, topk), got, rtol=0, atol=0)
 
 
+def test_feature_weights_full_size_vs_aten(device):
+    """At 1080p/20k: the int64 fixed-point sums equal the reference's ATen operations run on the GPU (oracle/weights.py)."""
+    from oracle import weights as ow
+
+    wl = workloads.get_workload("cfg3_1080p")
+    d = to_dev(workloads.make_inputs(wl), device)
+    ours = ours_stages(d, wl.height, wl.width)
+    fixed = ops.topk_feature_weights_fixed(wl.height, wl.width, ours["xys"], ours["conics"], ours["pixel_topk"])
+    ref = ow.feature_weights_fixed(ow.iter_topk_weights(ours["xys"], ours["conics"], ours["pixel_topk"], wl.height, wl.width),
+                                   wl.num_gaussians, 1e-4, device)
+    assert torch.equal(fixed, ref)
+
+
 @pytest.mark.parametrize("name", PY_CASES)
 def test_quantize_ste_symbols_bit_exact(name, device):
     z = py_fixture(name)
