@@ -1,0 +1,51 @@
+"""
+Host logic without a GPU: tile-row band splits (contiguous, covering, balanced by weight), the tile grid, and the seeded workloads
+(deterministic, with the configurations' shapes).
+"""
+import numpy as np
+import pytest
+
+from igs_b200 import bands, ops, workloads
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_band_rows_split_is_contiguous_covering_and_balanced(seed):
+    rng = np.random.default_rng(seed)
+    tiles_y = int(rng.integers(1, 200))
+    world = int(rng.integers(1, 9))
+    weights = rng.exponential(1.0, tiles_y) * (rng.random(tiles_y) < 0.8)  # some empty rows
+    for w in (None, weights.tolist()):
+        parts = [bands.band_rows(tiles_y, world, r, w) for r in range(world)]
+        assert parts[0][0] == 0 and parts[-1][1] == tiles_y
+        for (a0, a1), (b0, b1) in zip(parts, parts[1:]):
+            assert a1 == b0 and a0 <= a1
+        if w is not None and weights.sum() > 0:
+            # no band exceeds its share by more than one row's weight
+            share, biggest = weights.sum() / world, weights.max()
+            for a0, a1 in parts:
+                assert weights[a0:a1].sum() <= share + biggest + 1e-9
+
+
+def test_band_rows_rejects_bad_arguments():
+    with pytest.raises(ValueError):
+        bands.band_rows(10, 2, 2)
+    with pytest.raises(ValueError):
+        bands.band_rows(10, 2, 0, [1.0] * 9)
+
+
+def test_tile_grid():
+    assert ops.tile_grid(1080, 1920) == (120, 68, 1)
+    assert ops.tile_grid(1, 1) == (1, 1, 1)
+    assert ops.tile_grid(17, 33) == (3, 2, 1)
+
+
+def test_workloads_are_seeded_and_shaped():
+    wl = workloads.get_workload("cfg1_256")
+    a, b = workloads.make_inputs(wl), workloads.make_inputs(wl)
+    assert workloads.input_digest(a) == workloads.input_digest(b)
+    assert a["target"].shape == (3, 256, 256) and a["means"].shape == (1000, 2) and a["features"].shape == (1000, 3)
+    assert float(a["target"].min()) >= 0.0 and float(a["target"].max()) <= 1.0
+    yuv = workloads.make_inputs(workloads.get_workload("cfg2_480p_yuv"))
+    assert yuv["loss_target"].shape == (3, 480, 854) and yuv["loss_transform"].shape == (3, 3)
+    tex = workloads.get_workload("cfg5_tex9")
+    assert tex.channels == 9 and tex.images == 64 and workloads.get_workload("cfg4_2160p").sharding == "bands"
