@@ -64,54 +64,80 @@ __device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_
 // The reference skips an entry whose sigma is negative, NaN or infinite (forward.cu:301)
 __device__ __forceinline__ bool sigma_valid(const float sigma) { return !(sigma < 0.f || isnan(sigma) || isinf(sigma)); }
 
+// sigma of PPT pixels of one column (px) from a Gaussian's centre and halved conic (ha = a / 2, b, hc = c / 2): the same roundings as
+// igs::gaussian_sigma, since halving is exact (0.5 fma(a dx, dx, (c dy) dy) = fma(ha dx, dx, (hc dy) dy)); dx, ha dx and b dx are shared
+template <int PPT>
+__device__ __forceinline__ void column_sigma(const float4 g4, const float hc, const float px, const float (&py)[PPT], float (&sigma)[PPT]) {
+    const float dx = __fsub_rn(g4.x, px);
+    const float adx = __fmul_rn(g4.z, dx), bdx = __fmul_rn(g4.w, dx);
+#pragma unroll
+    for (int q = 0; q < PPT; ++q) {
+        const float dy = __fsub_rn(g4.y, py[q]);
+        sigma[q] = __fmaf_rn(bdx, dy, __fmaf_rn(adx, dx, __fmul_rn(__fmul_rn(hc, dy), dy)));
+    }
+}
+
 // The top-K selection of PPT pixels per thread over their tile's list (range into ids_sorted), in list order, with the slot rule of the
 // reference: free slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it.
 // The first ten entries fill the slots with fixed indices when all of them are valid for a pixel (what the rule does while slots are
 // free). The list is staged through s_geo / s_cc in chunks of kChunk entries by the CTA's kThreads / PPT threads, with CTA barriers:
-// every thread must call it. Each pixel's slot values stay in registers (val[q][k], its alpha); their list positions go to shared memory
-// (s_pos[k * kThreads + lid], -1 empty: one dynamic store per insertion instead of a select over ten registers). With two pixels per
-// thread the staged parameters and the loop are shared by both. Pixels outside the image (inside[q] false) take no entries.
+// every thread must call it. The slots live in shared memory, alpha in s_val and the list position in s_pos (both [k * kThreads + lid],
+// position -1 for empty), so an insertion is two dynamic stores instead of a select over ten registers; each pixel keeps the minimum of
+// each half of its slots (0-4, 5-9) and the first slot holding it in registers, so that an insertion rescans only the half it wrote (the
+// first slot of the strict minimum over all ten is the second half's only if that half's minimum is strictly smaller). The staged conic
+// is halved (exactly), which drops a multiplication from sigma, and the PPT pixels of a thread share a column, so dx and its products
+// are shared too. On return val[q][k] holds the slots' alpha. Pixels outside the image (inside[q] false) take no entries.
 template <int PPT>
 __device__ __forceinline__ void select_topk(const int2 range, const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
                                             const float *__restrict__ conics, const PixelCoord (&pc)[PPT], const bool (&inside)[PPT],
-                                            float4 *s_geo, float *s_cc, int *s_pos, float (&val)[PPT][kTopK]) {
+                                            float4 *s_geo, float *s_cc, int *s_pos, float *s_val, float (&val)[PPT][kTopK]) {
     constexpr int kStagers = kThreads / PPT;
     const int tid = threadIdx.x;
     const int len = range.y - range.x;
-    float px[PPT], py[PPT], min_val[PPT];
-    int filled[PPT], min_slot[PPT];
+    const float px = (float)pc[0].j;  // the pixels share a column
+    float py[PPT], min_val[PPT];
+    int filled[PPT];
+    float gv[PPT][2];  // per half of the slots (0-4, 5-9): its minimum and the first slot holding it
+    int gs[PPT][2];
 #pragma unroll
     for (int q = 0; q < PPT; ++q) {
-        px[q] = (float)pc[q].j, py[q] = (float)pc[q].i;
+        py[q] = (float)pc[q].i;
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             s_pos[k * kThreads + pc[q].tid] = -1;
-            val[q][k] = 0.f;
+            s_val[k * kThreads + pc[q].tid] = 0.f;
         }
         filled[q] = inside[q] ? 0 : kTopK;  // a pixel outside the image counts as full with an unbeatable minimum
-        min_slot[q] = 0;
         min_val[q] = inside[q] ? -1.f : INFINITY;
     }
-    auto rescan = [&](const int q) {
-        min_slot[q] = 0;
-        min_val[q] = val[q][0];
+    // minimum of one half of a pixel's slots (the first slot on ties)
+    auto scan_half = [&](const int q, const int h) {
+        const float *v = s_val + h * (kTopK / 2) * kThreads + pc[q].tid;
+        float m = v[0];
+        int ms = 0;
 #pragma unroll
-        for (int k = 1; k < kTopK; ++k)
-            if (val[q][k] < min_val[q]) min_slot[q] = k, min_val[q] = val[q][k];
-    };
-    // replace the first slot holding the minimum; the new minimum (first slot on ties) is found in the pass that writes the value
-    auto insert = [&](const int q, const float alpha, const int position) {
-        s_pos[min_slot[q] * kThreads + pc[q].tid] = position;
-        const int slot = min_slot[q];
-        min_slot[q] = 0;
-        min_val[q] = slot == 0 ? alpha : val[q][0];
-        val[q][0] = min_val[q];
-#pragma unroll
-        for (int k = 1; k < kTopK; ++k) {
-            const float v = k == slot ? alpha : val[q][k];
-            val[q][k] = v;
-            if (v < min_val[q]) min_slot[q] = k, min_val[q] = v;
+        for (int k = 1; k < kTopK / 2; ++k) {
+            const float x = v[k * kThreads];
+            if (x < m) m = x, ms = k;
         }
+        return make_float2(m, __int_as_float(ms + h * (kTopK / 2)));
+    };
+    auto rescan = [&](const int q) {
+        const float2 h0 = scan_half(q, 0), h1 = scan_half(q, 1);
+        gv[q][0] = h0.x, gs[q][0] = __float_as_int(h0.y);
+        gv[q][1] = h1.x, gs[q][1] = __float_as_int(h1.y);
+        min_val[q] = fminf(gv[q][0], gv[q][1]);
+    };
+    // replace the first slot holding the minimum (the second half's only if strictly smaller), then rescan that half
+    auto insert = [&](const int q, const float alpha, const int position) {
+        const int h = gv[q][1] < gv[q][0] ? 1 : 0;
+        const int slot = h ? gs[q][1] : gs[q][0];
+        s_pos[slot * kThreads + pc[q].tid] = position;
+        s_val[slot * kThreads + pc[q].tid] = alpha;
+        const float2 m = scan_half(q, h);
+        if (h) gv[q][1] = m.x, gs[q][1] = __float_as_int(m.y);
+        else gv[q][0] = m.x, gs[q][0] = __float_as_int(m.y);
+        min_val[q] = fminf(gv[q][0], gv[q][1]);
     };
     auto all_full = [&]() {
         bool full = true;
@@ -126,8 +152,8 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         for (int i = tid; i < count; i += kStagers) {
             const int g = __ldg(&ids_sorted[range.x + base + i]);
             const float2 xy = __ldg(&xys[g]);
-            s_geo[i] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            s_cc[i] = __ldg(&conics[3 * g + 2]);
+            s_geo[i] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            s_cc[i] = 0.5f * __ldg(&conics[3 * g + 2]);
         }
         __syncthreads();
         int start[PPT];  // first entry of the chunk each pixel still has to consider
@@ -140,8 +166,10 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
             for (int k = 0; k < kTopK; ++k) {
                 const float4 g4 = s_geo[k];
                 const float cc = s_cc[k];
+                float s[PPT];
+                column_sigma<PPT>(g4, cc, px, py, s);
 #pragma unroll
-                for (int q = 0; q < PPT; ++q) sig[q][k] = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                for (int q = 0; q < PPT; ++q) sig[q][k] = s[q];
             }
 #pragma unroll
             for (int q = 0; q < PPT; ++q) {
@@ -155,12 +183,13 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                 if (!all_valid) continue;
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) {
-                    val[q][k] = __expf(-sig[q][k]);
+                    const float alpha = __expf(-sig[q][k]);
+                    s_val[k * kThreads + pc[q].tid] = alpha;
                     s_pos[k * kThreads + pc[q].tid] = k;
                 }
                 filled[q] = kTopK;
-                start[q] = kTopK;
                 rescan(q);
+                start[q] = kTopK;
             }
         }
         int e = start[0];
@@ -171,10 +200,14 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
             for (; e < count; ++e) {
                 const float4 g4 = s_geo[e];
                 const float cc = s_cc[e];
+                float s[PPT];
+                column_sigma<PPT>(g4, cc, px, py, s);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
-                    const float sigma = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
-                    if (!sigma_valid(sigma)) continue;
+                    // every slot holds an alpha >= 0 (the minimum of a pixel outside the image is infinite), so sigma >= 0 suffices:
+                    // an infinite sigma gives alpha = 0, which replaces nothing, and NaN fails the test
+                    const float sigma = s[q];
+                    if (!(sigma >= 0.f)) continue;
                     const float alpha = __expf(-sigma);
                     if (alpha > min_val[q]) insert(q, alpha, base + e);
                 }
@@ -183,16 +216,16 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
             for (; e < count; ++e) {
                 const float4 g4 = s_geo[e];
                 const float cc = s_cc[e];
+                float s[PPT];
+                column_sigma<PPT>(g4, cc, px, py, s);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
                     if (e < start[q]) continue;
-                    const float sigma = igs::gaussian_sigma(g4.x, g4.y, g4.z, g4.w, cc, px[q], py[q]);
+                    const float sigma = s[q];
                     if (!sigma_valid(sigma)) continue;
                     const float alpha = __expf(-sigma);
                     if (filled[q] < kTopK) {
-#pragma unroll
-                        for (int k = 0; k < kTopK; ++k)
-                            if (k == filled[q]) val[q][k] = alpha;
+                        s_val[filled[q] * kThreads + pc[q].tid] = alpha;
                         s_pos[filled[q] * kThreads + pc[q].tid] = base + e;
                         if (++filled[q] == kTopK) rescan(q);
                     } else if (alpha > min_val[q]) {
@@ -202,6 +235,10 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
             }
         }
     }
+#pragma unroll
+    for (int q = 0; q < PPT; ++q)
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) val[q][k] = s_val[k * kThreads + pc[q].tid];
 }
 
 // The L1 loss of the rendered pixels fused into the forward pass (the training loss of model.py:1224-1227, ratio * F.l1_loss(image,
@@ -247,8 +284,8 @@ __global__ void __launch_bounds__(kFinishThreads) l1_finish_kernel(const float *
     if (threadIdx.x == 0) *loss = ratio * (all / numel);
 }
 
-// Pixels per thread of the forward pass: two (a thread takes the pixels of lane ids t and t + 128 of the tile layout), sharing the staged
-// Gaussians' loads and the loop, and 128 threads per tile.
+// Pixels per thread of the forward pass: two (a thread takes the pixels of lane ids t and t + 128 of the tile layout: the same column,
+// eight rows apart), sharing the staged Gaussians' loads, dx and the loop, and 128 threads per tile.
 constexpr int kFwdPixels = 2;
 constexpr int kFwdThreads = kThreads / kFwdPixels;
 
@@ -261,8 +298,8 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
     igs::wait_for_predecessor();
     constexpr int kMaxC = C > 0 ? C : kMaxChannels;
     const int channels = C > 0 ? C : channels_rt;
-    __shared__ float4 s_geo[kChunk];         // x, y, conic a, conic b
-    __shared__ float s_cc[kChunk];           // conic c
+    __shared__ float4 s_geo[kChunk];         // x, y, conic a / 2, conic b; then the colours of a one-chunk list
+    __shared__ float s_cc[kChunk];           // conic c / 2
     __shared__ int s_ids[kThreads * kTopK];  // the slots' list positions during the selection, then the IDs of [H, W, 10] lists
 
     const int tile = blockIdx.x;
@@ -277,10 +314,22 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
     const int len = range.y - range.x;
 
     float val[kFwdPixels][kTopK];
-    select_topk<kFwdPixels>(range, ids_sorted, xys, conics, pc, inside, s_geo, s_cc, s_ids, val);
+    __shared__ float s_val[kThreads * kTopK];  // the slots' alpha values during the selection
+    select_topk<kFwdPixels>(range, ids_sorted, xys, conics, pc, inside, s_geo, s_cc, s_ids, s_val, val);
 
     const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
     const bool addressable = len < (int)kNoSlot;
+    // a list of one chunk: its colours replace the staged geometry in shared memory, read by list position below
+    constexpr bool kStageColors = C > 0 && C <= 4;
+    const bool colors_staged = kStageColors && len <= kChunk;
+    if (colors_staged) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < len; e += kFwdThreads) {
+            const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + e]) * channels;
+            s_geo[e] = make_float4(__ldg(&f[0]), C > 1 ? __ldg(&f[1]) : 0.f, C > 2 ? __ldg(&f[2]) : 0.f, C > 3 ? __ldg(&f[3]) : 0.f);
+        }
+        __syncthreads();
+    }
     float acc = 0.f;  // the CTA's part of the L1 loss
 #pragma unroll
     for (int q = 0; q < kFwdPixels; ++q) {
@@ -290,22 +339,34 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
         // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
         float sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            gid[k] = pos[k] >= 0 ? __ldg(&ids_sorted[range.x + pos[k]]) : -1;
+        for (int k = 0; k < kTopK; ++k)
             if (pos[k] >= 0) sum += val[q][k];
-        }
         const double inv = 1.0 / ((double)sum + igs::kNormEps);
         float pix[kMaxC];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
+        if (colors_staged) {
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            if (gid[k] < 0) continue;
-            const float vis = (float)((double)val[q][k] * inv);
-            const float *f = colors + (size_t)gid[k] * channels;
+            for (int k = 0; k < kTopK; ++k) {
+                if (pos[k] < 0) continue;
+                const float vis = (float)((double)val[q][k] * inv);
+                const float4 f = s_geo[pos[k]];
+                const float fc[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+                for (int c = 0; c < kMaxC && c < 4; ++c) pix[c] += fc[c] * vis;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) gid[k] = pos[k] >= 0 ? __ldg(&ids_sorted[range.x + pos[k]]) : -1;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                if (gid[k] < 0) continue;
+                const float vis = (float)((double)val[q][k] * inv);
+                const float *f = colors + (size_t)gid[k] * channels;
+#pragma unroll
+                for (int c = 0; c < kMaxC; ++c)
+                    if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+            }
         }
         const int p = (pc[q].i - row_begin * kTile) * img_w + pc[q].j;
         if (inside[q]) {
@@ -558,8 +619,9 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
         const PixelCoord pcs[1] = {pc};
         const bool ins[1] = {inside};
         float val[1][kTopK];
-        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);
-        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, val);
+        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and values
+        float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
+        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
         __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
