@@ -14,7 +14,8 @@ using igs::kMaxChannels;
 using igs::kTopK;
 
 template <int C>
-__global__ void __launch_bounds__(256) loo_kernel(const int img_w, const int num_pixels, const int channels_rt, const float2 *__restrict__ xys,
+__global__ void __launch_bounds__(256) loo_kernel(const int img_w, const int num_pixels, const int channels_rt, const int num_points,
+                                                  const float2 *__restrict__ xys,
                                                   const float *__restrict__ conics, const float *__restrict__ colors,
                                                   const int *__restrict__ pixel_topk, const float *__restrict__ targets, const bool squared,
                                                   const float eps, float *__restrict__ loss_increase) {
@@ -33,7 +34,8 @@ __global__ void __launch_bounds__(256) loo_kernel(const int img_w, const int num
     }
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        const int g = valid ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        const int id = valid ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        const int g = id < num_points ? id : -1;  // an ID of N or more counts as an empty slot instead of reading out of bounds
         ids[k] = g;
         w[k] = 0.f;
         if (g < 0) continue;
@@ -95,10 +97,12 @@ int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_p
     IGS_REQUIRE(igs::aligned(xys, 8), "igs_loo_loss_increase: xys must be 8-byte aligned");
     const int blocks = igs::ceil_div(num_pixels, 256);
     if (channels == 3)
-        loo_kernel<3><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, reinterpret_cast<const float2 *>(xys), conics, colors,
+        loo_kernel<3><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, num_points, reinterpret_cast<const float2 *>(xys), conics,
+                                             colors,
                                              pixel_topk, targets, squared != 0, eps, loss_increase);
     else
-        loo_kernel<0><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, reinterpret_cast<const float2 *>(xys), conics, colors,
+        loo_kernel<0><<<blocks, 256, 0, s>>>(img_width, num_pixels, channels, num_points, reinterpret_cast<const float2 *>(xys), conics,
+                                             colors,
                                              pixel_topk, targets, squared != 0, eps, loss_increase);
     return igs::check_launch("igs_loo_loss_increase");
 }

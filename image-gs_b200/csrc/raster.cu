@@ -469,7 +469,8 @@ constexpr int kNoId = 0x7fffffff;
 
 template <int C, int NV>
 __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
-    raster_bwd_ids_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt, const float2 *__restrict__ xys,
+    raster_bwd_ids_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt, const int num_points,
+        const float2 *__restrict__ xys,
         const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
         const int *__restrict__ pixel_topk, float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
     constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
@@ -490,7 +491,8 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
     float denom = (float)igs::kNormEps;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        const int g = inside ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        const int id_in = inside ? __ldg(&pixel_topk[(size_t)p * kTopK + k]) : -1;
+        const int g = id_in < num_points ? id_in : -1;  // an ID of N or more counts as an empty slot instead of reading out of bounds
         id[k] = g < 0 ? kNoId : g;
         d[k] = 0.f;
         if (g < 0) continue;
@@ -611,8 +613,9 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     if (len < (int)kNoSlot) {
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
+            // empty (kNoSlot) or, in lists not written by the forward pass, past the end of the list: no entry
             const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
-            key[k] = v == kNoSlot ? -1 : (int)v;
+            key[k] = (int)v < len ? (int)v : -1;
         }
     } else {
         // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
@@ -854,11 +857,11 @@ int raster_fwd(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, in
 }
 
 template <int C, int NV>
-cudaError_t launch_bwd_ids(int tiles, int tiles_x, int img_h, int img_w, int channels, const float2 *xys, const float *conics,
+cudaError_t launch_bwd_ids(int tiles, int tiles_x, int img_h, int img_w, int channels, int num_points, const float2 *xys, const float *conics,
                            const float *colors, const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors,
                            cudaStream_t s) {
-    return igs::launch(raster_bwd_ids_kernel<C, NV>, tiles, kThreads, 0, s, tiles_x, img_h, img_w, channels, xys, conics, colors,
-                       v_output, pixel_topk, v_xy, v_conic, v_colors);
+    return igs::launch(raster_bwd_ids_kernel<C, NV>, tiles, kThreads, 0, s, tiles_x, img_h, img_w, channels, num_points, xys, conics,
+                       colors, v_output, pixel_topk, v_xy, v_conic, v_colors);
 }
 
 template <int C, int NV>
@@ -925,7 +928,8 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
                             : channels == 9  ? launch_bwd_ids<9, 16>
                             : channels <= 11 ? launch_bwd_ids<0, 16>
                                              : launch_bwd_ids<0, 32>;
-        err = launch(tiles, tiles_x, img_h, img_w, channels, xy2, conics, colors, v_output, pixel_topk, v_xy, v_conic, v_colors, s);
+        err = launch(tiles, tiles_x, img_h, img_w, channels, num_points, xy2, conics, colors, v_output, pixel_topk, v_xy, v_conic, v_colors,
+                     s);
     }
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;

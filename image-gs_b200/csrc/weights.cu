@@ -15,7 +15,8 @@ namespace {
 constexpr int kTopK = 10;
 constexpr int kThreads = 256;
 
-__global__ void __launch_bounds__(kThreads) feature_weights_kernel(const int img_h, const int img_w, const float2 *__restrict__ xys,
+__global__ void __launch_bounds__(kThreads) feature_weights_kernel(const int img_h, const int img_w, const int num_points,
+                                                                   const float2 *__restrict__ xys,
                                                                    const float *__restrict__ conics, const int *__restrict__ pixel_topk,
                                                                    const double eps, unsigned long long *__restrict__ fixed) {
     const int64_t p = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -25,9 +26,10 @@ __global__ void __launch_bounds__(kThreads) feature_weights_kernel(const int img
     const int2 *row = reinterpret_cast<const int2 *>(pixel_topk + p * kTopK);
 #pragma unroll
     for (int k = 0; k < kTopK / 2; ++k) {
+        // an ID outside [0, N) counts as an empty slot (the reference's indexing would fault on one of N or more)
         const int2 v = __ldg(&row[k]);
-        ids[2 * k] = v.x;
-        ids[2 * k + 1] = v.y;
+        ids[2 * k] = (unsigned)v.x < (unsigned)num_points ? v.x : -1;
+        ids[2 * k + 1] = (unsigned)v.y < (unsigned)num_points ? v.y : -1;
     }
     float w[kTopK];
 #pragma unroll
@@ -76,7 +78,8 @@ extern "C" int igs_feature_weights(int img_height, int img_width, int num_points
     IGS_REQUIRE(xys && conics && pixel_topk, "igs_feature_weights: null pointer");
     IGS_REQUIRE(igs::aligned(xys, 8) && igs::aligned(pixel_topk, 8), "igs_feature_weights: xys and pixel_topk must be 8-byte aligned");
     const int64_t blocks = (pixels + kThreads - 1) / kThreads;
-    feature_weights_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(img_height, img_width, reinterpret_cast<const float2 *>(xys), conics,
+    feature_weights_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(img_height, img_width, num_points, reinterpret_cast<const float2 *>(xys),
+                                                               conics,
                                                                pixel_topk, eps, reinterpret_cast<unsigned long long *>(fixed_point));
     return igs::check_launch("igs_feature_weights");
 }

@@ -106,12 +106,14 @@ int igs_raster_fwd_topk_tiles_l1(int tiles_x, int tiles_y, int img_height, int i
                                  float *v_output, void *workspace, size_t workspace_bytes, void *stream);
 
 /* nd_rasterize_backward_topk_norm (bindings.cu:444-502, kernel backward.cu:187-335): v_output [C,H,W]; outputs v_xy [N,2],
- * v_conic [N,3], v_colors [N,C] are zeroed and accumulated (float atomics: the last bits vary run to run). */
+ * v_conic [N,3], v_colors [N,C] are zeroed and accumulated (float atomics: the last bits vary run to run). IDs of pixel_topk outside
+ * [0, N) count as empty slots (the reference reads out of bounds for IDs of N or more). */
 int igs_raster_bwd_topk(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
                         const float *colors, const float *v_output, const int32_t *pixel_topk, float *v_xy, float *v_conic,
                         float *v_colors, void *stream);
 
-/* The backward pass from igs_raster_fwd_topk_tiles' lists, with the same gaussian_ids_sorted / tile_bins. */
+/* The backward pass from igs_raster_fwd_topk_tiles' lists, with the same gaussian_ids_sorted / tile_bins. A list position at or past
+ * the end of its tile's list counts as an empty slot. */
 int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int num_points, const int32_t *gaussian_ids_sorted,
                               const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
                               const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream);
@@ -151,7 +153,8 @@ int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin,
                                    float *v_colors, void *stream);
 
 /* topk_norm_loo_loss_increase (bindings.cu:895-936, kernel forward.cu:667-738): per Gaussian, the increase of the absolute (squared
- * when `squared`) error summed over pixels and channels when it alone leaves the top-K lists; targets [C,H,W]. */
+ * when `squared`) error summed over pixels and channels when it alone leaves the top-K lists; targets [C,H,W]. IDs of N or more count
+ * as empty slots. */
 int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_points, const float *xys, const float *conics,
                           const float *colors, const int32_t *pixel_topk, const float *targets, int squared, float eps,
                           float *loss_increase, void *stream);
@@ -160,7 +163,7 @@ int igs_loo_loss_increase(int img_height, int img_width, int channels, int num_p
  * its squared normalized top-K weight as 64-bit fixed point with 40 fractional bits (fixed_point [N] int64, zeroed here; the weights are
  * fixed_point / 2^40). The slot weights exp(-sigma) are recomputed with the reference's IEEE float32 arithmetic from pixel_topk [H,W,10]
  * (of igs_raster_fwd_topk), normalized in double with eps (1e-4 in the reference) and rounded half to even; integer atomics make the sums
- * independent of the order of the additions. */
+ * independent of the order of the additions. IDs outside [0, N) count as empty slots. */
 int igs_feature_weights(int img_height, int img_width, int num_points, const float *xys, const float *conics, const int32_t *pixel_topk,
                         double eps, int64_t *fixed_point, void *stream);
 
