@@ -185,10 +185,29 @@ def time_graph(graph, reps, flush):
 
 RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the raster kernels, from one ncu capture of this workload
-# (`ncu --set full --clock-control none -k regex:"raster_(fwd|bwd_pairs)" -s 2 -c 2 python bench.py --steps 2 --warmup 3 --no-cpu
-# --no-e2e --no-stages`, caches flushed before each pass); None where no capture was taken
-NCU_TRAFFIC = {"cfg3_1080p": {"forward": 26.49e6 + 37.97e6, "backward": 68.47e6 + 1.12e6}}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the step's raster kernel, from one ncu capture of this workload
+# (`ncu --set full --clock-control none -k regex:raster_step -s 2 -c 2 python bench.py --steps 2 --warmup 3 --no-cpu --no-e2e
+# --no-stages`, caches flushed before each pass); None where no capture was taken
+NCU_TRAFFIC = {}
+
+
+def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, traffic, label=""):
+    """The roofline entry of the step's dominant raster kernel from the single-stage times. The fused step kernel (stage "raster") moves,
+    algorithmically: the image written and the target read (8 C bytes a pixel), the list IDs (4 bytes an intersection), each Gaussian's
+    centre, conic and colours read once and its gradients written once (2 x 4 (5 + C) bytes), the tile ranges (8 bytes a tile); the
+    separate kernels (stages "forward" and "backward") move the [H, W, 10] lists of the operator surface and the image gradient too."""
+    if "raster" in stage_ms:
+        name, ms = "raster_step", stage_ms["raster"]
+        nbytes = p * 8 * c + num_isect * 4 + n * 4 * (5 + c) * 2 + num_tiles * 8
+    else:
+        dominant = max(("forward", "backward"), key=lambda s: stage_ms.get(s, 0.0))
+        name, ms = f"raster_{dominant}", stage_ms[dominant]
+        fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + num_isect * 4 + n * 4 * (5 + c)
+        bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
+        nbytes = fwd_bytes if dominant == "forward" else bwd_bytes
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": name + label, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": nbytes, "kernel_ms": ms}
 
 
 def step_options(wl, device):
@@ -250,16 +269,10 @@ def run_ours(args, wl):
         stage_ms[s.strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g
     if not stage_ms:
-        stage_ms = {"forward": ms_per_step, "backward": 0.0}
+        stage_ms = {"raster": ms_per_step}  # no per-stage times: the whole step stands in for the raster kernel
     hbm_peak, peak_kind = peaks()
     p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
-    # the forward kernel renders and takes the L1 loss: image write, [H, W, 10] lists of the operator surface, target read, gradient write
-    fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + num_isect * 4 + n * 4 * (5 + c)
-    bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
-    dominant = max(("forward", "backward"), key=lambda s: stage_ms[s])
-    dom_ms = stage_ms[dominant]
-    dom_bytes = fwd_bytes if dominant == "forward" else bwd_bytes
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    roofline = raster_roofline(stage_ms, p, c, n, k, num_isect, wl.num_tiles, hbm_peak, peak_kind, NCU_TRAFFIC.get(wl.name))
     step_bytes = (p * (8 * c + 8 * k) + n * 4 * (5 + 7 + 2 * (5 + c) + (5 + c) + 5 + 5) + num_isect * 4 * 5 + wl.num_tiles * 16)
     loss_bytes = 12 * c * p
 
@@ -287,10 +300,7 @@ def run_ours(args, wl):
                        "l2": "flushed between timed steps (256 MB write outside the event intervals)", "graph": "one CUDA graph per step"},
             "gaussian_pixel_evals_per_step": evals, "gaussian_pixel_evals_per_s": evals * value,
             "stages_ms": stage_ms,
-            "roofline": {"bound": "hbm", "kernel": f"raster_{dominant}", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC.get(wl.name, {}).get(dominant), "algorithmic_bytes": dom_bytes,
-                         "kernel_ms": dom_ms},
+            "roofline": roofline,
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
@@ -350,7 +360,7 @@ def run_bands(args, wl):
     # the band's own work (one graph, no communication) and the all-reduce alone, per rank
     local_ms = time_graph(step.local_graph, max(5, min(50, args.steps)), flush)
     stage_ms = {}
-    for s_ in (("_forward",), ("_backward",)) if not args.no_stages else ():
+    for s_ in (("_raster",),) if not args.no_stages else ():
         g = step._capture(s_)
         stage_ms[s_[0].strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g
@@ -392,14 +402,7 @@ def run_bands(args, wl):
         p = step.band_h * wl.width
         roofline = None
         if stage_ms:
-            fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + band_isect * 4 + n * 4 * (5 + c)
-            bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
-            dominant = max(("forward", "backward"), key=lambda s_: stage_ms[s_])
-            dom_bytes = fwd_bytes if dominant == "forward" else bwd_bytes
-            achieved = dom_bytes / (stage_ms[dominant] * 1e-3) / 1e9
-            roofline = {"bound": "hbm", "kernel": f"raster_{dominant} (rank 0's band)", "achieved": achieved, "peak": hbm_peak,
-                        "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
-                        "algorithmic_bytes": dom_bytes, "kernel_ms": stage_ms[dominant]}
+            roofline = raster_roofline(stage_ms, p, c, n, k, band_isect, step.num_tiles, hbm_peak, peak_kind, None, " (rank 0's band)")
         total_evals = float(evals.item())
         out = {
             "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

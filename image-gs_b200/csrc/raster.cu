@@ -77,6 +77,12 @@ __device__ __forceinline__ void column_sigma(const float4 g4, const float hc, co
     }
 }
 
+// sigma of one pixel from a Gaussian's centre and halved conic (g4 = x, y, a / 2, b; hc = c / 2), as column_sigma
+__device__ __forceinline__ float halved_sigma(const float4 g4, const float hc, const float px, const float py) {
+    const float dx = __fsub_rn(g4.x, px), dy = __fsub_rn(g4.y, py);
+    return __fmaf_rn(__fmul_rn(g4.w, dx), dy, __fmaf_rn(__fmul_rn(g4.z, dx), dx, __fmul_rn(__fmul_rn(hc, dy), dy)));
+}
+
 // The top-K selection of PPT pixels per thread over their tile's list (range into ids_sorted), in list order, with the slot rule of the
 // reference: free slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it.
 // The first ten entries fill the slots with fixed indices when all of them are valid for a pixel (what the rule does while slots are
@@ -581,132 +587,39 @@ struct PairSmem {
     int wsum[kThreads / 32];
 };
 
-template <int C, int NV>
-__global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
-    raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h,
-        const int channels_rt, const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
-        const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
-        const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
-    igs::wait_for_predecessor();
-    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
-    static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry sums and the channels");
-    const int channels = C > 0 ? C : channels_rt;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    PairSmem<kMaxC> &sm = *reinterpret_cast<PairSmem<kMaxC> *>(smem_raw);
+// Stage entries [chunk, chunk + kPairStage) of a tile's list for the backward pass (every thread of the CTA calls it): centres, the conic
+// halved as the selection stages it (a / 2, b, c / 2) and the colours
+template <int kMaxC>
+__device__ __forceinline__ void stage_pair_chunk(PairSmem<kMaxC> &sm, const int chunk, const int len, const int2 range,
+                                                 const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
+                                                 const float *__restrict__ conics, const float *__restrict__ colors, const int channels) {
+    const int n = min(kPairStage, len - chunk);
+    for (int e = threadIdx.x; e < n; e += kThreads) {
+        const int g = __ldg(&ids_sorted[range.x + chunk + e]);
+        const float2 xy = __ldg(&xys[g]);
+        sm.geo[e] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+        sm.cc[e] = 0.5f * __ldg(&conics[3 * g + 2]);
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+    }
+}
 
-    const int tile = blockIdx.x;
-    const int2 range = tile_bins[tile];
-    const int len = range.y - range.x;
-    if (len <= 0) return;
+// Steps 2 and 3 of the pairs-grouped backward pass for one tile (every thread of the CTA calls it): sm.vw, sm.vout and sm.pxy hold step
+// 1's per-pair and per-pixel values, key[k] the list position of the thread's slot k (-1 empty). The staged chunk of the list is used for
+// chunk 0 unless restage_first; every other chunk is staged by stage(chunk).
+template <int NV, int kMaxC, typename Stage>
+__device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const int (&key)[kTopK], const int len, const int2 range,
+                                                   const int *__restrict__ ids_sorted, const int channels, const bool restage_first,
+                                                   Stage stage, float *__restrict__ v_xy, float *__restrict__ v_conic,
+                                                   float *__restrict__ v_colors) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
-    const bool inside = pc.i < img_h && pc.j < img_w;
-    const float px = (float)pc.j, py = (float)pc.i;
-    const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
-    const int p = inside ? (pc.i - row_begin * kTile) * img_w + pc.j : 0;
-
-    // the pixel's loads, issued before the staging barrier so that their latency overlaps it
-    float v_out[kMaxC];
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
-    int key[kTopK];
-    if (len < (int)kNoSlot) {
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            // empty (kNoSlot) or, in lists not written by the forward pass, past the end of the list: no entry
-            const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
-            key[k] = (int)v < len ? (int)v : -1;
-        }
-    } else {
-        // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
-        const PixelCoord pcs[1] = {pc};
-        const bool ins[1] = {inside};
-        float val[1][kTopK];
-        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and values
-        float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
-        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
-        __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
-    }
-
-    // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
-    // memory in step 1)
-    auto stage = [&](int chunk) {
-        const int n = min(kPairStage, len - chunk);
-        for (int e = tid; e < n; e += kThreads) {
-            const int g = __ldg(&ids_sorted[range.x + chunk + e]);
-            const float2 xy = __ldg(&xys[g]);
-            sm.geo[e] = make_float4(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            sm.cc[e] = __ldg(&conics[3 * g + 2]);
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
-        }
-    };
-    stage(0);
-    sm.pxy[tid] = make_float2(px, py);
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
-    __syncthreads();
-
-    // 1. per-pixel gradients with respect to sigma and the colour weights (the reference's algebra, backward.cu:219-265, its divisions
-    //    by denom written as products with two reciprocals computed once)
-    float d[kTopK], s[kTopK];
-    float denom = (float)igs::kNormEps;
-    if (len <= kPairStage) {
-        // the whole list is staged: every slot reads shared memory
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            d[k] = 0.f, s[k] = 0.f;
-            if (key[k] < 0) continue;
-            const int e = key[k];
-            const float4 q = sm.geo[e];
-            d[k] = __expf(-igs::gaussian_sigma(q.x, q.y, q.z, q.w, sm.cc[e], px, py));
-            denom += d[k];
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += sm.col[e * kMaxC + c] * v_out[c];
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            d[k] = 0.f, s[k] = 0.f;
-            if (key[k] < 0) continue;
-            float gx, gy, a, b, c;
-            if (key[k] < kPairStage) {
-                const float4 q = sm.geo[key[k]];
-                gx = q.x, gy = q.y, a = q.z, b = q.w, c = sm.cc[key[k]];
-#pragma unroll
-                for (int ch = 0; ch < kMaxC; ++ch)
-                    if (ch < channels) s[k] += sm.col[key[k] * kMaxC + ch] * v_out[ch];
-            } else {
-                const int g = __ldg(&ids_sorted[range.x + key[k]]);
-                const float2 xy = __ldg(&xys[g]);
-                gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
-#pragma unroll
-                for (int ch = 0; ch < kMaxC; ++ch)
-                    if (ch < channels) s[k] += __ldg(&colors[(size_t)g * channels + ch]) * v_out[ch];
-            }
-            d[k] = __expf(-igs::gaussian_sigma(gx, gy, a, b, c, px, py));
-            denom += d[k];
-        }
-    }
-    // fast-math division is a product with the approximate reciprocal, so the reference's x / denom and x / (denom * denom) are these
-    // products, in its order of operations
-    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
-    float shared = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
-
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
     const int lane_of_x = 3 * (32 / NV), lane_of_y = 4 * (32 / NV);  // lanes holding S_x and S_y after the reduce-scatter
     for (int chunk = 0; chunk < len; chunk += kPairStage) {
         const int n_entries = min(kPairStage, len - chunk);
-        if (chunk > 0) {
+        if (chunk > 0 || restage_first) {
             __syncthreads();  // the previous chunk's pairs and parameters are consumed
             stage(chunk);
             __syncthreads();
@@ -806,10 +719,10 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
                     value = value_index == 1 ? total : 0.5f * total;
                     target = v_conic + 3 * (size_t)g + value_index;
                 } else if (value_index == 3) {
-                    value = q.z * sx + q.w * sy;
+                    value = (2.f * q.z) * sx + q.w * sy;  // the staged conic is halved; doubling it back is exact
                     target = v_xy + 2 * (size_t)g;
                 } else if (value_index == 4) {
-                    value = q.w * sx + sm.cc[e] * sy;
+                    value = q.w * sx + (2.f * sm.cc[e]) * sy;
                     target = v_xy + 2 * (size_t)g + 1;
                 } else {
                     value = total;
@@ -819,6 +732,260 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
             }
         }
     }
+}
+
+template <int C, int NV>
+__global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
+    raster_bwd_pairs_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h,
+        const int channels_rt, const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
+        const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
+        const uint16_t *__restrict__ tile_topk, float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
+    igs::wait_for_predecessor();
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
+    static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry sums and the channels");
+    const int channels = C > 0 ? C : channels_rt;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    PairSmem<kMaxC> &sm = *reinterpret_cast<PairSmem<kMaxC> *>(smem_raw);
+
+    const int tile = blockIdx.x;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+    if (len <= 0) return;
+    const int tid = threadIdx.x;
+    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const float px = (float)pc.j, py = (float)pc.i;
+    const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
+    const int p = inside ? (pc.i - row_begin * kTile) * img_w + pc.j : 0;
+
+    // the pixel's loads, issued before the staging barrier so that their latency overlaps it
+    float v_out[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) v_out[c] = (inside && c < channels) ? __ldg(&v_output[(size_t)c * num_pixels + p]) : 0.f;
+    int key[kTopK];
+    if (len < (int)kNoSlot) {
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            // empty (kNoSlot) or, in lists not written by the forward pass, past the end of the list: no entry
+            const uint16_t v = inside ? __ldg(&tile_topk[((size_t)tile * kTopK + k) * kThreads + tid]) : kNoSlot;
+            key[k] = (int)v < len ? (int)v : -1;
+        }
+    } else {
+        // a list too long for 16-bit positions: select the pixel's top-K again, exactly as the forward pass did
+        const PixelCoord pcs[1] = {pc};
+        const bool ins[1] = {inside};
+        float val[1][kTopK];
+        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and values
+        float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
+        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
+        __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
+    }
+
+    // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
+    // memory in step 1)
+    auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
+    stage(0);
+    sm.pxy[tid] = make_float2(px, py);
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+    __syncthreads();
+
+    // 1. per-pixel gradients with respect to sigma and the colour weights (the reference's algebra, backward.cu:219-265, its divisions
+    //    by denom written as products with two reciprocals computed once)
+    float d[kTopK], s[kTopK];
+    float denom = (float)igs::kNormEps;
+    if (len <= kPairStage) {
+        // the whole list is staged: every slot reads shared memory
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            d[k] = 0.f, s[k] = 0.f;
+            if (key[k] < 0) continue;
+            const int e = key[k];
+            const float4 q = sm.geo[e];
+            d[k] = __expf(-halved_sigma(q, sm.cc[e], px, py));
+            denom += d[k];
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += sm.col[e * kMaxC + c] * v_out[c];
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            d[k] = 0.f, s[k] = 0.f;
+            if (key[k] < 0) continue;
+            float gx, gy, a, b, c;
+            if (key[k] < kPairStage) {
+                const float4 q = sm.geo[key[k]];
+                gx = q.x, gy = q.y, a = 2.f * q.z, b = q.w, c = 2.f * sm.cc[key[k]];
+#pragma unroll
+                for (int ch = 0; ch < kMaxC; ++ch)
+                    if (ch < channels) s[k] += sm.col[key[k] * kMaxC + ch] * v_out[ch];
+            } else {
+                const int g = __ldg(&ids_sorted[range.x + key[k]]);
+                const float2 xy = __ldg(&xys[g]);
+                gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
+#pragma unroll
+                for (int ch = 0; ch < kMaxC; ++ch)
+                    if (ch < channels) s[k] += __ldg(&colors[(size_t)g * channels + ch]) * v_out[ch];
+            }
+            d[k] = __expf(-igs::gaussian_sigma(gx, gy, a, b, c, px, py));
+            denom += d[k];
+        }
+    }
+    // fast-math division is a product with the approximate reciprocal, so the reference's x / denom and x / (denom * denom) are these
+    // products, in its order of operations
+    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
+    float shared = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
+
+    pairs_grouped_sums<NV>(sm, key, len, range, ids_sorted, channels, false, stage, v_xy, v_conic, v_colors);
+}
+
+// ---- the training step's rasterization in one kernel -------------------------------------------------------------------------------
+//
+// With the L1 loss, the gradient with respect to the image, sign(image - target) * ratio / numel, is known as soon as a pixel's value is.
+// So one CTA per tile (256 threads, one pixel each) runs the forward and the backward pass of its tile back to back:
+//   * the top-K selection (select_topk, slots in sm.vw's space), the normalized sum, the image, the tile's part of the loss and the
+//     pixel's loss gradient;
+//   * the backward's step 1 from the selection's alphas and list positions (the backward pass recomputes the same alphas bit for bit),
+//     then steps 2 and 3 (pairs_grouped_sums) on the list still staged in shared memory.
+// Neither the top-K lists nor the image gradient go through HBM, and each slot's alpha is computed once.
+template <int C, int NV>
+__global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
+    raster_step_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h, const int channels_rt,
+        const int *__restrict__ ids_sorted, const int2 *__restrict__ tile_bins, const float2 *__restrict__ xys,
+        const float *__restrict__ conics, const float *__restrict__ colors, const FusedL1 l1, float *__restrict__ out_img,
+        float *__restrict__ v_xy, float *__restrict__ v_conic, float *__restrict__ v_colors) {
+    igs::wait_for_predecessor();
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
+    static_assert(5 + kMaxC <= NV, "NV must hold the 5 geometry sums and the channels");
+    const int channels = C > 0 ? C : channels_rt;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    PairSmem<kMaxC> &sm = *reinterpret_cast<PairSmem<kMaxC> *>(smem_raw);
+
+    const int tile = blockIdx.x;
+    const int2 range = tile_bins[tile];
+    const int len = range.y - range.x;
+    const int tid = threadIdx.x;
+    const PixelCoord pc = tile_pixel(tile, tiles_x, row_begin);
+    const bool inside = pc.i < img_h && pc.j < img_w;
+    const int num_pixels = band_h * img_w;  // one channel plane of the (band of the) image
+    const int p = inside ? (pc.i - row_begin * kTile) * img_w + pc.j : 0;
+
+    // 1. forward: the top-K selection; a one-chunk list keeps its staged geometry and gets its colours staged beside it
+    int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and alphas
+    float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
+    const PixelCoord pcs[1] = {pc};
+    const bool ins[1] = {inside};
+    float val[1][kTopK];
+    select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
+    int key[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
+    const bool one_chunk = len <= kPairStage;
+    if (one_chunk) {
+        for (int e = tid; e < len; e += kThreads) {
+            const int g = __ldg(&ids_sorted[range.x + e]);
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+        }
+        __syncthreads();
+    }
+
+    // 2. the pixel's value (normalized in double, as the reference), the image, the L1 loss and its gradient
+    float target[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) target[c] = (inside && c < channels) ? __ldcs(&l1.target[(size_t)c * num_pixels + p]) : 0.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+        if (key[k] >= 0) sum += val[0][k];
+    const double inv_sum = 1.0 / ((double)sum + igs::kNormEps);
+    float pix[kMaxC];
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        if (key[k] < 0) continue;
+        const float vis = (float)((double)val[0][k] * inv_sum);
+        if (one_chunk) {
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) pix[c] += sm.col[key[k] * kMaxC + c] * vis;
+        } else {
+            const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+        }
+    }
+    float v_out[kMaxC];
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) {
+        v_out[c] = 0.f;
+        if (!inside || c >= channels) continue;
+        out_img[(size_t)c * num_pixels + p] = pix[c];
+        const float d = pix[c] - target[c];
+        acc += fabsf(d);
+        v_out[c] = l1_sign(d) * l1.grad_value;
+        if (l1.v_output != nullptr) __stcs(&l1.v_output[(size_t)c * num_pixels + p], v_out[c]);
+    }
+    const float total = cta_sum(acc, reinterpret_cast<float *>(sm.wsum));  // its barriers also end every read of the slots
+    if (tid == 0) l1.partials[tile] = total;
+    if (len <= 0) return;
+
+    // 3. backward, step 1 (the reference's algebra, backward.cu:219-265, as raster_bwd_pairs_kernel) from the selection's alphas
+    float d[kTopK], s[kTopK];
+    float denom = (float)igs::kNormEps;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        d[k] = 0.f, s[k] = 0.f;
+        if (key[k] < 0) continue;
+        d[k] = val[0][k];
+        denom += d[k];
+        if (one_chunk) {
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
+        } else {
+            const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c)
+                if (c < channels) s[k] += __ldg(&f[c]) * v_out[c];
+        }
+    }
+    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
+    float shared = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
+    sm.pxy[tid] = make_float2((float)pc.j, (float)pc.i);
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+
+    // 4. backward, steps 2 and 3
+    auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
+    pairs_grouped_sums<NV>(sm, key, len, range, ids_sorted, channels, !one_chunk, stage, v_xy, v_conic, v_colors);
+}
+
+template <int C, int NV>
+cudaError_t launch_step(int tiles, int tiles_x, int img_h, int img_w, int row_begin, int band_h, int channels, const int *ids,
+                        const int2 *bins, const float2 *xys, const float *conics, const float *colors, const FusedL1 &l1, float *out_img,
+                        float *v_xy, float *v_conic, float *v_colors, cudaStream_t s) {
+    constexpr int kMaxC = C > 0 ? C : (NV - 5 < kMaxChannels ? NV - 5 : kMaxChannels);
+    const size_t bytes = sizeof(PairSmem<kMaxC>);
+    cudaError_t err = cudaFuncSetAttribute(raster_step_kernel<C, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err != cudaSuccess) return err;
+    return igs::launch(raster_step_kernel<C, NV>, tiles, kThreads, bytes, s, tiles_x, img_h, img_w, row_begin, band_h, channels, ids, bins,
+                       xys, conics, colors, l1, out_img, v_xy, v_conic, v_colors);
 }
 
 template <int C>
@@ -877,6 +1044,17 @@ cudaError_t launch_bwd_pairs(int tiles, int tiles_x, int img_h, int img_w, int r
                        bins, xys, conics, colors, v_output, tile_topk, v_xy, v_conic, v_colors);
 }
 
+// The backward kernels accumulate with atomics: zero the gradients first, with one memset when v_xy, v_conic and v_colors are one block
+cudaError_t zero_gradients(int num_points, int channels, float *v_xy, float *v_conic, float *v_colors, cudaStream_t s) {
+    const size_t n = (size_t)num_points;
+    if (v_conic == v_xy + 2 * n && (channels == 0 || v_colors == v_conic + 3 * n))
+        return cudaMemsetAsync(v_xy, 0, sizeof(float) * (5 + (size_t)channels) * n, s);
+    cudaError_t e = cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * n, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * n, s);
+    if (e == cudaSuccess && channels > 0) e = cudaMemsetAsync(v_colors, 0, sizeof(float) * (size_t)channels * n, s);
+    return e;
+}
+
 int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, int num_points, const int32_t *ids_sorted,
                const int32_t *tile_bins, const float *xys,
                const float *conics, const float *colors, const float *v_output, const int32_t *pixel_topk, const uint16_t *tile_topk,
@@ -886,18 +1064,7 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
     cudaStream_t s = igs::as_stream(stream);
     if (num_points > 0) {
         IGS_REQUIRE(v_xy && v_conic && (v_colors || channels == 0), "%s: null gradient pointer", who);
-        // the kernel accumulates with atomics; one memset when the three gradients are one block (v_xy, v_conic, v_colors back to back)
-        const size_t n = (size_t)num_points;
-        const bool block = v_conic == v_xy + 2 * n && (channels == 0 || v_colors == v_conic + 3 * n);
-        cudaError_t e;
-        if (block) {
-            e = cudaMemsetAsync(v_xy, 0, sizeof(float) * (5 + (size_t)channels) * n, s);
-        } else {
-            e = cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * n, s);
-            if (e == cudaSuccess) e = cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * n, s);
-            if (e == cudaSuccess && channels > 0) e = cudaMemsetAsync(v_colors, 0, sizeof(float) * (size_t)channels * n, s);
-        }
-        if (e != cudaSuccess) return igs::check_launch(who);
+        if (zero_gradients(num_points, channels, v_xy, v_conic, v_colors, s) != cudaSuccess) return igs::check_launch(who);
     }
     const int tiles_x = igs::ceil_div(img_w, kTile), tiles_y = igs::ceil_div(img_h, kTile);
     if (row_end < 0) row_end = tiles_y;
@@ -933,6 +1100,52 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
     }
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
     return IGS_OK;
+}
+
+// The fused training step over tile rows [row_begin, row_end) (the whole image: 0, tiles_y): image, loss, gradients
+int raster_step(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, int num_points,
+                const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics, const float *colors,
+                const float *target, float ratio, float *out_img, float *loss, float *v_output, float *v_xy, float *v_conic, float *v_colors,
+                void *workspace, size_t workspace_bytes, void *stream, const char *who) {
+    IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && img_h >= 0 && img_w >= 0 && num_points >= 0, "%s: negative size", who);
+    IGS_REQUIRE(channels >= 1 && channels <= kMaxChannels, "%s: 1 to %d channels (got %d)", who, kMaxChannels, channels);
+    IGS_REQUIRE(tiles_x == igs::ceil_div(img_w, kTile) && tiles_y == igs::ceil_div(img_h, kTile),
+                "%s: tile grid %dx%d does not cover a %dx%d image with %dx%d tiles", who, tiles_x, tiles_y, img_w, img_h, kTile, kTile);
+    IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
+                row_end, tiles_y);
+    const int tiles = tiles_x * (row_end - row_begin);
+    IGS_REQUIRE(loss != nullptr, "%s: null loss", who);
+    IGS_REQUIRE(num_points == 0 || (v_xy && v_conic && v_colors), "%s: null gradient pointer", who);
+    cudaStream_t s = igs::as_stream(stream);
+    if (num_points > 0 && zero_gradients(num_points, channels, v_xy, v_conic, v_colors, s) != cudaSuccess) return igs::check_launch(who);
+    if (tiles == 0) {  // no pixels (an empty band): no loss, zero gradients
+        if (cudaMemsetAsync(loss, 0, sizeof(float), s) != cudaSuccess) return igs::check_launch(who);
+        return IGS_OK;
+    }
+    IGS_REQUIRE(tile_bins && xys && conics && colors && target && out_img && workspace, "%s: null pointer", who);
+    IGS_REQUIRE(num_points == 0 || ids_sorted, "%s: null gaussian_ids_sorted", who);
+    IGS_REQUIRE(igs::aligned(tile_bins, 8) && igs::aligned(xys, 8), "%s: tile_bins and xys must be 8-byte aligned", who);
+    IGS_REQUIRE(workspace_bytes >= igs_raster_l1_workspace(tiles), "%s: workspace too small (%zu bytes, need %zu)", who, workspace_bytes,
+                igs_raster_l1_workspace(tiles));
+    IGS_REQUIRE(igs::aligned(workspace, 16), "%s: workspace must be 16-byte aligned", who);
+    const float numel = (float)((int64_t)channels * img_h * img_w);
+    FusedL1 l1;
+    l1.target = target;
+    l1.v_output = v_output;
+    l1.grad_value = ratio / numel;
+    l1.partials = static_cast<float *>(workspace);
+    const int band_h = std::min(img_h, row_end * kTile) - row_begin * kTile;
+    const auto launch = channels == 3    ? launch_step<3, 8>
+                        : channels <= 3  ? launch_step<0, 8>
+                        : channels == 9  ? launch_step<9, 16>
+                        : channels <= 11 ? launch_step<0, 16>
+                                         : launch_step<0, 32>;
+    const cudaError_t err = launch(tiles, tiles_x, img_h, img_w, row_begin, band_h, channels, ids_sorted,
+                                   reinterpret_cast<const int2 *>(tile_bins), reinterpret_cast<const float2 *>(xys), conics, colors, l1,
+                                   out_img, v_xy, v_conic, v_colors, s);
+    if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+    igs::launch(l1_finish_kernel, 1, kFinishThreads, 0, s, l1.partials, tiles, ratio, numel, loss);
+    return igs::check_launch(who);
 }
 
 }  // namespace
@@ -1027,6 +1240,25 @@ int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin,
     IGS_REQUIRE(row_end >= 0, "igs_raster_bwd_topk_tiles_band: negative row_end");
     return raster_bwd(img_height, img_width, row_begin, row_end, channels, num_points, gaussian_ids_sorted, tile_bins, xys, conics, colors,
                       v_output_band, nullptr, tile_topk, v_xy, v_conic, v_colors, stream, "igs_raster_bwd_topk_tiles_band");
+}
+
+int igs_raster_step_l1_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                            int num_points, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                            const float *conics, const float *colors, const float *target, float ratio, float *out_img, float *loss,
+                            float *v_output, float *v_xy, float *v_conic, float *v_colors, void *workspace, size_t workspace_bytes,
+                            void *stream) {
+    return raster_step(tiles_x, tiles_y, img_height, img_width, row_begin, row_end, channels, num_points, gaussian_ids_sorted, tile_bins,
+                       xys, conics, colors, target, ratio, out_img, loss, v_output, v_xy, v_conic, v_colors, workspace, workspace_bytes,
+                       stream, "igs_raster_step_l1_band");
+}
+
+int igs_raster_step_l1(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int num_points,
+                       const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                       const float *colors, const float *target, float ratio, float *out_img, float *loss, float *v_output, float *v_xy,
+                       float *v_conic, float *v_colors, void *workspace, size_t workspace_bytes, void *stream) {
+    return raster_step(tiles_x, tiles_y, img_height, img_width, 0, tiles_y, channels, num_points, gaussian_ids_sorted, tile_bins, xys,
+                       conics, colors, target, ratio, out_img, loss, v_output, v_xy, v_conic, v_colors, workspace, workspace_bytes, stream,
+                       "igs_raster_step_l1");
 }
 
 }  // extern "C"

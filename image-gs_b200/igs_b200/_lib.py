@@ -32,6 +32,10 @@ SIGNATURES = {
     "igs_raster_fwd_topk_tiles_l1": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P, P, P, c_size_t, P]),
     "igs_raster_bwd_topk": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     "igs_raster_bwd_topk_tiles": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
+    "igs_raster_step_l1": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P, P, P, P, P, c_size_t,
+                                   P]),
+    "igs_raster_step_l1_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P,
+                                        P, P, P, P, c_size_t, P]),
     "igs_band_tiles_hit": (c_int, [c_int, P, P, c_int, c_int, c_int, c_int, P, P]),
     "igs_sort_intersects_band": (c_int, [c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
     "igs_raster_fwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),

@@ -71,8 +71,9 @@ class BandStep:
     single band, no communication)."""
 
     def __init__(self, means, scales, rotations, features, target, img_h, img_w, row_begin, row_end, group=None, capacity=None,
-                 capacity_ratio: float = 2.0, l1_ratio: float = 1.0):
+                 capacity_ratio: float = 2.0, l1_ratio: float = 1.0, fused: bool = True):
         self.lib = _lib.load()
+        self.fused = fused  # the band's forward, loss and backward in one kernel (igs_raster_step_l1_band); else two kernels
         self.device = means.device
         self.n, self.c = features.shape
         self.h, self.w = img_h, img_w
@@ -97,7 +98,7 @@ class BandStep:
         self.cum_ws_bytes = self.lib.igs_cumsum_workspace(n)
         self.cum_ws = torch.empty(self.cum_ws_bytes, device=dev, dtype=torch.uint8)
         self.image = torch.empty(nc, self.band_h, img_w, device=dev, dtype=f32)
-        self.v_image = torch.empty_like(self.image)
+        self.v_image = None if fused else torch.empty_like(self.image)
         # the band's loss is its share of the whole image's, ratio * sum over the band |d| / (C H W), computed by the forward kernel
         self.l1_ratio = float(l1_ratio)
         self.l1_ws_bytes = self.lib.igs_raster_l1_workspace(max(1, self.num_tiles))
@@ -122,7 +123,7 @@ class BandStep:
         self.sort_ws_bytes = self.lib.igs_sort_workspace(self.capacity, self.tb[0], self.r1 - self.r0)
         self.sort_ws = torch.empty(self.sort_ws_bytes, device=dev, dtype=torch.uint8)
         self.max_list = min(self.n, self.capacity)
-        self.topk = torch.empty(max(1, self.num_tiles), TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        self.topk = None if fused else torch.empty(max(1, self.num_tiles), TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
         self.local_graph = self.final_graph = None
 
     def _stream(self):
@@ -143,6 +144,12 @@ class BandStep:
         _lib.check(self.lib.igs_sort_intersects_band(self.n, self.capacity, ptr(self.xys), ptr(self.radii), ptr(self.cum), self.tb[0],
                                                      self.tb[1], self.r0, self.r1, ptr(self.ids), ptr(self.bins), ptr(self.sort_ws),
                                                      self.sort_ws_bytes, self._stream()), "bin")
+
+    def _raster(self):
+        _lib.check(self.lib.igs_raster_step_l1_band(self.tb[0], self.tb[1], self.h, self.w, self.r0, self.r1, self.c, self.n, ptr(self.ids),
+                                                    ptr(self.bins), ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.target),
+                                                    self.l1_ratio, ptr(self.image), ptr(self.loss), None, ptr(self.v_xy), ptr(self.v_conic),
+                                                    ptr(self.v_colors), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "raster step")
 
     def _forward(self):
         if self.num_tiles == 0:
@@ -165,8 +172,11 @@ class BandStep:
                                             ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                             ptr(self.v_rot), self._stream()), "project_backward")
 
-    LOCAL = ("_project", "_cumsum", "_bin", "_forward", "_backward")
-    KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_forward": 2, "_backward": 1, "_project_backward": 1}
+    KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_raster": 2, "_forward": 2, "_backward": 1, "_project_backward": 1}
+
+    @property
+    def LOCAL(self):
+        return ("_project", "_cumsum", "_bin") + (("_raster",) if self.fused else ("_forward", "_backward"))
 
     def all_reduce(self):
         if self.group is not None:
@@ -202,7 +212,7 @@ class BandStep:
 
     @property
     def kernels_per_step(self):
-        return sum(self.KERNELS.values())
+        return sum(self.KERNELS[s] for s in self.LOCAL + ("_project_backward",))
 
     def gaussian_pixel_evals(self):
         """Forward evaluations of the band: sum over its tiles of list length x in-image pixels of the tile."""

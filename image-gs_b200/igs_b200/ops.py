@@ -180,6 +180,35 @@ def nd_rasterize_forward_topk_norm_tiles_l1(tile_bounds, img_size, max_list_len,
     return out_img, tile_topk, loss, v_output
 
 
+def raster_step_l1(tile_bounds, img_size, gaussian_ids_sorted, tile_bins, xys, conics, colors, target, ratio=1.0, with_v_output=False):
+    """The training step's rasterization with the L1 loss in one kernel (igs_raster_step_l1): out_img [C,H,W], loss = ratio *
+    mean|out_img - target|, and the gradients of the loss v_xy [N,2], v_conic [N,3], v_colors [N,C] (plus v_output, the loss's gradient
+    with respect to out_img, when with_v_output), as nd_rasterize_forward_topk_norm_tiles_l1 followed by
+    nd_rasterize_backward_topk_norm_tiles would give them."""
+    h, w = _check_raster_geometry(tile_bounds, (TILE, TILE, 1), img_size)
+    channels = colors.size(1)
+    _check_input(target, "target", torch.float32)
+    if tuple(target.shape) != (channels, h, w):
+        raise RuntimeError(f"target must be [{channels}, {h}, {w}]")
+    n = xys.size(0)
+    dev = xys.device
+    num_tiles = int(tile_bounds[0]) * int(tile_bounds[1])
+    lib = _lib.load()
+    out_img = torch.empty(channels, h, w, device=dev, dtype=torch.float32)
+    v_output = torch.empty_like(out_img) if with_v_output else None
+    loss = torch.empty((), device=dev, dtype=torch.float32)
+    grads = torch.empty(n * (5 + channels), device=dev, dtype=torch.float32)
+    v_xy, v_conic, v_colors = grads[:2 * n].view(n, 2), grads[2 * n:5 * n].view(n, 3), grads[5 * n:].view(n, channels)
+    ws_bytes = lib.igs_raster_l1_workspace(num_tiles)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib_call("igs_raster_step_l1", int(tile_bounds[0]), int(tile_bounds[1]), h, w, channels, n, ptr(gaussian_ids_sorted),
+                  ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors), ptr(target), float(ratio), ptr(out_img), ptr(loss), ptr(v_output),
+                  ptr(v_xy), ptr(v_conic), ptr(v_colors), ptr(ws), ws_bytes, stream_of(dev))
+    out = (out_img, loss, v_xy, v_conic, v_colors)
+    return out + (v_output,) if with_v_output else out
+
+
 def nd_rasterize_backward_topk_norm(img_height, img_width, BLOCK_H, BLOCK_W, xys, conics, colors, v_output, pixel_topk):
     """-> v_xy [N,2], v_conic [N,3], v_colors [N,C] (bindings.cu:444-502); v_output channel-planar [C,H,W]."""
     for t, n in ((xys, "xys"), (conics, "conics"), (colors, "colors"), (v_output, "v_output")):

@@ -5,6 +5,9 @@ path of Image-GS's CUDA-graph step (model.py:1160-1209) for the hot path only:
     [quantize-STE] -> project -> prefix sum -> tile binning -> top-K forward -> L1 loss + gradient -> top-K backward -> projection backward
     [-> rate term forward/backward]
 
+The top-K forward, the L1 loss with its gradient and the top-K backward run as one kernel per tile (igs_raster_step_l1), so the top-K
+lists and the image gradient never go through HBM; fused=False runs them as the separate forward (with the loss) and backward kernels.
+
 The intersection buffers hold `capacity` entries (capacity_ratio times the count of the first step, at least 1024, as model.py:110,1186),
 so nothing is read back to the host inside the step; the true count is kept on the device (num_intersects) for overflow checks.
 """
@@ -24,10 +27,13 @@ class RasterStep:
     """One image's step. Inputs are device tensors: means [N,2], scales [N,2] (pixels), rotations [N,1], features [N,C], target [C,H,W]."""
 
     def __init__(self, means, scales, rotations, features, target, capacity: Optional[int] = None, capacity_ratio: float = 2.0,
-                 l1_ratio: float = 1.0, quant: Optional[dict] = None, loss_transform=None, rate: Optional[dict] = None):
+                 l1_ratio: float = 1.0, quant: Optional[dict] = None, loss_transform=None, rate: Optional[dict] = None,
+                 fused: bool = True):
         """quant: dict(pos_steps [2], scale_step, rot_step, feat_steps [C]) puts the straight-through quantizer in front (scales must be
         the canonical, non-negative ones); loss_transform [C,C]: render feat T^T (YUV loss space, needs quant); rate: dict(model (the
-        fields of compress.rate.RateModel), inv_rot_step, factor) adds the rate term on the raw features and rotations."""
+        fields of compress.rate.RateModel), inv_rot_step, factor) adds the rate term on the raw features and rotations. fused=False:
+        separate forward and backward kernels, with the top-K lists and the image gradient (v_image) kept in HBM."""
+        self.fused = fused
         self.lib = _lib.load()
         self.device = means.device
         self.n, self.c = features.shape
@@ -60,7 +66,7 @@ class RasterStep:
         self.cum_ws_bytes = self.lib.igs_cumsum_workspace(n)
         self.cum_ws = torch.empty(self.cum_ws_bytes, device=dev, dtype=torch.uint8)
         self.image = torch.empty(nc, self.h, self.w, device=dev, dtype=f32)
-        self.v_image = torch.empty_like(self.image)
+        self.v_image = None if fused else torch.empty_like(self.image)
         self.loss = torch.empty((), device=dev, dtype=f32)
         self.l1_ws_bytes = self.lib.igs_raster_l1_workspace(self.num_tiles)
         self.l1_ws = torch.zeros(self.l1_ws_bytes, device=dev, dtype=torch.uint8)
@@ -81,8 +87,9 @@ class RasterStep:
         self.sort_ws_bytes = self.lib.igs_sort_workspace(self.capacity, self.tb[0], self.tb[1])
         self.sort_ws = torch.empty(self.sort_ws_bytes, device=dev, dtype=torch.uint8)
         self.max_list = min(self.n, self.capacity)
-        # top-K lists in the 16-bit tile-list form (tiles with 65535+ entries are selected again by the backward pass)
-        self.topk = torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        # top-K lists in the 16-bit tile-list form between the separate kernels (tiles with 65535+ entries are selected again by the
+        # backward pass)
+        self.topk = None if fused else torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
         if self.rate is not None:
             m = self.rate["model"]
             self.rate_loss = torch.empty((), device=dev, dtype=f32)
@@ -151,6 +158,13 @@ class RasterStep:
                                                  ptr(self.ids), ptr(self.bins), ptr(self.sort_ws), self.sort_ws_bytes, self._stream()),
                     "bin")
 
+    def _raster(self):
+        """Render, the L1 loss and its gradient, and the top-K backward pass, in one kernel per tile."""
+        self._check(self.lib.igs_raster_step_l1(self.tb[0], self.tb[1], self.h, self.w, self.c, self.n, ptr(self.ids), ptr(self.bins),
+                                                ptr(self.xys), ptr(self.conics), ptr(self.features), ptr(self.target), self.l1_ratio,
+                                                ptr(self.image), ptr(self.loss), ptr(self.v_image), ptr(self.v_xy), ptr(self.v_conic),
+                                                ptr(self.v_colors), ptr(self.l1_ws), self.l1_ws_bytes, self._stream()), "raster step")
+
     def _forward(self):
         """Render, with the L1 loss and its gradient with respect to the image computed in the same kernel."""
         self._check(self.lib.igs_raster_fwd_topk_tiles_l1(self.tb[0], self.tb[1], self.h, self.w, self.c, self.max_list, ptr(self.ids),
@@ -168,10 +182,14 @@ class RasterStep:
                                              ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                              ptr(self.v_rot), self._stream()), "project_backward")
 
-    BASE_STAGES = ("_project", "_cumsum", "_bin", "_forward", "_backward", "_project_backward")
     # kernels each stage launches (memsets excluded)
-    KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_forward": 2, "_backward": 1, "_project_backward": 1,
+    KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_raster": 2, "_forward": 2, "_backward": 1, "_project_backward": 1,
                "_rate_term": 2, "_feature_grads": 1}
+
+    @property
+    def BASE_STAGES(self):
+        raster = ("_raster",) if self.fused else ("_forward", "_backward")
+        return ("_project", "_cumsum", "_bin") + raster + ("_project_backward",)
 
     @property
     def STAGES(self):

@@ -105,6 +105,17 @@ int igs_raster_fwd_topk_tiles_l1(int tiles_x, int tiles_y, int img_height, int i
                                  const float *colors, const float *target, float ratio, float *out_img, uint16_t *tile_topk, float *loss,
                                  float *v_output, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The training step's rasterization with the L1 loss in one kernel: the top-K forward pass, loss = ratio * mean|out_img - target| (as
+ * igs_raster_fwd_topk_tiles_l1) and the backward pass of that loss (as igs_raster_bwd_topk_tiles with v_output = the loss's gradient),
+ * per tile back to back, so neither the top-K lists nor the image gradient are written. v_xy [N,2], v_conic [N,3], v_colors [N,C] are
+ * zeroed and accumulated (float atomics); v_output [C,H,W] receives the image gradient when not null. workspace:
+ * igs_raster_l1_workspace(tiles_x * tiles_y) bytes, 16-byte aligned. It replaces, for the L1 training step, the reference's
+ * nd_rasterize_forward_topk_norm + F.l1_loss + nd_rasterize_backward_topk_norm (rasterize_sum.py:14-212 with model.py:1224-1227). */
+int igs_raster_step_l1(int tiles_x, int tiles_y, int img_height, int img_width, int channels, int num_points,
+                       const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics,
+                       const float *colors, const float *target, float ratio, float *out_img, float *loss, float *v_output, float *v_xy,
+                       float *v_conic, float *v_colors, void *workspace, size_t workspace_bytes, void *stream);
+
 /* nd_rasterize_backward_topk_norm (bindings.cu:444-502, kernel backward.cu:187-335): v_output [C,H,W]; outputs v_xy [N,2],
  * v_conic [N,3], v_colors [N,C] are zeroed and accumulated (float atomics: the last bits vary run to run). IDs of pixel_topk outside
  * [0, N) count as empty slots (the reference reads out of bounds for IDs of N or more). */
@@ -123,6 +134,15 @@ int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int n
 /* The tiles of rows [row_begin, row_end) that each Gaussian's rectangle covers: the band's num_tiles_hit, to prefix-sum for its binning */
 int igs_band_tiles_hit(int num_points, const float *xys, const int32_t *radii, int tiles_x, int tiles_y, int row_begin, int row_end,
                        int32_t *num_tiles_hit, void *stream);
+
+/* igs_raster_step_l1 over tile rows [row_begin, row_end): target, out_img and v_output hold the band's rows ([C, band rows, W]), tile_bins
+ * and gaussian_ids_sorted come from igs_sort_intersects_band, and the loss is normalized by the whole image's C * H * W, so the bands'
+ * losses and gradients add up to the whole image's. */
+int igs_raster_step_l1_band(int tiles_x, int tiles_y, int img_height, int img_width, int row_begin, int row_end, int channels,
+                            int num_points, const int32_t *gaussian_ids_sorted, const int32_t *tile_bins, const float *xys,
+                            const float *conics, const float *colors, const float *target, float ratio, float *out_img, float *loss,
+                            float *v_output, float *v_xy, float *v_conic, float *v_colors, void *workspace, size_t workspace_bytes,
+                            void *stream);
 
 /* igs_sort_intersects restricted to tile rows [row_begin, row_end): cum_tiles_hit is the prefix sum of igs_band_tiles_hit; tile_bins
  * [tiles_x * (row_end - row_begin), 2] numbers the band's tiles from its first row; workspace igs_sort_workspace(capacity, tiles_x,

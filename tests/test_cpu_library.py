@@ -58,6 +58,18 @@ def test_invalid_arguments_rejected_on_host():
     assert "tile grid" in lib.igs_last_error().decode()
     assert lib.igs_raster_fwd_topk_tiles(1, 1, 16, 16, 3, -1, null, null, null, null, null, null, fake, null) == 1
     assert "max_list_len" in lib.igs_last_error().decode()
+    assert lib.igs_raster_step_l1(1, 1, 16, 16, 0, 10, null, null, null, null, null, null, 1.0, null, fake, null, null, null, null, null,
+                                  0, null) == 1
+    assert "channels" in lib.igs_last_error().decode()
+    assert lib.igs_raster_step_l1(2, 1, 16, 16, 3, 0, null, null, null, null, null, null, 1.0, null, fake, null, null, null, null, null,
+                                  0, null) == 1
+    assert "tile grid" in lib.igs_last_error().decode()
+    assert lib.igs_raster_step_l1(1, 1, 16, 16, 3, 0, null, null, null, null, null, null, 1.0, null, null, null, null, null, null, null,
+                                  0, null) == 1
+    assert "null loss" in lib.igs_last_error().decode()
+    assert lib.igs_raster_step_l1_band(1, 2, 32, 16, 1, 3, 3, 0, null, null, null, null, null, null, 1.0, null, fake, null, null, null,
+                                       null, null, 0, null) == 1
+    assert "tile rows" in lib.igs_last_error().decode()
     assert lib.igs_sort_intersects(10, 100, null, null, null, 4, 4, null, null, null, 0, null) == 1
     assert lib.igs_quantize_ste(10, 3, null, null, null, null, null, 0.0, 0.1, null, null, null, null, null, null, null, null, null, null,
                                 null, null) == 1

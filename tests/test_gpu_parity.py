@@ -114,6 +114,13 @@ def test_all_stages_vs_reference(name, device, ref_module):
     assert_close_render(ours["image"], ref["image"], what="image")
     for key in ("v_xy", "v_conic", "v_colors", "v_cov2d", "v_mean2d", "v_scale", "v_rot"):
         assert_close_grad(ours[key], ref[key], what=key)
+    # the training step's fused kernel (forward, L1 loss, backward in one) against the reference's kernels with the same loss gradient
+    tb = ops.tile_grid(wl.height, wl.width)
+    f_img, _, f_xy, f_conic, f_colors = ops.raster_step_l1(tb, (wl.width, wl.height, 1), ours["gaussian_ids_sorted"], ours["tile_bins"],
+                                                           ours["xys"], ours["conics"], dinp["features"], dinp["target"])
+    assert torch.equal(f_img, ours["image"])
+    for key, got in (("v_xy", f_xy), ("v_conic", f_conic), ("v_colors", f_colors)):
+        assert_close_grad(got, ref[key], what=key + " (fused step)")
 
 
 @pytest.mark.parametrize("name", ["ragged_120x88", "cfg1_256", "c9_80x64", "c12_40x48", "big_64x64"])
@@ -175,6 +182,12 @@ def test_tile_lists_beyond_16_bit_positions(device, ref_module):
         a = v[("v_xy", "v_conic", "v_colors").index(nm)]
         assert_close_grad(a, ours[nm], what=nm)
         assert_close_grad(a, ref[nm], what=nm + " vs reference")
+    # the fused step kernel keeps 32-bit list positions in shared memory: the same render and gradients without a second selection
+    f_img, _, f_xy, f_conic, f_colors = ops.raster_step_l1(tb, (w, h, 1), ours["gaussian_ids_sorted"], ours["tile_bins"], ours["xys"],
+                                                           ours["conics"], dinp["features"], dinp["target"])
+    assert torch.equal(f_img, ours["image"])
+    for nm, a in (("v_xy", f_xy), ("v_conic", f_conic), ("v_colors", f_colors)):
+        assert_close_grad(a, ref[nm], what=nm + " (fused step) vs reference")
 
 
 def test_capacity_drops_like_reference(device):
