@@ -186,9 +186,10 @@ def time_graph(graph, reps, flush):
 RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the step's raster kernel, from one ncu capture of this workload
-# (`ncu --set full --clock-control none -k regex:raster_step -s 2 -c 2 python bench.py --steps 2 --warmup 3 --no-cpu --no-e2e
-# --no-stages`, caches flushed before each pass); None where no capture was taken
-NCU_TRAFFIC = {}
+# (`ncu --set full --clock-control none -k regex:raster_step -s 2 -c 1 python bench.py --steps 2 --warmup 3 --no-cpu --no-e2e
+# --no-stages`, caches flushed before each pass: the image's 24.9 MB of writes were still in L2 when the kernel ended); None where no
+# capture was taken
+NCU_TRAFFIC = {"cfg3_1080p": 26.994e6 + 0.238e6}
 
 
 def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, traffic, label=""):
@@ -230,7 +231,8 @@ def run_ours(args, wl):
     inp = workloads.make_inputs(wl, image_index=rank if not wl.rate_term else 0)
     d = {k: v.to(device) for k, v in inp.items()}
     target = d["loss_target"] if "loss_target" in d else d["target"]
-    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], target, **step_options(wl, device))
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], target, fused=not args.split,
+                               **step_options(wl, device))
     graph = step.capture()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(args.warmup):
@@ -327,7 +329,8 @@ def run_bands(args, wl):
     per_row = bands.row_intersections(d["means"], d["scales"], d["rotations"], wl.height, wl.width)
     r0, r1 = bands.band_rows(tiles_y, world, rank, [r + 32.0 * tiles_x for r in per_row])
     group = torch.distributed.group.WORLD if world > 1 else None
-    step = bands.BandStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], wl.height, wl.width, r0, r1, group=group)
+    step = bands.BandStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], wl.height, wl.width, r0, r1, group=group,
+                          fused=not args.split)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(args.warmup):
         step.replay()
@@ -360,7 +363,7 @@ def run_bands(args, wl):
     # the band's own work (one graph, no communication) and the all-reduce alone, per rank
     local_ms = time_graph(step.local_graph, max(5, min(50, args.steps)), flush)
     stage_ms = {}
-    for s_ in (("_raster",),) if not args.no_stages else ():
+    for s_ in ((("_forward",), ("_backward",)) if args.split else (("_raster",),)) if not args.no_stages else ():
         g = step._capture(s_)
         stage_ms[s_[0].strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g
@@ -597,6 +600,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
     ap.add_argument("--no-stages", action="store_true", help="skip the per-stage timing")
+    ap.add_argument("--split", action="store_true", help="run the step with the separate top-K forward and backward kernels instead of "
+                    "the fused step kernel (for comparison)")
     ap.add_argument("--aux", action="store_true", help="time the rows around the step (neighbour search, feature weights, LOO) instead")
     args = ap.parse_args()
     wl = workloads.get_workload(args.workload)
