@@ -106,6 +106,8 @@ def dist_setup(gpus):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        # NCCL's own log lines (its version banner at NCCL_DEBUG=WARN) go to stderr: rank 0's stdout is the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     return world, rank, local
 
