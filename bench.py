@@ -431,17 +431,30 @@ def run_bands(args, wl):
 
 def run_step_e2e(args, step, dev_params, inp, device, world, api):
     """The step through the C ABI with host buffers: the Gaussian parameters copied host -> device from pinned memory into the step's
-    input tensors and the loss read back to the host every step."""
+    input tensors and the loss read back to the host every step. For the one-image step the copies are nodes of the step's CUDA graph
+    (one graph launch per step); the bands' step copies around its graphs and its all-reduce."""
     keys = ("means", "scales", "rotations", "features")
     host = [inp[k].pin_memory() for k in keys]
     dev = list(dev_params)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
-    def one():
+    def copy_in():
         for d, h in zip(dev, host):
             d.copy_(h, non_blocking=True)
-        step.replay()
+
+    def copy_out():
         loss_host.copy_(step.loss, non_blocking=True)
+
+    if api == "step":
+        graph = step.capture(before=copy_in, after=copy_out)
+
+        def one():
+            graph.replay()
+    else:
+        def one():
+            copy_in()
+            step.replay()
+            copy_out()
 
     for _ in range(args.warmup):
         one()
@@ -463,7 +476,8 @@ def run_step_e2e(args, step, dev_params, inp, device, world, api):
     return {"value": world * args.steps / (float(t.item()) / 1e3) if api != "bands" else args.steps / (float(t.item()) / 1e3),
             "unit": "steps/s", "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world,
             "api": ("igs_b200.bands.BandStep" if api == "bands" else "igs_b200.pipeline.RasterStep") +
-                   " over the C ABI (host parameters copied in and the loss read back every step)"}
+                   " over the C ABI (host parameters copied in and the loss read back every step" +
+                   (", both copies captured in the step's CUDA graph)" if api == "step" else ")")}
 
 
 def run_e2e(args, wl, inp, device, capacity, world):

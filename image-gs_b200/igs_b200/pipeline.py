@@ -208,19 +208,27 @@ class RasterStep:
     def kernels_per_step(self):
         return sum(self.KERNELS[s] for s in self.STAGES)
 
-    def capture(self, stages=None):
-        """A CUDA graph of the step (or of the given stages)."""
+    def capture(self, stages=None, before=None, after=None):
+        """A CUDA graph of the step (or of the given stages); before() and after() issue extra work around them on the same stream (for
+        example the copies of pinned host parameters in and of the loss out, which then run as nodes of the graph)."""
         stages = stages or self.STAGES
+
+        def issue():
+            if before is not None:
+                before()
+            for s in stages:
+                getattr(self, s)()
+            if after is not None:
+                after()
+
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
-            for s in stages:  # warm-up outside the capture
-                getattr(self, s)()
+            issue()  # warm-up outside the capture
         torch.cuda.current_stream(self.device).wait_stream(stream)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            for s in stages:
-                getattr(self, s)()
+            issue()
         return graph
 
     def replay(self):
