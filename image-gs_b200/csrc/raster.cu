@@ -41,6 +41,8 @@ using igs::kTopK;
 constexpr int kThreads = kTilePixels;  // pixels of a tile (and threads of the backward's CTA)
 constexpr int kChunk = 256;            // list entries staged per round in the forward pass
 constexpr int kPairStage = 256;        // longest tile list of the pairs-grouped backward pass
+// the fused step kernel keeps the selection's last staged chunk for its backward part: both passes stage the same chunks
+static_assert(kChunk == kPairStage, "the forward and backward passes must stage the same chunks of a tile's list");
 constexpr int kPairs = kThreads * kTopK;
 struct PixelCoord {
     int i, j;  // row, column in the image
@@ -578,7 +580,8 @@ struct PairSmem {
     float4 geo[kPairStage];            // x, y, conic a, conic b
     float cc[kPairStage];              // conic c
     float col[kPairStage * kMaxC];     // features
-    float2 vw[kTopK][kThreads];        // (dL/dsigma, colour weight) per slot and pixel
+    float2 vw[kTopK][kThreads];        // (dL/dsigma, colour weight) per slot and pixel; in the fused step kernel first the
+                                       // selection's list positions and alphas ([kTopK][kThreads] each)
     float vout[kMaxC][kThreads];       // dL/dout per channel and pixel
     float2 pxy[kThreads];              // pixel coordinates
     uint16_t pairs[kPairs];            // (slot << 8) | pixel, grouped by entry
