@@ -10,8 +10,9 @@
 // B200 layout: one CTA per tile (grid = tiles, so the hardware balances uneven list lengths over the 148 SMs); pixels are numbered so
 // that 32 consecutive ones form a compact 8x4 patch; the forward's 128 threads take two pixels each (patches t and t + 128), the
 // backward's 256 threads one; the tile's list is staged in shared memory in chunks of 256 entries (one 16-byte and one 4-byte broadcast
-// load per Gaussian, shared by a thread's pixels). The training step's forward also takes the L1 loss of its pixels and writes the
-// loss's gradient with respect to the image. Two output forms of the top-K lists:
+// load per Gaussian, shared by a thread's pixels). The forward can also take the L1 loss of its pixels and write the loss's gradient with
+// respect to the image. The training step runs forward, L1 loss and backward of a tile in one kernel (raster_step_kernel, 256 threads,
+// one pixel each), keeping the top-K lists and the image gradient on chip. Two output forms of the top-K lists of the separate forward:
 //   * pixel_topk [H, W, 10] int32 Gaussian IDs (the reference's operator output), written through shared memory as coalesced 8-byte rows;
 //   * tile lists (autograd path): per tile, slot-major [10][256] uint16 positions in the tile's Gaussian list, 20 bytes per pixel instead
 //     of 40, written as coalesced 64-byte warp rows, and read back by the backward pass, which stages the same list in shared memory.
@@ -19,9 +20,10 @@
 //
 // Backward (the math of nd_rasterize_backward_topk_norm_kernel, backward.cu:187-308): with D = 1e-4 + sum_k d_k and s_k = f_k . v_out,
 // v_sigma_k = -d_k (s_k / D - sum_j d_j s_j / D^2) and the colour weight d_k / D; per Gaussian v_conic += (v_sigma dx^2 / 2, v_sigma dx dy,
-// v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Two kernels:
-//   * raster_bwd_pairs_kernel (training step, from the tile lists): the tile's (pixel, slot) pairs grouped by Gaussian in shared memory,
-//     one warp per Gaussian summing its pairs, then one global atomic per (tile, Gaussian, value); see the comment above it;
+// v_sigma dy^2 / 2), v_xy += v_sigma (a dx + b dy, b dx + c dy), v_color += (d_k / D) v_out. Two kernels and the fused one:
+//   * raster_bwd_pairs_kernel (autograd path, from the tile lists): the tile's (pixel, slot) pairs grouped by Gaussian in shared memory,
+//     one warp per Gaussian summing its pairs, then one global atomic per (tile, Gaussian, value); see the comment above it (the fused
+//     raster_step_kernel ends with the same steps);
 //   * raster_bwd_ids_kernel (the [H, W, 10] operator): each warp visits the union of its 32 pixels' top-K Gaussian IDs in increasing
 //     order (a warp-wide minimum per step), sums the 5 + C values of each over the warp with a recursive-halving reduce-scatter, and
 //     adds them with one global atomic per value.
