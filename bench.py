@@ -187,14 +187,16 @@ def time_graph(graph, reps, flush):
 
 RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the step's raster kernel, from one ncu capture of this workload
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the step's raster kernels, from ncu captures of this workload
 # (`ncu --set full --clock-control none -k regex:raster_step -s 2 -c 1 python bench.py --steps 2 --warmup 3 --no-cpu --no-e2e
-# --no-stages`, caches flushed before each pass: the image's 24.9 MB of writes were still in L2 when the kernel ended); None where no
-# capture was taken
-NCU_TRAFFIC = {"cfg3_1080p": 26.994e6 + 0.238e6}
+# --no-stages`, and the same with `-k regex:"raster_(fwd|bwd_pairs)" -c 2 ... --split`; caches flushed before each pass, writes still
+# in L2 when a kernel ended not counted); None where no capture was taken
+NCU_TRAFFIC = {("cfg3_1080p", "raster_step"): 26.994e6 + 0.238e6,
+               ("cfg3_1080p", "raster_forward"): 26.447e6 + 36.868e6,
+               ("cfg3_1080p", "raster_backward"): 68.466e6 + 1.702e6}
 
 
-def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, traffic, label=""):
+def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, workload=None, label=""):
     """The roofline entry of the step's dominant raster kernel from the single-stage times. The fused step kernel (stage "raster") moves,
     algorithmically: the image written and the target read (8 C bytes a pixel), the list IDs (4 bytes an intersection), each Gaussian's
     centre, conic and colours read once and its gradients written once (2 x 4 (5 + C) bytes), the tile ranges (8 bytes a tile); the
@@ -210,7 +212,7 @@ def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_k
         nbytes = fwd_bytes if dominant == "forward" else bwd_bytes
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": name + label, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": nbytes, "kernel_ms": ms}
+            "peak_kind": peak_kind, "traffic": NCU_TRAFFIC.get((workload, name)), "algorithmic_bytes": nbytes, "kernel_ms": ms}
 
 
 def step_options(wl, device):
@@ -276,7 +278,7 @@ def run_ours(args, wl):
         stage_ms = {"raster": ms_per_step}  # no per-stage times: the whole step stands in for the raster kernel
     hbm_peak, peak_kind = peaks()
     p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
-    roofline = raster_roofline(stage_ms, p, c, n, k, num_isect, wl.num_tiles, hbm_peak, peak_kind, NCU_TRAFFIC.get(wl.name))
+    roofline = raster_roofline(stage_ms, p, c, n, k, num_isect, wl.num_tiles, hbm_peak, peak_kind, wl.name)
     step_bytes = (p * (8 * c + 8 * k) + n * 4 * (5 + 7 + 2 * (5 + c) + (5 + c) + 5 + 5) + num_isect * 4 * 5 + wl.num_tiles * 16)
     loss_bytes = 12 * c * p
 
