@@ -194,6 +194,9 @@ RATE_MODEL = os.path.join(ROOT, "tests", "golden", "py_cfg2_480p_yuv.npz")
 NCU_TRAFFIC = {("cfg3_1080p", "raster_step"): 26.994e6 + 0.238e6,
                ("cfg3_1080p", "raster_forward"): 26.447e6 + 36.868e6,
                ("cfg3_1080p", "raster_backward"): 68.466e6 + 1.702e6}
+# the same captures' smsp__issue_active.avg.pct_of_peak_sustained_active: what bounds these kernels (instruction issue, not HBM)
+NCU_ISSUE_ACTIVE = {("cfg3_1080p", "raster_step"): 0.841, ("cfg3_1080p", "raster_forward"): 0.711,
+                    ("cfg3_1080p", "raster_backward"): 0.765}
 
 
 def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, workload=None, label=""):
@@ -212,7 +215,8 @@ def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_k
         nbytes = fwd_bytes if dominant == "forward" else bwd_bytes
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": name + label, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "peak_kind": peak_kind, "traffic": NCU_TRAFFIC.get((workload, name)), "algorithmic_bytes": nbytes, "kernel_ms": ms}
+            "peak_kind": peak_kind, "traffic": NCU_TRAFFIC.get((workload, name)), "algorithmic_bytes": nbytes, "kernel_ms": ms,
+            "issue_active": NCU_ISSUE_ACTIVE.get((workload, name))}
 
 
 def step_options(wl, device):
