@@ -151,6 +151,8 @@ def run_reference(args, wl):
     threads = len(os.sched_getaffinity(0))
     cpu.set_threads(threads)
     a = [inp[k].numpy() for k in ("means", "scales", "rotations", "features", "target")]
+    _, _, _, hits = cpu.project_fwd(a[0], a[1], a[2], wl.height, wl.width)
+    num_isect = int(np.asarray(hits, dtype=np.int64).sum())
     for _ in range(args.warmup):
         cpu.train_step(*a, wl.height, wl.width)
     times = []
@@ -165,7 +167,8 @@ def run_reference(args, wl):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded sinusoid target, random Gaussians)",
-        "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels},
+        "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
+                   "tile": 16, "top_k": 10, "intersections": num_isect},
         "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU implementation of this path; this is the oracle's C restatement of its kernels",
