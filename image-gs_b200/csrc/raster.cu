@@ -1127,8 +1127,8 @@ int raster_step(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, i
         if (cudaMemsetAsync(loss, 0, sizeof(float), s) != cudaSuccess) return igs::check_launch(who);
         return IGS_OK;
     }
-    IGS_REQUIRE(tile_bins && xys && conics && colors && target && out_img && workspace, "%s: null pointer", who);
-    IGS_REQUIRE(num_points == 0 || ids_sorted, "%s: null gaussian_ids_sorted", who);
+    IGS_REQUIRE(tile_bins && target && out_img && workspace, "%s: null pointer", who);
+    IGS_REQUIRE(num_points == 0 || (ids_sorted && xys && conics && colors), "%s: null Gaussian pointer", who);  // unread without Gaussians
     IGS_REQUIRE(igs::aligned(tile_bins, 8) && igs::aligned(xys, 8), "%s: tile_bins and xys must be 8-byte aligned", who);
     IGS_REQUIRE(workspace_bytes >= igs_raster_l1_workspace(tiles), "%s: workspace too small (%zu bytes, need %zu)", who, workspace_bytes,
                 igs_raster_l1_workspace(tiles));

@@ -96,3 +96,34 @@ def test_pipeline_fused_step_matches_two_kernel_step(name, device):
     names = ["v_mean2d", "v_scale", "v_rot", "v_colors"] + (["v_feat"] if opts else [])
     for k in names:  # summation order only (float atomics; the rate term's and the loss transform's sums amplify it slightly)
         assert_close_grad(getattr(fused, k), getattr(split, k), what=k)
+
+
+@pytest.mark.parametrize("case", ["no_gaussians", "one_pixel", "truncated_lists"])
+def test_fused_step_edge_cases(case, device):
+    """No Gaussians (the image is zero, the loss is ratio * mean|target|), a 1x1 image, and lists cut short by a capacity below the
+    intersection count: the fused kernel agrees with the separate kernels."""
+    h, w, n = {"no_gaussians": (40, 56, 0), "one_pixel": (1, 1, 5), "truncated_lists": (64, 80, 400)}[case]
+    _, inp = make_case(h, w, max(n, 1), seed=17)
+    d = to_dev(inp, device)
+    if n == 0:
+        d = {k: (v[:0] if k in ("means", "scales", "rotations", "features") else v) for k, v in d.items()}
+    tb = ops.tile_grid(h, w)
+    xys, radii, conics, hits = ops.project_gaussians_2d_scale_rot_forward(n, d["means"], d["scales"], d["rotations"], h, w, tb)
+    cum, total = ops.cumulative_intersects(hits)
+    cap = int(total.item()) if n else 0
+    if case == "truncated_lists":
+        cap //= 2
+    feats, target = d["features"], d["target"]
+    ids, bins = ops.sort_intersects_by_tile(n, max(cap, 1) if n else 0, xys, radii, cum, tb)
+    f_img, f_loss, f_xy, f_conic, f_colors = ops.raster_step_l1(tb, (w, h, 1), ids, bins, xys, conics, feats, target, ratio=0.5)
+    if n == 0:
+        assert not bool(f_img.any())
+        assert abs(float(f_loss) - 0.5 * float(target.abs().mean())) <= 2e-6 * float(target.abs().mean())
+        return
+    img, tile_topk, loss, v_out = ops.nd_rasterize_forward_topk_norm_tiles_l1(tb, (w, h, 1), max(cap, 1), ids, bins, xys, conics, feats,
+                                                                             target, ratio=0.5)
+    v_xy, v_conic, v_colors = ops.nd_rasterize_backward_topk_norm_tiles(h, w, ids, bins, xys, conics, feats, v_out, tile_topk)
+    assert torch.equal(f_img, img)
+    assert abs(float(f_loss) - float(loss)) <= 2e-6 * max(abs(float(loss)), 1e-30)
+    for a, b, name in ((f_xy, v_xy, "v_xy"), (f_conic, v_conic, "v_conic"), (f_colors, v_colors, "v_colors")):
+        assert_close_grad(a, b, rtol=1e-5, what=name)
