@@ -106,9 +106,18 @@ def dist_setup(gpus):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        # NCCL's own log lines (its version banner at NCCL_DEBUG=WARN) go to stderr: rank 0's stdout is the one JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # NCCL prints its version banner on the process's stdout when it creates the communicator: send file descriptor 1 to stderr
+        # meanwhile, so that rank 0's stdout holds only the JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local
 
 
