@@ -186,8 +186,13 @@ def raster_step_l1(tile_bounds, img_size, gaussian_ids_sorted, tile_bins, xys, c
     with respect to out_img, when with_v_output), as nd_rasterize_forward_topk_norm_tiles_l1 followed by
     nd_rasterize_backward_topk_norm_tiles would give them."""
     h, w = _check_raster_geometry(tile_bounds, (TILE, TILE, 1), img_size)
+    _check_input(gaussian_ids_sorted, "gaussian_ids_sorted", torch.int32)
+    _check_input(tile_bins, "tile_bins", torch.int32)
+    for t, name in ((xys, "xys"), (conics, "conics"), (colors, "colors"), (target, "target")):
+        _check_input(t, name, torch.float32)
     channels = colors.size(1)
-    _check_input(target, "target", torch.float32)
+    if channels > MAX_CHANNELS:
+        raise RuntimeError(f"at most {MAX_CHANNELS} channels")
     if tuple(target.shape) != (channels, h, w):
         raise RuntimeError(f"target must be [{channels}, {h}, {w}]")
     n = xys.size(0)
