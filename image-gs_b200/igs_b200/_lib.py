@@ -50,6 +50,8 @@ SIGNATURES = {
     "igs_l1_loss": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
     "igs_quantize_ste": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_float, P, P, P, P, P, P, P, P, P, P, P, P]),
     "igs_feat_transform_bwd": (c_int, [c_int, c_int, P, P, P, P, P]),
+    "igs_rate_model_workspace": (c_size_t, [c_int]),
+    "igs_rate_model": (c_int, [c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
     "igs_rate_workspace": (c_size_t, [c_int]),
     "igs_rate_fwd": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_float, c_float, c_float, P, P, P, P, P, c_size_t,
                              P]),

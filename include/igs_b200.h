@@ -220,6 +220,22 @@ int igs_quantize_ste(int num_points, int channels, const float *xy, const float 
 int igs_feat_transform_bwd(int num_points, int channels, const float *v_feat_t, const float *feat_transform, const float *v_extra,
                            float *v_feat, void *stream);
 
+/* rate_model (compress/rate.py:131-164, with predicting_sources 116-128): the fixed inputs of the rate term from the quantized Gaussians,
+ * on the GPU. Inputs (device): neighbors [P,8] int64 (the bitstream-order neighbours of igs_nearest_neighbors mapped back to the
+ * Gaussians' order, -1 for none), feat [P,C] the dequantized features, log2_scale [P,2] the dequantized log2 scales, q_rot [P] the rotation
+ * indices (integer values), steps [C] the feature steps (> 0), channel_weights [C]; color_refs and pred_refs [C] (host) as
+ * compress.quantization.get_channel_refs and compress.prediction.get_prediction_refs give them (-1 for none). Outputs (device):
+ * neighbors_out [P,8] int32 (clamped to 0), weights [P,8], slope [P,C], inv_steps [C], inv_feat [C], feat_coeffs [C], inv_rot [P],
+ * offsets [P+1] int32, sources [<= 8P] int32 and source_weights [<= 8P] (offsets[P] of them). Workspace: igs_rate_model_workspace bytes,
+ * 16-byte aligned. Float operations follow the reference's float32 order; the means of the rounded residuals and rotation indices are
+ * exact integer sums. */
+size_t igs_rate_model_workspace(int num_points);
+int igs_rate_model(int num_points, int channels, const int64_t *neighbors, const float *feat, const float *log2_scale, const float *q_rot,
+                   const int32_t *color_refs, const int32_t *pred_refs, const float *steps, const float *channel_weights,
+                   int32_t *neighbors_out, float *weights, float *slope, float *inv_steps, float *inv_feat, float *feat_coeffs,
+                   float *inv_rot, int32_t *offsets, int32_t *sources, float *source_weights, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
 /* rate_loss_forward (gsplat/gsplat/cuda/csrc/rate.cu:201-279; definition compress/rate.py:167-175 rate_bits): loss (device scalar)
  * = factor / max(l1_loss / l1_ratio, 1e-4) * (sum_{g,c} feat_coeffs[c] (sqrt(r^2 + 1/4) - 1/2) + sum_g rot_coeffs[g] (sqrt(t^2 + 1/4) - 1/2)),
  * own_grad [N,C] and rot_grad [N] for the backward pass. color_refs / pred_refs: C host integers each. neighbors [N,K] int32.

@@ -70,6 +70,13 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.igs_raster_step_l1_band(1, 2, 32, 16, 1, 3, 3, 0, null, null, null, null, null, null, 1.0, null, fake, null, null, null,
                                        null, null, 0, null) == 1
     assert "tile rows" in lib.igs_last_error().decode()
+    no_refs = (ctypes.c_int32 * 3)(-1, -1, -1)
+    self_ref = (ctypes.c_int32 * 3)(0, 0, 1)  # channel 0 predicting from itself
+    as_ptr = lambda a: ctypes.cast(a, ctypes.c_void_p)  # noqa: E731
+    assert lib.igs_rate_model(10, 3, *([fake] * 4), as_ptr(no_refs), as_ptr(self_ref), *([fake] * 13), 1 << 20, null) == 1
+    assert "prediction reference" in lib.igs_last_error().decode()
+    assert lib.igs_rate_model(10, 0, *([fake] * 4), as_ptr(no_refs), as_ptr(no_refs), *([fake] * 13), 1 << 20, null) == 1
+    assert "channels" in lib.igs_last_error().decode()
     assert lib.igs_sort_intersects(10, 100, null, null, null, 4, 4, null, null, null, 0, null) == 1
     assert lib.igs_quantize_ste(10, 3, null, null, null, null, null, 0.0, 0.1, null, null, null, null, null, null, null, null, null, null,
                                 null, null) == 1
