@@ -562,7 +562,8 @@ def run_e2e(args, wl, inp, device, capacity, world):
 def run_aux(args):
     """The rows around the step, each timed on the GPU and beside the reference's CPU code where it has one: the neighbour search of the
     rate model's preparation at 80,000 Gaussians (vs the reference's C++ causal_neighbors, built from source into oracle/_ref, on all host
-    threads), the per-Gaussian feature weights and the leave-one-out loss increase at 1080p/20k. One JSON line."""
+    threads) and the whole rate model of those Gaussians, the per-Gaussian feature weights and the leave-one-out loss increase at
+    1080p/20k. One JSON line."""
     from igs_b200 import neighbors as nb
     from igs_b200 import ops
 
@@ -607,6 +608,29 @@ def run_aux(args):
         entry["reference_cpu_ms"] = None
         entry["reference_note"] = str(e)
     out["causal_neighbors"] = entry
+
+    # the whole rate model (compress.rate.rate_model) of the same 80,000 Gaussians, YUV prediction references: bitstream order,
+    # neighbour search and igs_rate_model on the GPU; wall time per call (it reads the positions' range and the list length back)
+    from igs_b200 import rate_model as rm
+
+    steps = torch.full((wl4.channels,), 1.0 / 64, device=device)
+    feat = torch.round(inp4["features"].to(device) / steps) * steps
+    log2_scale = torch.round(torch.log2(inp4["scales"].abs().to(device)) / 0.03125) * 0.03125
+    q_rot = torch.round(inp4["rotations"].to(device)[:, 0] / (np.pi / 256))
+    weights = torch.tensor([1.0, 0.25, 0.25], device=device)
+
+    def prepare():
+        return rm.rate_model(q, feat, log2_scale, q_rot, [-1, -1, -1], [-1, 0, 1], steps, weights, refine_bits=3)
+
+    prepare()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        prepare()
+    torch.cuda.synchronize()
+    out["rate_model_80k"] = {"wall_ms": 1e3 * (time.perf_counter() - t0) / 5,
+                             "note": "bitstream order (igs_bitstream_order), neighbour search and igs_rate_model on the GPU; two small "
+                                     "read-backs"}
 
     # feature weights and leave-one-out at 1080p/20k from the step's top-K lists
     wl = workloads.get_workload("cfg3_1080p")

@@ -50,6 +50,8 @@ SIGNATURES = {
     "igs_l1_loss": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
     "igs_quantize_ste": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_float, P, P, P, P, P, P, P, P, P, P, P, P]),
     "igs_feat_transform_bwd": (c_int, [c_int, c_int, P, P, P, P, P]),
+    "igs_bitstream_order_workspace": (c_size_t, [c_int]),
+    "igs_bitstream_order": (c_int, [c_int, P, c_int, P, P, c_size_t, P]),
     "igs_rate_model_workspace": (c_size_t, [c_int]),
     "igs_rate_model": (c_int, [c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
     "igs_rate_workspace": (c_size_t, [c_int]),
@@ -57,6 +59,9 @@ SIGNATURES = {
                              P]),
     "igs_rate_bwd": (c_int, [c_int, c_int, P, P, P, P, P, P, P, P, P, P]),
 }
+
+# status codes of include/igs_b200.h
+IGS_OK, IGS_ERR_INVALID, IGS_ERR_CUDA, IGS_ERR_UNSUPPORTED = 0, 1, 2, 3
 
 _lib = None
 

@@ -220,6 +220,16 @@ int igs_quantize_ste(int num_points, int channels, const float *xy, const float 
 int igs_feat_transform_bwd(int num_points, int channels, const float *v_feat_t, const float *feat_transform, const float *v_extra,
                            float *v_feat, void *stream);
 
+/* bitstream_order (compress/__init__.py:43-58): the order of the Gaussians along the Morton curve of their integer positions [P, 2] (int64,
+ * 16-byte aligned) coarsened by refine_bits, ties by the Morton code of the full positions, then by index; order [P] int64. Reads the
+ * positions' range back once (the call synchronizes the stream: not for CUDA-graph capture). Positions spanning 2^32 coarse levels or more
+ * are rejected (IGS_ERR_INVALID, as the reference rejects them); a key wider than 64 bits (coordinates spanning more than about 2^16 coarse
+ * and fine levels together) returns IGS_ERR_UNSUPPORTED for a host sort. Workspace: igs_bitstream_order_workspace bytes, 256-byte
+ * aligned. */
+size_t igs_bitstream_order_workspace(int num_points);
+int igs_bitstream_order(int num_points, const int64_t *positions, int refine_bits, int64_t *order, void *workspace, size_t workspace_bytes,
+                        void *stream);
+
 /* rate_model (compress/rate.py:131-164, with predicting_sources 116-128): the fixed inputs of the rate term from the quantized Gaussians,
  * on the GPU. Inputs (device): neighbors [P,8] int64 (the bitstream-order neighbours of igs_nearest_neighbors mapped back to the
  * Gaussians' order, -1 for none), feat [P,C] the dequantized features, log2_scale [P,2] the dequantized log2 scales, q_rot [P] the rotation

@@ -69,3 +69,33 @@ def test_matches_reference_search_at_80k(device):
     ordered = np.ascontiguousarray(q[nb.bitstream_order(q, 3)])
     got = nb.causal_neighbors(torch.from_numpy(ordered).to(device)).cpu().numpy()
     np.testing.assert_array_equal(got, ref.causal_neighbors(ordered))
+
+
+@pytest.mark.parametrize("refine_bits", [0, 3])
+@pytest.mark.parametrize("case", ["small", "ragged", "large", "duplicates", "negative", "one_point", "all_equal"])
+def test_bitstream_order_on_the_gpu_equals_the_host_sort(case, refine_bits, device):
+    """igs_bitstream_order (Morton keys, stable radix sort) gives the host sort's order (numpy, the reference's definition) exactly."""
+    rng = np.random.default_rng(7 * ["small", "ragged", "large", "duplicates", "negative", "one_point", "all_equal"].index(case) + refine_bits)
+    n = {"small": 100, "ragged": 2048 * 3 + 17, "large": 100_000, "duplicates": 5000, "negative": 3000, "one_point": 1,
+         "all_equal": 700}[case]
+    span = 30720 if case != "small" else 64
+    q = rng.integers(0, span, size=(n, 2), dtype=np.int64)
+    if case == "duplicates":
+        q = q[rng.integers(0, 50, size=n)]  # fifty distinct positions, many ties broken by index
+    if case == "negative":
+        q -= 20000
+    if case == "all_equal":
+        q[:] = 1234
+    got = nb.bitstream_order_device(torch.from_numpy(q).to(device), refine_bits)
+    assert got is not None
+    np.testing.assert_array_equal(got.cpu().numpy(), nb.bitstream_order(q, refine_bits))
+
+
+def test_bitstream_order_falls_back_for_wide_keys(device):
+    rng = np.random.default_rng(4)
+    q = rng.integers(0, 2**30, size=(1000, 2), dtype=np.int64)  # coarse and fine codes together wider than 64 bits
+    assert nb.bitstream_order_device(torch.from_numpy(q).to(device), 2) is None
+    got = nb.bitstream_neighbors(q, 2, device=device)  # the host sort then gives the order
+    np.testing.assert_array_equal(got, on.bitstream_neighbors(q, 2))
+    with pytest.raises(ValueError, match="2\\^32"):
+        nb.bitstream_order_device(torch.tensor([[0, 0], [2**33, 0]], dtype=torch.int64, device=device), 0)
