@@ -188,3 +188,22 @@ def test_neighbors_oracle_matches_reference_fixture(name):
     got = on.bitstream_neighbors(z["q_xy"].astype(np.int64), 3)
     np.testing.assert_array_equal(got.clip(min=0), z["neighbors"])
     np.testing.assert_array_equal(got >= 0, z["weights"] > 0)
+
+
+@pytest.mark.parametrize("name", ["cfg2_480p_yuv", "rgb_subgreen_320x200"])
+def test_rate_model_oracle_matches_reference_fixture(name):
+    """oracle/rate_model.py (numpy, brute-force neighbours) reproduces the reference's own compress.rate.rate_model outputs stored in the
+    fixture: neighbours, weights and in-neighbour lists exactly, slopes and coefficients to float32 rounding."""
+    from oracle import rate_model as orm
+
+    z = np.load(os.path.join(GOLDEN, f"py_{name}.npz"))
+    pred_refs = [-1 if int(p) == c else int(p) for c, p in enumerate(z["pred_channels"])]
+    weights = [1.0, 0.25, 0.25] if name == "cfg2_480p_yuv" else [1.0, 1.0, 1.0]  # as make_golden_py.py
+    got = orm.rate_model(z["q_xy"].astype(np.int64), z["q_feat"] * z["feat_steps"], z["q_scale"] * np.float32(z["scale_step"]),
+                         z["q_rot"][:, 0], [int(r) for r in z["color_refs"]], pred_refs, z["feat_steps"], weights, refine_bits=3)
+    for k in ("neighbors", "weights", "offsets", "sources", "source_weights", "inv_steps"):
+        np.testing.assert_array_equal(got[k], z[k], err_msg=k)
+    np.testing.assert_allclose(got["slope"], z["slope"], rtol=0, atol=2e-6, err_msg="slope")
+    for k in ("feat_coeffs", "inv_rot"):
+        np.testing.assert_allclose(got[k], z[k], rtol=2e-6, atol=0, err_msg=k)
+    assert got["pred_channels"] == tuple(int(p) for p in z["pred_channels"])
