@@ -212,23 +212,29 @@ NCU_ISSUE_ACTIVE = {("cfg3_1080p", "raster_step"): 0.841, ("cfg3_1080p", "raster
 
 
 def raster_roofline(stage_ms, p, c, n, k, num_isect, num_tiles, hbm_peak, peak_kind, workload=None, label=""):
-    """The roofline entry of the step's dominant raster kernel from the single-stage times. The fused step kernel (stage "raster") moves,
-    algorithmically: the image written and the target read (8 C bytes a pixel), the list IDs (4 bytes an intersection), each Gaussian's
-    centre, conic and colours read once and its gradients written once (2 x 4 (5 + C) bytes), the tile ranges (8 bytes a tile); the
-    separate kernels (stages "forward" and "backward") move the [H, W, 10] lists of the operator surface and the image gradient too."""
+    """The roofline entry of the step's dominant raster kernel from the single-stage times. algorithmic_bytes is the per-step figure of
+    the operator surface (the reference's dataflow: the image and the [H, W, 10] lists written by the forward and read back by the
+    backward, the image gradient, the Gaussians' parameters and gradients, the list IDs) for the work the kernel does:
+      forward with the L1 loss: P (4C + 4K) + I 4 + N 4 (5 + C) + 12 C P (the loss reads the image and the target, writes the gradient);
+      backward: P (4C + 4K) + N 4 ((5 + C) + (2 + 3 + C));
+      the fused step kernel (stage "raster"): both.
+    moved_bytes is what the kernel itself must move: the fused kernel only reads the target and the lists' Gaussians and writes the image
+    and the gradients (8 C P + I 4 + 2 N 4 (5 + C) + 8 T), since it keeps the lists and the image gradient on chip."""
+    fwd_bytes = p * (4 * c + 4 * k) + num_isect * 4 + n * 4 * (5 + c) + 12 * c * p
+    bwd_bytes = p * (4 * c + 4 * k) + n * 4 * ((5 + c) + (2 + 3 + c))
     if "raster" in stage_ms:
         name, ms = "raster_step", stage_ms["raster"]
-        nbytes = p * 8 * c + num_isect * 4 + n * 4 * (5 + c) * 2 + num_tiles * 8
+        nbytes = fwd_bytes + bwd_bytes
+        moved = p * 8 * c + num_isect * 4 + n * 4 * (5 + c) * 2 + num_tiles * 8
     else:
         dominant = max(("forward", "backward"), key=lambda s: stage_ms.get(s, 0.0))
         name, ms = f"raster_{dominant}", stage_ms[dominant]
-        fwd_bytes = p * (4 * c + 4 * k) + p * 8 * c + num_isect * 4 + n * 4 * (5 + c)
-        bwd_bytes = p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
         nbytes = fwd_bytes if dominant == "forward" else bwd_bytes
+        moved = nbytes
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": name + label, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "peak_kind": peak_kind, "traffic": NCU_TRAFFIC.get((workload, name)), "algorithmic_bytes": nbytes, "kernel_ms": ms,
-            "issue_active": NCU_ISSUE_ACTIVE.get((workload, name))}
+            "peak_kind": peak_kind, "traffic": NCU_TRAFFIC.get((workload, name)), "algorithmic_bytes": nbytes, "moved_bytes": moved,
+            "kernel_ms": ms, "issue_active": NCU_ISSUE_ACTIVE.get((workload, name))}
 
 
 def step_options(wl, device):

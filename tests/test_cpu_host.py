@@ -57,14 +57,17 @@ def test_roofline_bytes_of_the_raster_kernels():
     import bench
 
     p, c, n, k, isect, tiles = 2_073_600, 3, 20_000, 10, 178_298, 8_160
+    fwd = p * (4 * c + 4 * k) + isect * 4 + n * 4 * (5 + c) + 12 * c * p
+    bwd = p * (4 * c + 4 * k) + n * 4 * ((5 + c) + (2 + 3 + c))
     fused = bench.raster_roofline({"raster": 0.2}, p, c, n, k, isect, tiles, 6540.2, "measured", "cfg3_1080p")
     assert fused["kernel"] == "raster_step"
-    assert fused["algorithmic_bytes"] == p * 8 * c + isect * 4 + n * 4 * (5 + c) * 2 + tiles * 8
+    assert fused["algorithmic_bytes"] == fwd + bwd  # the operator surface of forward, loss and backward
+    assert fused["moved_bytes"] == p * 8 * c + isect * 4 + n * 4 * (5 + c) * 2 + tiles * 8
     assert fused["achieved"] == pytest.approx(fused["algorithmic_bytes"] / 0.2e-3 / 1e9)
     assert fused["frac"] == pytest.approx(fused["achieved"] / 6540.2)
     assert fused["traffic"] > 0 and 0 < fused["issue_active"] <= 1
     split = bench.raster_roofline({"forward": 0.11, "backward": 0.13}, p, c, n, k, isect, tiles, 6540.2, "measured", "cfg3_1080p")
     assert split["kernel"] == "raster_backward" and split["kernel_ms"] == 0.13
-    assert split["algorithmic_bytes"] == p * (4 * c + 4 * k) + n * 4 * (5 + c) * 2
+    assert split["algorithmic_bytes"] == bwd == split["moved_bytes"]
     other = bench.raster_roofline({"raster": 0.5}, p, c, n, k, isect, tiles, 6540.2, "measured", "cfg4_2160p")
     assert other["traffic"] is None and other["issue_active"] is None  # no capture of that workload
