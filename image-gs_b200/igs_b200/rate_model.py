@@ -34,13 +34,15 @@ class RateModel(NamedTuple):
 
 
 def channel_operands(color_refs, pred_refs, device):
-    """The channel references as index tensors (compress/rate.py:69-78): the colour references as (channel indices, mask), None when no
-    channel has one, and the prediction reference of each channel (itself when it has none)."""
-    own = torch.arange(len(color_refs), device=device)
-    color = torch.tensor(list(color_refs), device=device)
-    pred = torch.tensor(list(pred_refs), device=device)
-    color_idx = (torch.where(color >= 0, color, own), color >= 0) if bool((color >= 0).any()) else None
-    return color_idx, torch.where(pred >= 0, pred, own)
+    """The channel references in the index-tensor form of the reference's RateModel.operands (compress/rate.py:69-78), for its Python
+    rate_bits: (colour reference of each channel with the mask of channels that have one, or None when none has) and the prediction
+    reference of each channel, a channel without one standing for itself."""
+    fill = lambda refs: [int(r) if int(r) >= 0 else c for c, r in enumerate(refs)]  # noqa: E731
+    pred_idx = torch.tensor(fill(pred_refs), device=device)
+    if not any(int(r) >= 0 for r in color_refs):
+        return None, pred_idx
+    mask = torch.tensor([int(r) >= 0 for r in color_refs], device=device)
+    return (torch.tensor(fill(color_refs), device=device), mask), pred_idx
 
 
 def rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, channel_weights, dtype=torch.float32,
