@@ -77,6 +77,11 @@ def test_invalid_arguments_rejected_on_host():
     assert "prediction reference" in lib.igs_last_error().decode()
     assert lib.igs_rate_model(10, 0, *([fake] * 4), as_ptr(no_refs), as_ptr(no_refs), *([fake] * 13), 1 << 20, null) == 1
     assert "channels" in lib.igs_last_error().decode()
+    assert lib.igs_bitstream_order(10, fake, 40, fake, fake, 1 << 20, null) == 1
+    assert "refine_bits" in lib.igs_last_error().decode()
+    assert lib.igs_bitstream_order(-1, fake, 0, fake, fake, 1 << 20, null) == 1
+    assert "negative" in lib.igs_last_error().decode()
+    assert lib.igs_bitstream_order(0, null, 0, null, null, 0, null) == 0  # nothing to order
     assert lib.igs_sort_intersects(10, 100, null, null, null, 4, 4, null, null, null, 0, null) == 1
     assert lib.igs_quantize_ste(10, 3, null, null, null, null, null, 0.0, 0.1, null, null, null, null, null, null, null, null, null, null,
                                 null, null) == 1
