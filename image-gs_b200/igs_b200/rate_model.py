@@ -89,3 +89,30 @@ def rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, chan
     return RateModel(out_neighbors, weights, slope, inv_steps, inv_feat, feat_coeffs, inv_rot, offsets, sources[:edges],
                      source_weights[:edges], channel_operands(color_refs, pred_refs, device), tuple(int(r) for r in color_refs),
                      pred_channels)
+
+
+def install(*module_names):
+    """Route the reference's calls of compress.rate.rate_model and bitstream_neighbors to these GPU versions (same signatures): the names
+    are replaced in each named module that is imported or importable (default: compress.rate and model, which binds rate_model when it is
+    imported, model.py:43). Returns {(module, name): original} for restore()."""
+    import importlib
+
+    replaced = {}
+    for name in module_names or ("compress.rate", "model"):
+        try:
+            module = importlib.import_module(name)
+        except ImportError:
+            continue
+        for attr, new in (("rate_model", rate_model), ("bitstream_neighbors", bitstream_neighbors)):
+            if hasattr(module, attr):
+                replaced[(name, attr)] = getattr(module, attr)
+                setattr(module, attr, new)
+    return replaced
+
+
+def restore(replaced):
+    """Undo install()."""
+    import importlib
+
+    for (name, attr), original in replaced.items():
+        setattr(importlib.import_module(name), attr, original)

@@ -71,3 +71,20 @@ def test_roofline_bytes_of_the_raster_kernels():
     assert split["algorithmic_bytes"] == bwd == split["moved_bytes"]
     other = bench.raster_roofline({"raster": 0.5}, p, c, n, k, isect, tiles, 6540.2, "measured", "cfg4_2160p")
     assert other["traffic"] is None and other["issue_active"] is None  # no capture of that workload
+
+
+def test_rate_model_install_replaces_and_restores(monkeypatch):
+    """igs_b200.rate_model.install routes a module's rate_model / bitstream_neighbors to the GPU versions and restore undoes it."""
+    import sys
+    import types
+
+    from igs_b200 import neighbors, rate_model
+
+    fake = types.ModuleType("fake_compress_rate")
+    fake.rate_model, fake.bitstream_neighbors, fake.other = "ref_rate_model", "ref_neighbors", "untouched"
+    monkeypatch.setitem(sys.modules, "fake_compress_rate", fake)
+    replaced = rate_model.install("fake_compress_rate", "no_such_module_here")
+    assert fake.rate_model is rate_model.rate_model and fake.bitstream_neighbors is neighbors.bitstream_neighbors
+    assert fake.other == "untouched" and len(replaced) == 2
+    rate_model.restore(replaced)
+    assert fake.rate_model == "ref_rate_model" and fake.bitstream_neighbors == "ref_neighbors"
