@@ -429,11 +429,17 @@ int igs_sort_intersects_band(int num_points, int capacity, const float *xys, con
 //
 // For callers that cannot call cudaMalloc and have no workspace to lend: a plugin inside a host application that owns all device memory,
 // or code running where an allocation would synchronize the device and stall its other streams. The scratch lives in a fixed array of
-// this library instead, sized for IGS_NOALLOC_MAX_CAPACITY intersections over IGS_NOALLOC_MAX_TILES tiles (about 16 MiB). Every device that
-// loads the library holds one copy until the process exits. All calls on a device share it: calls that overlap on the GPU (on different
-// streams) race; what must start at zero (the per-tile counters) is cleared by every call.
+// this library instead, sized for IGS_NOALLOC_MAX_CAPACITY intersections over IGS_NOALLOC_MAX_TILES tiles (about 16 MiB). Every CUDA
+// context that runs the library (the device's primary context, or a host application's own) holds one copy until the context or the
+// process ends. All calls in a context share it: calls that overlap on the GPU (on different streams) race; what must start at zero
+// (the per-tile counters) is cleared by every call. The first call in a context looks up the copy's address; make it before any stream
+// capture in that context.
+
+#include <cuda.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 
 namespace {
 
@@ -443,25 +449,67 @@ constexpr size_t kNoAllocScratchBytes =
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void *g_noalloc_address[kMaxDevices] = {};
+// A __device__ array has one address per CUDA context, not per device: a host application may run this library under contexts of its
+// own (cuCtxCreate / cuCtxSetCurrent) beside the device's primary one, and a context destroyed and created again (cudaDeviceReset, for
+// one) gets new memory. So the address is cached per context, keyed by the context's ID (cuCtxGetId: unique for the life of the process,
+// never reused, unlike the CUcontext handle). The two driver functions are reached through the runtime (cudaGetDriverEntryPoint), so
+// the library does not link libcuda itself.
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
 
-// The scratch array's device address on the current device. In host code g_noalloc_scratch names a host-side stand-in, so the address is
-// looked up once per device, with that device current.
+std::mutex g_noalloc_mutex;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+std::vector<std::pair<unsigned long long, void *>> g_noalloc_address;  // (context ID, the array's address in that context)
+
+int noalloc_driver_entry_points() {
+    if (g_ctx_get_current != nullptr && g_ctx_get_id != nullptr) return IGS_OK;
+    void *get_current = nullptr, *get_id = nullptr;
+    cudaDriverEntryPointQueryResult found_current = cudaDriverEntryPointSymbolNotFound, found_id = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &get_current, cudaEnableDefault, &found_current) != cudaSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &get_id, cudaEnableDefault, &found_id) != cudaSuccess ||
+        found_current != cudaDriverEntryPointSuccess || found_id != cudaDriverEntryPointSuccess || !get_current || !get_id) {
+        cudaGetLastError();
+        return igs::set_error(IGS_ERR_UNSUPPORTED, "igs_sort_intersects_noalloc: the driver lacks cuCtxGetCurrent / cuCtxGetId");
+    }
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(get_current);
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(get_id);
+    return IGS_OK;
+}
+
+// The scratch array's device address in the calling thread's current context. In host code g_noalloc_scratch names a host-side
+// stand-in, so the address is looked up (cudaGetSymbolAddress, with that context current) the first time a context calls, and cached.
+// With no context current yet the runtime's lookup makes the current device's primary context current, as any runtime call would.
 int noalloc_scratch(void **address) {
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess) return igs::check_launch("igs_sort_intersects_noalloc: cudaGetDevice");
-    if (device < 0 || device >= kMaxDevices) return igs::set_error(IGS_ERR_UNSUPPORTED, "igs_sort_intersects_noalloc: device %d", device);
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_address[device] == nullptr) {
-        void *p = nullptr;
+    int status = noalloc_driver_entry_points();
+    if (status != IGS_OK) return status;
+    CUcontext ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS)
+        return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: cuCtxGetCurrent failed");
+    void *p = nullptr;
+    if (ctx == nullptr) {
+        // no context yet on this thread: the runtime's lookup establishes the primary context, which is then current
         const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (err != cudaSuccess)
             return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
-        g_noalloc_address[device] = p;
+        if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+            return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: no current CUDA context");
     }
-    *address = g_noalloc_address[device];
+    unsigned long long id = 0;
+    if (g_ctx_get_id(ctx, &id) != CUDA_SUCCESS) return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: cuCtxGetId failed");
+    for (const auto &entry : g_noalloc_address)
+        if (entry.first == id) {
+            *address = entry.second;
+            return IGS_OK;
+        }
+    if (p == nullptr) {
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess)
+            return igs::set_error(IGS_ERR_CUDA, "igs_sort_intersects_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
+    }
+    g_noalloc_address.emplace_back(id, p);
+    *address = p;
     return IGS_OK;
 }
 

@@ -69,10 +69,12 @@ int igs_sort_intersects(int num_points, int capacity, const float *xys, const in
 
 /* The binning of igs_sort_intersects for callers that cannot allocate device memory and have no workspace to lend (a plugin in a host
  * application that owns all device memory, or code where an allocation would synchronize the device). No counterpart in the
- * reference. Its scratch is a fixed array inside the library, about 16 MiB on every device that loads it, held until the process exits;
- * capacity above IGS_NOALLOC_MAX_CAPACITY or more than IGS_NOALLOC_MAX_TILES tiles is rejected with IGS_ERR_INVALID. The first call on
- * each device looks up the array's device address (with that device current); make that first call before any stream capture. All
- * calls on a device share the array, so calls that overlap on the GPU race; each call clears what must start at zero. */
+ * reference. Its scratch is a fixed array inside the library, about 16 MiB in every CUDA context that runs it (the device's primary
+ * context or one the host application created), held until that context or the process ends; capacity above IGS_NOALLOC_MAX_CAPACITY
+ * or more than IGS_NOALLOC_MAX_TILES tiles is rejected with IGS_ERR_INVALID. The array's address belongs to one context: the first call
+ * in each context looks it up (with that context current) and caches it under the context's unique ID; make that first call before any
+ * stream capture. All calls in a context share the array, so calls that overlap on the GPU race; each call clears what must start at
+ * zero. */
 #define IGS_NOALLOC_MAX_CAPACITY 1048576
 #define IGS_NOALLOC_MAX_TILES 65536
 int igs_sort_intersects_noalloc(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit,

@@ -2,7 +2,8 @@
 The allocation-free binning entry point, igs_sort_intersects_noalloc: for callers that cannot call cudaMalloc and have no workspace to lend
 (for example a plugin inside a host application that owns all device memory, or code where an allocation would synchronize the device).
 It is called here through the C ABI and checked against igs_sort_intersects with a caller-provided workspace, on two calls in a row of
-different sizes: both calls use the library's one fixed scratch array, so the second must not see anything the first left in it.
+different sizes: both calls use the library's one fixed scratch array, so the second must not see anything the first left in it; and
+under several CUDA contexts of one device (the array has one address per context), in a child process.
 """
 import ctypes
 import os
@@ -64,3 +65,15 @@ def test_noalloc_binning_rejects_oversized_requests(device):
     tiles = header_constant("IGS_NOALLOC_MAX_TILES")
     assert lib.igs_sort_intersects_noalloc(10, 16, ptr(xys), ptr(radii), ptr(cum), tiles + 1, 1, ptr(out), ptr(out), stream) == 1
     assert "tiles" in lib.igs_last_error().decode()
+
+
+def test_noalloc_binning_under_several_contexts(device):
+    """The fixed scratch array has one address per CUDA context. A host application may run the library under contexts of its own, or
+    destroy a context and create another: the child process drives the C ABI from plain driver-API contexts (two side by side, one
+    created after another was destroyed, and the primary one), and every call must match igs_sort_intersects and the CPU oracle."""
+    import subprocess
+    import sys
+
+    child = os.path.join(os.path.dirname(os.path.abspath(__file__)), "noalloc_contexts_child.py")
+    proc = subprocess.run([sys.executable, child], capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stdout[-2000:] + proc.stderr[-4000:]
