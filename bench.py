@@ -149,6 +149,16 @@ def cpu_model():
     return "unknown"
 
 
+L2_NOTE = ("GPU arm: L2 flushed between timed steps (256 MB write outside the event intervals); the CPU arm (--impl reference) times "
+           "whole steps on the host")
+
+
+def workload_config(wl, num_isect, world):
+    """The workload as both arms describe it (one independent image per GPU; the CPU arm's rank 0 times its share)."""
+    return {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
+            "tile": 16, "top_k": 10, "intersections": num_isect, "parallelism": f"dp{world} (independent images)", "l2": L2_NOTE}
+
+
 def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -176,8 +186,7 @@ def run_reference(args, wl):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded sinusoid target, random Gaussians)",
-        "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
-                   "tile": 16, "top_k": 10, "intersections": num_isect},
+        "config": workload_config(wl, num_isect, args.gpus),
         "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU implementation of this path; this is the oracle's C restatement of its kernels",
@@ -323,9 +332,8 @@ def run_ours(args, wl):
             "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded sinusoid target, random Gaussians; one independent image per GPU)",
-            "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
-                       "tile": 16, "top_k": 10, "intersections": num_isect, "capacity": step.capacity, "parallelism": f"dp{world} (independent images)",
-                       "l2": "flushed between timed steps (256 MB write outside the event intervals)", "graph": "one CUDA graph per step"},
+            "config": workload_config(wl, num_isect, world),
+            "capacity": step.capacity, "graph": "one CUDA graph per step",
             "gaussian_pixel_evals_per_step": evals, "gaussian_pixel_evals_per_s": evals * value,
             "stages_ms": stage_ms,
             "roofline": roofline,

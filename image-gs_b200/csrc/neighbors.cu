@@ -180,7 +180,9 @@ __global__ void __launch_bounds__(kThreads) neighbors_kernel(const int num, cons
             }
             for (int gy = max(0, cy - ring); gy <= min(g.grid_h - 1, cy + ring); ++gy) {
                 const bool edge_row = gy == cy - ring || gy == cy + ring;
-                const int step = edge_row ? 1 : max(2 * ring, 1);  // inner rows of the ring: only its left and right cells
+                // the square's top and bottom rows are walked cell by cell; a row between them meets the square's border in two
+                // cells only, columns cx - ring and cx + ring, so it jumps from one to the other
+                const int step = edge_row ? 1 : max(2 * ring, 1);
                 for (int gx = cx - ring; gx <= cx + ring; gx += step) {
                     if (gx < 0 || gx >= g.grid_w) continue;
                     const int c = gy * g.grid_w + gx;

@@ -7,7 +7,8 @@ lie under the reference tree, with the flags of gsplat/setup.py:45-80 (-O3 --use
 host compiler, the vendored glm on the include path), for sm_100a. Objects and the module go to oracle/_ref/ only; the reference tree is
 read-only. The resulting module is named gsplat_ref_csrc and exposes the reference's pybind functions (gsplat/gsplat/cuda/csrc/ext.cpp:4-32).
 
-Usage: python oracle/build_ref.py [REFERENCE_ROOT]   (default: /root/reference). Needs nvcc, no GPU.
+Usage: python oracle/build_ref.py [REFERENCE_ROOT]. The reference tree is the argument, else $IGS_REFERENCE_ROOT, else this recipe's
+default location (DEFAULT_REFERENCE_ROOT). Needs nvcc, no GPU.
 """
 import glob
 import os
@@ -16,6 +17,12 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 MODULE = "gsplat_ref_csrc"
+DEFAULT_REFERENCE_ROOT = "/root/reference"  # where the build container mounts the reference tree; the GPU machine has none
+
+
+def reference_root(given=None):
+    """The reference tree: the given path, else $IGS_REFERENCE_ROOT, else DEFAULT_REFERENCE_ROOT."""
+    return given or os.environ.get("IGS_REFERENCE_ROOT") or DEFAULT_REFERENCE_ROOT
 
 
 def built_module_path():
@@ -24,8 +31,8 @@ def built_module_path():
     return hits[0] if hits else None
 
 
-def build(reference_root="/root/reference", verbose=False):
-    csrc = os.path.join(reference_root, "gsplat", "gsplat", "cuda", "csrc")
+def build(root=None, verbose=False):
+    csrc = os.path.join(reference_root(root), "gsplat", "gsplat", "cuda", "csrc")
     if not os.path.isdir(csrc):
         raise FileNotFoundError(f"reference CUDA sources not found at {csrc}")
     os.makedirs(OUT, exist_ok=True)
@@ -71,7 +78,7 @@ def prediction_module_path():
     return hits[0] if hits else None
 
 
-def build_prediction(reference_root="/root/reference"):
+def build_prediction(root=None):
     """Compiles the reference's compress/csrc/prediction.cpp (its neighbour search and predictor; a pybind11 module) where it lies, with
     g++ (-O3 -ffp-contract=off -pthread, and the source hash define that compress/common.py:13-27 checks), into oracle/_ref/. It is the
     CPU baseline and checker of the GPU neighbour search."""
@@ -81,7 +88,7 @@ def build_prediction(reference_root="/root/reference"):
 
     from torch.utils.cpp_extension import include_paths
 
-    src = os.path.join(reference_root, "compress", "csrc", "prediction.cpp")
+    src = os.path.join(reference_root(root), "compress", "csrc", "prediction.cpp")
     if not os.path.exists(src):
         raise FileNotFoundError(src)
     os.makedirs(OUT, exist_ok=True)
@@ -108,6 +115,6 @@ def load_prediction():
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
     print(build(root, verbose=True))
     print(build_prediction(root))

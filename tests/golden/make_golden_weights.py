@@ -69,4 +69,6 @@ def main(ref_root, out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2] if len(sys.argv) > 2 else HERE)
+    from oracle.build_ref import reference_root
+
+    main(reference_root(sys.argv[1] if len(sys.argv) > 1 else None), sys.argv[2] if len(sys.argv) > 2 else HERE)
