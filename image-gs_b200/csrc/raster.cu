@@ -574,9 +574,9 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
 //      lanes of a warp holding the same entry are grouped (__match_any_sync) and the group's leader counts it in the warp's own row of
 //      counters; a CTA-wide scan turns the (warp, entry) counts into places; each pair is stored at its place;
 //   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
-//      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v dx, v dy and w v_out (dx, dy from the Gaussian's center), then one
-//      reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = conic (S_x, S_y) (the
-//      reference's per-pixel v (a dx + b dy, b dx + c dy) summed), v_color = S_c.
+//      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v (a dx + b dy), v (b dx + c dy) and w v_out (dx, dy from the Gaussian's
+//      center, a, b, c its conic), then one reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy,
+//      S_yy / 2), v_xy = the last two sums, v_color = S_c.
 template <int kMaxC>
 struct PairSmem {
     float4 geo[kPairStage];            // x, y, conic a, conic b
@@ -621,7 +621,6 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
-    const int lane_of_x = 3 * (32 / NV), lane_of_y = 4 * (32 / NV);  // lanes holding S_x and S_y after the reduce-scatter
     for (int chunk = 0; chunk < len; chunk += kPairStage) {
         const int n_entries = min(kPairStage, len - chunk);
         if (chunk > 0 || restage_first) {
@@ -696,6 +695,7 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             const int b = sm.start[e], n = sm.start[e + 1] - b;
             if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
             const float4 q = sm.geo[e];
+            const float ca = 2.f * q.z, cb = q.w, cc = 2.f * sm.cc[e];  // the staged conic is halved; doubling it back is exact
             float acc[NV];
 #pragma unroll
             for (int v = 0; v < NV; ++v) acc[v] = 0.f;
@@ -709,26 +709,24 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
                 acc[0] = fmaf(tx, dx, acc[0]);
                 acc[1] = fmaf(tx, dy, acc[1]);
                 acc[2] = fmaf(ty, dy, acc[2]);
-                acc[3] += tx;
-                acc[4] += ty;
+                // v_xy per pair, v (a dx + b dy) and v (b dx + c dy) as the reference sums them: with the conic factored out of the
+                // sums, a Sx and b Sy can cancel to a few parts in 10^4 of themselves and lose the result's accuracy
+                acc[3] = fmaf(vw.x, fmaf(ca, dx, cb * dy), acc[3]);
+                acc[4] = fmaf(vw.x, fmaf(cb, dx, cc * dy), acc[4]);
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c)
                     if (c < channels) acc[5 + c] = fmaf(vw.y, sm.vout[c][pix], acc[5 + c]);
             }
             const float total = warp_sum_scatter<NV>(acc, lane);
-            const float sx = __shfl_sync(0xffffffffu, total, lane_of_x), sy = __shfl_sync(0xffffffffu, total, lane_of_y);
             if (holds_total) {
                 const int g = __ldg(&ids_sorted[range.x + chunk + e]);
                 float value, *target;
                 if (value_index < 3) {
                     value = value_index == 1 ? total : 0.5f * total;
                     target = v_conic + 3 * (size_t)g + value_index;
-                } else if (value_index == 3) {
-                    value = (2.f * q.z) * sx + q.w * sy;  // the staged conic is halved; doubling it back is exact
-                    target = v_xy + 2 * (size_t)g;
-                } else if (value_index == 4) {
-                    value = q.w * sx + (2.f * sm.cc[e]) * sy;
-                    target = v_xy + 2 * (size_t)g + 1;
+                } else if (value_index < 5) {
+                    value = total;
+                    target = v_xy + 2 * (size_t)g + (value_index - 3);
                 } else {
                     value = total;
                     target = v_colors + (size_t)g * channels + (value_index - 5);
