@@ -315,10 +315,11 @@ def run_ours(args, wl):
 
     # end to end with host buffers: through the C ABI (the step as above, parameters copied in and the loss read back every step), and
     # through the drop-in gsplat API with autograd (what model.py calls)
-    e2e = e2e_autograd = None
+    e2e = e2e_autograd = e2e_autograd_graph = None
     if not args.no_e2e:
         e2e = run_step_e2e(args, step, step.raw, inp, device, world, "step")
         e2e_autograd = run_e2e(args, wl, inp, device, step.capacity, world)
+        e2e_autograd_graph = run_e2e(args, wl, inp, device, step.capacity, world, graph=True)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -340,7 +341,7 @@ def run_ours(args, wl):
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
-            "e2e": e2e, "e2e_autograd": e2e_autograd, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
+            "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
             "clocks": clk,
         }
         print(json.dumps(out))
@@ -512,7 +513,10 @@ def run_step_e2e(args, step, dev_params, inp, device, world, api):
                    (", both copies captured in the step's CUDA graph)" if api == "step" else ")")}
 
 
-def run_e2e(args, wl, inp, device, capacity, world):
+def run_e2e(args, wl, inp, device, capacity, world, graph=False):
+    """The step through the drop-in gsplat API with autograd and F.l1_loss, as model.py calls it, with the parameters copied in from
+    pinned host memory and the loss read back every step: eagerly (graph=False), or captured in one CUDA graph with the copies, the
+    forward, the loss and the backward pass as model.py's CUDA-graph step does (model.py:1160-1209; the optimizer is outside the metric)."""
     import torch.nn.functional as F
 
     import gsplat
@@ -521,15 +525,16 @@ def run_e2e(args, wl, inp, device, capacity, world):
 
     host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
     target = (inp["loss_target"] if "loss_target" in inp else inp["target"]).to(device)
-    dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+    dev = {k: torch.empty_like(v, device=device).requires_grad_(True) for k, v in host.items()}
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
     tb = wl.tile_bounds
     opts = step_options(wl, device)
 
-    def one():
-        for k in dev:
-            dev[k].copy_(host[k], non_blocking=True)
-        means, scales, rots, feats = [dev[k].requires_grad_(True) for k in ("means", "scales", "rotations", "features")]
+    def body():
+        with torch.no_grad():
+            for k in dev:
+                dev[k].copy_(host[k], non_blocking=True)
+        means, scales, rots, feats = [dev[k] for k in ("means", "scales", "rotations", "features")]
         raw_feats, raw_rots = feats, rots
         if "quant" in opts:  # model._get_params (model.py:993-1006) and the loss-space features (model.py:963-964)
             q = opts["quant"]
@@ -545,9 +550,29 @@ def run_e2e(args, wl, inp, device, capacity, world):
             loss = loss + ag.rate_loss(raw_feats, raw_rots, loss, r["model"], r["inv_rot_step"], 1.0, r["factor"])
         loss.backward()
         loss_host.copy_(loss.detach(), non_blocking=True)
-        for k in dev:
-            dev[k] = dev[k].detach()
-        return loss_host
+
+    def clear_grads():
+        for v in dev.values():
+            v.grad = None
+
+    if graph:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(max(3, args.warmup)):  # eager warm-up on a side stream, as before any capture
+                clear_grads()
+                body()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize()
+        clear_grads()  # backward() then allocates the gradients from the graph's memory pool
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body()
+        one = g.replay
+    else:
+        def one():
+            clear_grads()
+            body()
 
     for _ in range(args.warmup):
         one()
@@ -570,7 +595,9 @@ def run_e2e(args, wl, inp, device, capacity, world):
     return {"value": value, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "api": ("igs_b200.autograd.quantize_ste + feat @ T.T + " if "quant" in opts else "") +
                    "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + F.l1_loss" +
-                   (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward"}
+                   (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward" +
+                   (", copies, forward, loss and backward replayed as one CUDA graph (model.py's graph-captured step)" if graph else
+                    ", eager")}
 
 
 def run_aux(args):
