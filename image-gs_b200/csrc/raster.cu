@@ -90,18 +90,20 @@ __device__ __forceinline__ float halved_sigma(const float4 g4, const float hc, c
 // The top-K selection of PPT pixels per thread over their tile's list (range into ids_sorted), in list order, with the slot rule of the
 // reference: free slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it.
 // The first ten entries fill the slots with fixed indices when all of them are valid for a pixel (what the rule does while slots are
-// free). The list is staged through s_geo / s_cc in chunks of kChunk entries by the CTA's kThreads / PPT threads, with CTA barriers:
-// every thread must call it. The slots live in shared memory, alpha in s_val and the list position in s_pos (both [k * kThreads + lid],
-// position -1 for empty), so an insertion is two dynamic stores instead of a select over ten registers; each pixel keeps the minimum of
-// each half of its slots (0-4, 5-9) and the first slot holding it in registers, so that an insertion rescans only the half it wrote (the
-// first slot of the strict minimum over all ten is the second half's only if that half's minimum is strictly smaller). The staged conic
-// is halved (exactly), which drops a multiplication from sigma, and the PPT pixels of a thread share a column, so dx and its products
-// are shared too. On return val[q][k] holds the slots' alpha. Pixels outside the image (inside[q] false) take no entries.
+// free); only a pixel that cannot take that path starts from empty slots. The list is staged through s_geo / s_cc in chunks of kChunk
+// entries by the CTA's kThreads / PPT threads, with CTA barriers: every thread must call it. The slots live in shared memory, alpha in
+// s_val and the list position in s_pos (both [k * kThreads + lid], position -1 for empty), so an insertion is two dynamic stores instead
+// of a select over ten registers; each pixel keeps the minimum of each half of its slots (0-4, 5-9) and the first slot holding it in
+// registers, so that an insertion rescans only the half it wrote (the first slot of the strict minimum over all ten is the second
+// half's only if that half's minimum is strictly smaller). The staged conic is halved (exactly), which drops a multiplication from
+// sigma, and the PPT pixels of a thread share a column, so dx and its products are shared too. On return val[q][k] holds the slots'
+// alpha. Pixels outside the image (inside[q] false) take no entries.
 template <int PPT>
 __device__ __forceinline__ void select_topk(const int2 range, const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
                                             const float *__restrict__ conics, const PixelCoord (&pc)[PPT], const bool (&inside)[PPT],
                                             float4 *s_geo, float *s_cc, int *s_pos, float *s_val, float (&val)[PPT][kTopK]) {
     constexpr int kStagers = kThreads / PPT;
+    constexpr int kHalf = kTopK / 2;
     const int tid = threadIdx.x;
     const int len = range.y - range.x;
     const float px = (float)pc[0].j;  // the pixels share a column
@@ -109,28 +111,31 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
     int filled[PPT];
     float gv[PPT][2];  // per half of the slots (0-4, 5-9): its minimum and the first slot holding it
     int gs[PPT][2];
-#pragma unroll
-    for (int q = 0; q < PPT; ++q) {
-        py[q] = (float)pc[q].i;
+    auto clear_slots = [&](const int q) {
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
             s_pos[k * kThreads + pc[q].tid] = -1;
             s_val[k * kThreads + pc[q].tid] = 0.f;
         }
+    };
+#pragma unroll
+    for (int q = 0; q < PPT; ++q) {
+        py[q] = (float)pc[q].i;
         filled[q] = inside[q] ? 0 : kTopK;  // a pixel outside the image counts as full with an unbeatable minimum
         min_val[q] = inside[q] ? -1.f : INFINITY;
+        if (len <= 0) clear_slots(q);  // no chunk below: the slots stay empty
     }
     // minimum of one half of a pixel's slots (the first slot on ties)
     auto scan_half = [&](const int q, const int h) {
-        const float *v = s_val + h * (kTopK / 2) * kThreads + pc[q].tid;
+        const float *v = s_val + h * kHalf * kThreads + pc[q].tid;
         float m = v[0];
         int ms = 0;
 #pragma unroll
-        for (int k = 1; k < kTopK / 2; ++k) {
+        for (int k = 1; k < kHalf; ++k) {
             const float x = v[k * kThreads];
             if (x < m) m = x, ms = k;
         }
-        return make_float2(m, __int_as_float(ms + h * (kTopK / 2)));
+        return make_float2(m, __int_as_float(ms + h * kHalf));
     };
     auto rescan = [&](const int q) {
         const float2 h0 = scan_half(q, 0), h1 = scan_half(q, 1);
@@ -169,36 +174,51 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         int start[PPT];  // first entry of the chunk each pixel still has to consider
 #pragma unroll
         for (int q = 0; q < PPT; ++q) start[q] = 0;
-        if (base == 0 && count >= kTopK) {
-            // fast fill, per pixel: all of the first ten entries valid -> slots 0..9 in order
+        if (base == 0) {
+            // fast fill, per pixel: all of the first ten entries valid -> slots 0..9 in order, the half minima from registers; any other
+            // pixel starts from empty slots
             float sig[PPT][kTopK];
+            if (count >= kTopK) {
 #pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                const float4 g4 = s_geo[k];
-                const float cc = s_cc[k];
-                float s[PPT];
-                column_sigma<PPT>(g4, cc, px, py, s);
+                for (int k = 0; k < kTopK; ++k) {
+                    const float4 g4 = s_geo[k];
+                    const float cc = s_cc[k];
+                    float sk[PPT];
+                    column_sigma<PPT>(g4, cc, px, py, sk);
 #pragma unroll
-                for (int q = 0; q < PPT; ++q) sig[q][k] = s[q];
+                    for (int q = 0; q < PPT; ++q) sig[q][k] = sk[q];
+                }
             }
 #pragma unroll
             for (int q = 0; q < PPT; ++q) {
-                if (!inside[q]) {
-                    start[q] = kTopK;  // never inserts: keeps the pixels' starts equal in the common case below
+                bool fast = count >= kTopK && inside[q];
+                if (fast) {
+#pragma unroll
+                    for (int k = 0; k < kTopK; ++k) fast = fast && sigma_valid(sig[q][k]);
+                }
+                if (!fast) {
+                    clear_slots(q);
+                    if (!inside[q] && count >= kTopK) start[q] = kTopK;  // never inserts: keeps the pixels' starts equal below
                     continue;
                 }
-                bool all_valid = true;
-#pragma unroll
-                for (int k = 0; k < kTopK; ++k) all_valid = all_valid && sigma_valid(sig[q][k]);
-                if (!all_valid) continue;
+                float a[kTopK];
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) {
-                    const float alpha = __expf(-sig[q][k]);
-                    s_val[k * kThreads + pc[q].tid] = alpha;
+                    a[k] = __expf(-sig[q][k]);
+                    s_val[k * kThreads + pc[q].tid] = a[k];
                     s_pos[k * kThreads + pc[q].tid] = k;
                 }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float m = a[h * kHalf];
+                    int ms = h * kHalf;
+#pragma unroll
+                    for (int k = 1; k < kHalf; ++k)
+                        if (a[h * kHalf + k] < m) m = a[h * kHalf + k], ms = h * kHalf + k;
+                    gv[q][h] = m, gs[q][h] = ms;
+                }
+                min_val[q] = fminf(gv[q][0], gv[q][1]);
                 filled[q] = kTopK;
-                rescan(q);
                 start[q] = kTopK;
             }
         }
@@ -207,31 +227,31 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         for (int q = 1; q < PPT; ++q) e = min(e, start[q]);
         if (all_full()) {
             // the common case: every pixel full (all starts equal), only the replacement rule
+#pragma unroll 2
             for (; e < count; ++e) {
                 const float4 g4 = s_geo[e];
                 const float cc = s_cc[e];
-                float s[PPT];
-                column_sigma<PPT>(g4, cc, px, py, s);
+                float sk[PPT];
+                column_sigma<PPT>(g4, cc, px, py, sk);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
-                    // every slot holds an alpha >= 0 (the minimum of a pixel outside the image is infinite), so sigma >= 0 suffices:
-                    // an infinite sigma gives alpha = 0, which replaces nothing, and NaN fails the test
-                    const float sigma = s[q];
-                    if (!(sigma >= 0.f)) continue;
+                    // every slot holds an alpha >= 0 (the minimum of a pixel outside the image is infinite), so sigma >= 0 suffices: an
+                    // infinite sigma gives alpha = 0, which replaces nothing, and NaN fails the test
+                    const float sigma = sk[q];
                     const float alpha = __expf(-sigma);
-                    if (alpha > min_val[q]) insert(q, alpha, base + e);
+                    if (sigma >= 0.f && alpha > min_val[q]) insert(q, alpha, base + e);
                 }
             }
         } else {
             for (; e < count; ++e) {
                 const float4 g4 = s_geo[e];
                 const float cc = s_cc[e];
-                float s[PPT];
-                column_sigma<PPT>(g4, cc, px, py, s);
+                float sk[PPT];
+                column_sigma<PPT>(g4, cc, px, py, sk);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
                     if (e < start[q]) continue;
-                    const float sigma = s[q];
+                    const float sigma = sk[q];
                     if (!sigma_valid(sigma)) continue;
                     const float alpha = __expf(-sigma);
                     if (filled[q] < kTopK) {
@@ -346,12 +366,9 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
         int pos[kTopK], gid[kTopK];
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) pos[k] = s_ids[k * kThreads + pc[q].tid];
-        // normalized sum over the slots in slot order; the reference normalizes in double (sum + 1e-4 with a double epsilon)
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k)
-            if (pos[k] >= 0) sum += val[q][k];
-        const double inv = 1.0 / ((double)sum + igs::kNormEps);
+        // the normalized sum U / D: U = sum_k d_k f_k and D = 1e-4 + sum_k d_k accumulated in slot order, one reciprocal (within a few
+        // float roundings of the reference's per-slot double-precision division; the training step's kernel computes the same)
+        float denom = (float)igs::kNormEps;
         float pix[kMaxC];
 #pragma unroll
         for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
@@ -359,11 +376,12 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
 #pragma unroll
             for (int k = 0; k < kTopK; ++k) {
                 if (pos[k] < 0) continue;
-                const float vis = (float)((double)val[q][k] * inv);
+                const float d = val[q][k];
+                denom += d;
                 const float4 f = s_geo[pos[k]];
                 const float fc[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-                for (int c = 0; c < kMaxC && c < 4; ++c) pix[c] += fc[c] * vis;
+                for (int c = 0; c < kMaxC && c < 4; ++c) pix[c] = fmaf(d, fc[c], pix[c]);
             }
         } else {
 #pragma unroll
@@ -371,13 +389,17 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
 #pragma unroll
             for (int k = 0; k < kTopK; ++k) {
                 if (gid[k] < 0) continue;
-                const float vis = (float)((double)val[q][k] * inv);
+                const float d = val[q][k];
+                denom += d;
                 const float *f = colors + (size_t)gid[k] * channels;
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c)
-                    if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+                    if (c < channels) pix[c] = fmaf(d, __ldg(&f[c]), pix[c]);
             }
         }
+        const float inv_denom = 1.f / denom;
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) pix[c] *= inv_denom;
         const int p = (pc[q].i - row_begin * kTile) * img_w + pc[q].j;
         if (inside[q]) {
 #pragma unroll
@@ -567,28 +589,38 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
 
 // ---- backward pass from the tile lists, pairs grouped by Gaussian ---------------------------------------------------------------------
 //
-// One CTA of 256 threads (one per pixel) per tile; lists longer than kPairStage entries go through steps 2-3 in chunks of kPairStage:
-//   1. per pixel: d_k = exp(-sigma_k), the colour weight w_k = d_k / D and v_k = dL/dsigma_k of its top-K entries (the reference's
-//      algebra, backward.cu:219-265) into shared memory, with the pixel's v_out and coordinates;
+// The reference's per-pixel algebra (backward.cu:219-265): with D = 1e-4 + sum_k d_k, s_k = f_k . v_out and
+// S = -sum_k d_k s_k / D^2, dL/dsigma_k = -d_k (s_k / D + S) and the colour weight is d_k / D. Since sum_k d_k s_k = v_out . U with
+// U = sum_k d_k f_k (the unnormalised render), a pixel's pairs need only d_k, D, S and v_out: s_k is formed where the pair is summed,
+// from the entry's colour, which is the same for every pair of that entry, so no per-pair gradient is stored. One CTA of 256 threads (one per pixel) per tile; lists longer than kPairStage entries go through steps 2-3
+// in chunks of kPairStage:
+//   1. per pixel: its slots' d_k (the selection's alphas, or exp(-sigma_k) recomputed from the tile lists) in shared memory, and its
+//      coordinates, 1 / D, S and v_out;
 //   2. the tile's (pixel, slot) pairs are grouped by list position with a counting sort in shared memory without atomics: per slot the
 //      lanes of a warp holding the same entry are grouped (__match_any_sync) and the group's leader counts it in the warp's own row of
 //      counters; a CTA-wide scan turns the (warp, entry) counts into places; each pair is stored at its place;
 //   3. one warp per entry: the lanes stride over the entry's pairs (consecutive records are mostly consecutive pixels, so the shared
-//      reads do not conflict) summing v dx^2, v dx dy, v dy^2, v (a dx + b dy), v (b dx + c dy) and w v_out (dx, dy from the Gaussian's
-//      center, a, b, c its conic), then one reduce-scatter over the warp and one global atomic per value: v_conic = (S_xx / 2, S_xy,
-//      S_yy / 2), v_xy = the last two sums, v_color = S_c.
+//      reads do not conflict), form v = dL/dsigma and w = d / D of each and sum v dx^2, v dx dy, v dy^2, v (a dx + b dy), v (b dx + c dy)
+//      and w v_out (dx, dy from the Gaussian's center, a, b, c its conic), then one reduce-scatter over the warp and one global atomic per
+//      value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = the next two sums, v_color = S_c.
 template <int kMaxC>
 struct PairSmem {
-    float4 geo[kPairStage];            // x, y, conic a, conic b
-    float cc[kPairStage];              // conic c
-    float col[kPairStage * kMaxC];     // features
-    float2 vw[kTopK][kThreads];        // (dL/dsigma, colour weight) per slot and pixel; in the fused step kernel first the
-                                       // selection's list positions and alphas ([kTopK][kThreads] each)
-    float vout[kMaxC][kThreads];       // dL/dout per channel and pixel
-    float2 pxy[kThreads];              // pixel coordinates
-    uint16_t pairs[kPairs];            // (slot << 8) | pixel, grouped by entry
-    int start[kPairStage + 1];         // segment starts
-    uint16_t wcnt[kThreads / 32][kPairStage];  // pairs per (warp, entry), then each warp's first place in the entry's segment
+    static constexpr bool kPackedOut = kMaxC <= 4;  // a pixel's v_out as one float4
+    float4 geo[kPairStage];         // x, y, conic a / 2, conic b
+    float cc[kPairStage];           // conic c / 2
+    float col[kPairStage * kMaxC];  // features
+    union {
+        int pos[kTopK][kThreads];  // the selection's slots: positions in the tile's list (-1 empty), read into registers before step 2
+        struct {
+            uint16_t pairs[kPairs];                    // (slot << 8) | pixel, grouped by entry
+            uint16_t wcnt[kThreads / 32][kPairStage];  // pairs per (warp, entry), then each warp's first place in the entry's segment
+            int start[kPairStage + 1];                 // segment starts
+        } g;
+    };
+    float alpha[kTopK][kThreads];                // d_k = exp(-sigma_k) of each slot (the selection's alphas)
+    float4 pix[kThreads];                        // x, y, 1 / D, S
+    float4 vout4[kPackedOut ? kThreads : 1];     // v_out (C <= 4)
+    float vout[kPackedOut ? 1 : kMaxC][kPackedOut ? 1 : kThreads];  // v_out per channel (C > 4)
     int wsum[kThreads / 32];
 };
 
@@ -610,9 +642,38 @@ __device__ __forceinline__ void stage_pair_chunk(PairSmem<kMaxC> &sm, const int 
     }
 }
 
-// Steps 2 and 3 of the pairs-grouped backward pass for one tile (every thread of the CTA calls it): sm.vw, sm.vout and sm.pxy hold step
-// 1's per-pair and per-pixel values, key[k] the list position of the thread's slot k (-1 empty). The staged chunk of the list is used for
-// chunk 0 unless restage_first; every other chunk is staged by stage(chunk).
+// Step 1's per-pixel values: 1 / D and S = -sum_k d_k s_k / D^2 (s_k = f_k . v_out), formed as -(v_out . U) / D^2 from the pixel's
+// U = sum_k d_k f_k: the same sum in another order (the reference adds the slots' terms, backward.cu:243-252), without reading the
+// slots' features again. The reference's divisions by D and D^2 are products with approximate reciprocals under fast math; so are these.
+template <int kMaxC>
+__device__ __forceinline__ float2 pixel_terms(const float denom, const float (&u)[kMaxC], const float (&v_out)[kMaxC]) {
+    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
+    float vu = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxC; ++c) vu = fmaf(v_out[c], u[c], vu);
+    return make_float2(inv, -inv2 * vu);
+}
+
+// Step 1's per-pixel record: coordinates, 1 / D, S and v_out
+template <int kMaxC>
+__device__ __forceinline__ void store_pixel_grad(PairSmem<kMaxC> &sm, const int tid, const float px, const float py, const float2 terms,
+                                                 const float (&v_out)[kMaxC]) {
+    sm.pix[tid] = make_float4(px, py, terms.x, terms.y);
+    if constexpr (PairSmem<kMaxC>::kPackedOut) {
+        float v4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) v4[c] = v_out[c];
+        sm.vout4[tid] = make_float4(v4[0], v4[1], v4[2], v4[3]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+    }
+}
+
+// Steps 2 and 3 of the pairs-grouped backward pass for one tile (every thread of the CTA calls it, after a CTA barrier that follows the
+// last read of sm.pos): sm.alpha and sm.pix / sm.vout hold step 1's per-slot and per-pixel values, key[k] the list position of the
+// thread's slot k (-1 empty). The staged chunk of the list is used for chunk 0 unless restage_first; every other chunk is staged by
+// stage(chunk).
 template <int NV, int kMaxC, typename Stage>
 __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const int (&key)[kTopK], const int len, const int2 range,
                                                    const int *__restrict__ ids_sorted, const int channels, const bool restage_first,
@@ -631,7 +692,7 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
         // 2. counting sort of this chunk's pairs by entry without atomics: per slot, the lanes of a warp holding the same entry are grouped
         //    with __match_any_sync; each warp counts its pairs per entry in its own row of wcnt (a group's leader adds the group, so no
         //    two lanes write one counter), which also gives each pair its place among the warp's pairs of that entry (< 32: 5 bits)
-        for (int e = lane; e < n_entries; e += 32) sm.wcnt[warp][e] = 0;
+        for (int e = lane; e < n_entries; e += 32) sm.g.wcnt[warp][e] = 0;
         __syncwarp();
         unsigned off_lo = 0u, off_hi = 0u;  // the pairs' places, 5 bits per slot
 #pragma unroll
@@ -640,9 +701,9 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
             const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
             const unsigned below = peers & ((1u << lane) - 1u);
-            const int base = mine ? (int)sm.wcnt[warp][e] : 0;
+            const int base = mine ? (int)sm.g.wcnt[warp][e] : 0;
             __syncwarp();
-            if (mine && below == 0u) sm.wcnt[warp][e] = (uint16_t)(base + __popc(peers));
+            if (mine && below == 0u) sm.g.wcnt[warp][e] = (uint16_t)(base + __popc(peers));
             __syncwarp();
             const unsigned off = (unsigned)(base + __popc(below)) & 31u;
             if (k < 6) off_lo |= off << (5 * k);
@@ -656,8 +717,8 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             if (e < n_entries) {
 #pragma unroll
                 for (int w = 0; w < kThreads / 32; ++w) {
-                    const int c = sm.wcnt[w][e];
-                    sm.wcnt[w][e] = (uint16_t)total;
+                    const int c = sm.g.wcnt[w][e];
+                    sm.g.wcnt[w][e] = (uint16_t)total;
                     total += c;
                 }
             }
@@ -674,11 +735,11 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             for (int w = 0; w < kThreads / 32; ++w) before += w < warp ? sm.wsum[w] : 0;
             const int start = before + incl - total;
             if (e < n_entries) {
-                sm.start[e] = start;
+                sm.g.start[e] = start;
 #pragma unroll
-                for (int w = 0; w < kThreads / 32; ++w) sm.wcnt[w][e] = (uint16_t)(sm.wcnt[w][e] + start);
+                for (int w = 0; w < kThreads / 32; ++w) sm.g.wcnt[w][e] = (uint16_t)(sm.g.wcnt[w][e] + start);
             }
-            if (e == n_entries - 1) sm.start[n_entries] = start + total;
+            if (e == n_entries - 1) sm.g.start[n_entries] = start + total;
         }
         __syncthreads();
 #pragma unroll
@@ -686,36 +747,54 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             const int e = key[k] - chunk;
             const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
             const unsigned off = (k < 6 ? off_lo >> (5 * k) : off_hi >> (5 * (k - 6))) & 31u;
-            if (mine) sm.pairs[sm.wcnt[warp][e] + off] = (uint16_t)((k << 8) | tid);
+            if (mine) sm.g.pairs[sm.g.wcnt[warp][e] + off] = (uint16_t)((k << 8) | tid);
         }
         __syncthreads();
 
         // 3. one warp per entry
         for (int e = warp; e < n_entries; e += kThreads / 32) {
-            const int b = sm.start[e], n = sm.start[e + 1] - b;
+            const int b = sm.g.start[e], n = sm.g.start[e + 1] - b;
             if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
             const float4 q = sm.geo[e];
             const float ca = 2.f * q.z, cb = q.w, cc = 2.f * sm.cc[e];  // the staged conic is halved; doubling it back is exact
+            float f[kMaxC];
+#pragma unroll
+            for (int c = 0; c < kMaxC; ++c) f[c] = c < channels ? sm.col[e * kMaxC + c] : 0.f;
             float acc[NV];
 #pragma unroll
             for (int v = 0; v < NV; ++v) acc[v] = 0.f;
             for (int i = lane; i < n; i += 32) {
-                const unsigned rec = sm.pairs[b + i];
+                const unsigned rec = sm.g.pairs[b + i];
                 const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
-                const float2 vw = sm.vw[slot][pix];
-                const float2 xy = sm.pxy[pix];
-                const float dx = q.x - xy.x, dy = q.y - xy.y;
-                const float tx = vw.x * dx, ty = vw.x * dy;
+                const float d = sm.alpha[slot][pix];
+                const float4 pr = sm.pix[pix];  // x, y, 1 / D, S
+                float vo[kMaxC];
+                if constexpr (PairSmem<kMaxC>::kPackedOut) {
+                    const float4 v4 = sm.vout4[pix];
+                    const float va[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                    for (int c = 0; c < kMaxC; ++c) vo[c] = va[c];
+                } else {
+#pragma unroll
+                    for (int c = 0; c < kMaxC; ++c) vo[c] = c < channels ? sm.vout[c][pix] : 0.f;
+                }
+                float sk = 0.f;  // f_k . v_out in the reference's channel order
+#pragma unroll
+                for (int c = 0; c < kMaxC; ++c) sk = fmaf(f[c], vo[c], sk);
+                const float vs = -d * fmaf(sk, pr.z, pr.w);  // dL/dsigma
+                const float wk = d * pr.z;                   // the colour weight d / D
+                const float dx = q.x - pr.x, dy = q.y - pr.y;
+                const float tx = vs * dx, ty = vs * dy;
                 acc[0] = fmaf(tx, dx, acc[0]);
                 acc[1] = fmaf(tx, dy, acc[1]);
                 acc[2] = fmaf(ty, dy, acc[2]);
                 // v_xy per pair, v (a dx + b dy) and v (b dx + c dy) as the reference sums them: with the conic factored out of the
                 // sums, a Sx and b Sy can cancel to a few parts in 10^4 of themselves and lose the result's accuracy
-                acc[3] = fmaf(vw.x, fmaf(ca, dx, cb * dy), acc[3]);
-                acc[4] = fmaf(vw.x, fmaf(cb, dx, cc * dy), acc[4]);
+                acc[3] = fmaf(vs, fmaf(ca, dx, cb * dy), acc[3]);
+                acc[4] = fmaf(vs, fmaf(cb, dx, cc * dy), acc[4]);
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c)
-                    if (c < channels) acc[5 + c] = fmaf(vw.y, sm.vout[c][pix], acc[5 + c]);
+                    if (c < channels) acc[5 + c] = fmaf(wk, vo[c], acc[5 + c]);
             }
             const float total = warp_sum_scatter<NV>(acc, lane);
             if (holds_total) {
@@ -778,73 +857,48 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
         const PixelCoord pcs[1] = {pc};
         const bool ins[1] = {inside};
         float val[1][kTopK];
-        int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and values
-        float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
-        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
+        select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, &sm.pos[0][0], &sm.alpha[0][0], val);
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
-        __syncthreads();  // the staging arrays and the positions' scratch (sm.vw) are reused below
+        for (int k = 0; k < kTopK; ++k) key[k] = sm.pos[k][tid];
+        __syncthreads();  // the staging arrays and the positions (sm.pos, shared with step 2's arrays) are reused below
     }
 
     // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
     // memory in step 1)
     auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
     stage(0);
-    sm.pxy[tid] = make_float2(px, py);
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
     __syncthreads();
 
-    // 1. per-pixel gradients with respect to sigma and the colour weights (the reference's algebra, backward.cu:219-265, its divisions
-    //    by denom written as products with two reciprocals computed once)
-    float d[kTopK], s[kTopK];
+    // 1. the slots' d_k = exp(-sigma_k) (the reference's sigma, forward.cu:309-311) and the pixel's record
     float denom = (float)igs::kNormEps;
-    if (len <= kPairStage) {
-        // the whole list is staged: every slot reads shared memory
+    float u[kMaxC];
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            d[k] = 0.f, s[k] = 0.f;
-            if (key[k] < 0) continue;
-            const int e = key[k];
-            const float4 q = sm.geo[e];
-            d[k] = __expf(-halved_sigma(q, sm.cc[e], px, py));
-            denom += d[k];
+    for (int c = 0; c < kMaxC; ++c) u[c] = 0.f;
 #pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += sm.col[e * kMaxC + c] * v_out[c];
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            d[k] = 0.f, s[k] = 0.f;
-            if (key[k] < 0) continue;
-            float gx, gy, a, b, c;
+    for (int k = 0; k < kTopK; ++k) {
+        float d = 0.f;
+        if (key[k] >= 0) {
             if (key[k] < kPairStage) {
-                const float4 q = sm.geo[key[k]];
-                gx = q.x, gy = q.y, a = 2.f * q.z, b = q.w, c = 2.f * sm.cc[key[k]];
+                const int e = key[k];
+                d = __expf(-halved_sigma(sm.geo[e], sm.cc[e], px, py));
 #pragma unroll
-                for (int ch = 0; ch < kMaxC; ++ch)
-                    if (ch < channels) s[k] += sm.col[key[k] * kMaxC + ch] * v_out[ch];
+                for (int c = 0; c < kMaxC; ++c)
+                    if (c < channels) u[c] = fmaf(d, sm.col[e * kMaxC + c], u[c]);
             } else {
+                // past the staged chunk of a longer list
                 const int g = __ldg(&ids_sorted[range.x + key[k]]);
                 const float2 xy = __ldg(&xys[g]);
-                gx = xy.x, gy = xy.y, a = __ldg(&conics[3 * g]), b = __ldg(&conics[3 * g + 1]), c = __ldg(&conics[3 * g + 2]);
+                d = __expf(-igs::gaussian_sigma(xy.x, xy.y, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2]), px,
+                                                py));
 #pragma unroll
-                for (int ch = 0; ch < kMaxC; ++ch)
-                    if (ch < channels) s[k] += __ldg(&colors[(size_t)g * channels + ch]) * v_out[ch];
+                for (int c = 0; c < kMaxC; ++c)
+                    if (c < channels) u[c] = fmaf(d, __ldg(&colors[(size_t)g * channels + c]), u[c]);
             }
-            d[k] = __expf(-igs::gaussian_sigma(gx, gy, a, b, c, px, py));
-            denom += d[k];
+            denom += d;
         }
+        sm.alpha[k][tid] = d;
     }
-    // fast-math division is a product with the approximate reciprocal, so the reference's x / denom and x / (denom * denom) are these
-    // products, in its order of operations
-    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
-    float shared = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
+    store_pixel_grad(sm, tid, px, py, pixel_terms<kMaxC>(denom, u, v_out), v_out);
 
     pairs_grouped_sums<NV>(sm, key, len, range, ids_sorted, channels, false, stage, v_xy, v_conic, v_colors);
 }
@@ -853,11 +907,11 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
 //
 // With the L1 loss, the gradient with respect to the image, sign(image - target) * ratio / numel, is known as soon as a pixel's value is.
 // So one CTA per tile (256 threads, one pixel each) runs the forward and the backward pass of its tile back to back:
-//   * the top-K selection (select_topk, slots in sm.vw's space), the normalized sum, the image, the tile's part of the loss and the
-//     pixel's loss gradient;
-//   * the backward's step 1 from the selection's alphas and list positions (the backward pass recomputes the same alphas bit for bit),
-//     then steps 2 and 3 (pairs_grouped_sums) on the list still staged in shared memory.
-// Neither the top-K lists nor the image gradient go through HBM, and each slot's alpha is computed once.
+//   * the top-K selection (select_topk, slots in sm.pos / sm.alpha), the normalized sum U / D, the image, the tile's part of the loss
+//     and the pixel's loss gradient;
+//   * the backward's step 1 from the selection's alphas (the backward pass recomputes the same alphas bit for bit, so they stay in
+//     shared memory) and the render's U, then steps 2 and 3 (pairs_grouped_sums) on the list still staged in shared memory.
+// Neither the top-K lists nor the image gradient go through HBM, and each slot's alpha and colour are read once for the render.
 template <int C, int NV>
 __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     raster_step_kernel(const int tiles_x, const int img_h, const int img_w, const int row_begin, const int band_h, const int channels_rt,
@@ -881,15 +935,13 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     const int p = inside ? (pc.i - row_begin * kTile) * img_w + pc.j : 0;
 
     // 1. forward: the top-K selection; a one-chunk list keeps its staged geometry and gets its colours staged beside it
-    int *positions = reinterpret_cast<int *>(&sm.vw[0][0]);  // sm.vw (2 x kTopK x kThreads words) holds positions and alphas
-    float *values = reinterpret_cast<float *>(&sm.vw[0][0]) + kTopK * kThreads;
     const PixelCoord pcs[1] = {pc};
     const bool ins[1] = {inside};
     float val[1][kTopK];
-    select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, positions, values, val);
+    select_topk<1>(range, ids_sorted, xys, conics, pcs, ins, sm.geo, sm.cc, &sm.pos[0][0], &sm.alpha[0][0], val);
     int key[kTopK];
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) key[k] = positions[k * kThreads + tid];
+    for (int k = 0; k < kTopK; ++k) key[k] = sm.pos[k][tid];
     const bool one_chunk = len <= kPairStage;
     if (one_chunk) {
         for (int e = tid; e < len; e += kThreads) {
@@ -898,81 +950,54 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
             for (int c = 0; c < kMaxC; ++c)
                 if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
         }
-        __syncthreads();
     }
+    __syncthreads();  // the colours are staged, and every slot position is read (sm.pos is step 2's space)
 
-    // 2. the pixel's value (normalized in double, as the reference), the image, the L1 loss and its gradient
+    // 2. the pixel's value U / D (U = sum_k d_k f_k in slot order, D = 1e-4 + sum_k d_k), the image, the L1 loss and its gradient
     float target[kMaxC];
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) target[c] = (inside && c < channels) ? __ldcs(&l1.target[(size_t)c * num_pixels + p]) : 0.f;
-    float sum = 0.f;
+    float denom = (float)igs::kNormEps;
+    float u[kMaxC];
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k)
-        if (key[k] >= 0) sum += val[0][k];
-    const double inv_sum = 1.0 / ((double)sum + igs::kNormEps);
-    float pix[kMaxC];
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) pix[c] = 0.f;
+    for (int c = 0; c < kMaxC; ++c) u[c] = 0.f;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
         if (key[k] < 0) continue;
-        const float vis = (float)((double)val[0][k] * inv_sum);
+        const float d = val[0][k];
+        denom += d;
         if (one_chunk) {
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) pix[c] += sm.col[key[k] * kMaxC + c] * vis;
+                if (c < channels) u[c] = fmaf(d, sm.col[key[k] * kMaxC + c], u[c]);
         } else {
             const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) pix[c] += __ldg(&f[c]) * vis;
+                if (c < channels) u[c] = fmaf(d, __ldg(&f[c]), u[c]);
         }
     }
+    const float inv_denom = 1.f / denom;
     float v_out[kMaxC];
     float acc = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxC; ++c) {
         v_out[c] = 0.f;
         if (!inside || c >= channels) continue;
-        out_img[(size_t)c * num_pixels + p] = pix[c];
-        const float d = pix[c] - target[c];
+        const float pix = u[c] * inv_denom;
+        out_img[(size_t)c * num_pixels + p] = pix;
+        const float d = pix - target[c];
         acc += fabsf(d);
         v_out[c] = l1_sign(d) * l1.grad_value;
         if (l1.v_output != nullptr) __stcs(&l1.v_output[(size_t)c * num_pixels + p], v_out[c]);
     }
-    const float total = cta_sum(acc, reinterpret_cast<float *>(sm.wsum));  // its barriers also end every read of the slots
+    const float total = cta_sum(acc, reinterpret_cast<float *>(sm.wsum));
     if (tid == 0) l1.partials[tile] = total;
     if (len <= 0) return;
 
-    // 3. backward, step 1 (the reference's algebra, backward.cu:219-265, as raster_bwd_pairs_kernel) from the selection's alphas
-    float d[kTopK], s[kTopK];
-    float denom = (float)igs::kNormEps;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        d[k] = 0.f, s[k] = 0.f;
-        if (key[k] < 0) continue;
-        d[k] = val[0][k];
-        denom += d[k];
-        if (one_chunk) {
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += sm.col[key[k] * kMaxC + c] * v_out[c];
-        } else {
-            const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) s[k] += __ldg(&f[c]) * v_out[c];
-        }
-    }
-    const float inv = 1.f / denom, inv2 = 1.f / (denom * denom);
-    float shared = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) shared += -d[k] * inv2 * s[k];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) sm.vw[k][tid] = make_float2(-d[k] * (s[k] * inv + shared), d[k] * inv);
-    sm.pxy[tid] = make_float2((float)pc.j, (float)pc.i);
-#pragma unroll
-    for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+    // 3. backward, step 1: the pixel's record (the slots' d_k are the selection's alphas, in sm.alpha)
+    const float2 terms = pixel_terms<kMaxC>(denom, u, v_out);
+    store_pixel_grad(sm, tid, (float)pc.j, (float)pc.i, terms, v_out);
 
     // 4. backward, steps 2 and 3
     auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };

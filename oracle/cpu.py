@@ -109,6 +109,17 @@ def raster_bwd(h, w, xys, conics, colors, v_output, pixel_topk):
     return v_xy, v_conic, v_colors
 
 
+def raster_bwd_abs(h, w, xys, conics, colors, v_output, pixel_topk):
+    """The sums of |term| behind each gradient value of raster_bwd (the float-rounding scale of a summed gradient) -> v_xy, v_conic,
+    v_colors magnitudes"""
+    xys, conics, colors, v_output, pixel_topk = _f32(xys), _f32(conics), _f32(colors), _f32(v_output), _i32(pixel_topk)
+    n, c = colors.shape
+    v_xy, v_conic, v_colors = np.zeros((n, 2), np.float32), np.zeros((n, 3), np.float32), np.zeros((n, c), np.float32)
+    lib().orc_raster_bwd_abs(int(h), int(w), c, n, _p(xys), _p(conics), _p(colors), _p(v_output), _p(pixel_topk), _p(v_xy), _p(v_conic),
+                             _p(v_colors))
+    return v_xy, v_conic, v_colors
+
+
 def loo_loss_increase(h, w, xys, conics, colors, pixel_topk, targets, squared, eps):
     """forward.cu:667-738 -> loss_increase [N]"""
     xys, conics, colors, pixel_topk, targets = _f32(xys), _f32(conics), _f32(colors), _i32(pixel_topk), _f32(targets)

@@ -381,6 +381,7 @@ typedef struct {
     const float *xys, *conics, *colors, *v_output;
     const int *pixel_topk;
     double *acc; /* parts x n x (5 + C) */
+    int absolute; /* sum the terms' magnitudes instead (orc_raster_bwd_abs) */
 } bwd_ctx;
 
 static void raster_bwd_part(void *arg, int part_begin, int part_end) {
@@ -419,6 +420,15 @@ static void raster_bwd_part(void *arg, int part_begin, int part_end) {
                 const float dx = x->xys[2 * g] - px, dy = x->xys[2 * g + 1] - py;
                 const float a = x->conics[3 * g], b = x->conics[3 * g + 1], c2 = x->conics[3 * g + 2];
                 double *o = &acc[(size_t)g * nv];
+                if (x->absolute) {
+                    o[0] += fabs(0.5f * vs * dx * dx);
+                    o[1] += fabs(vs * dx * dy);
+                    o[2] += fabs(0.5f * vs * dy * dy);
+                    o[3] += fabs(vs * (a * dx + b * dy));
+                    o[4] += fabs(vs * (b * dx + c2 * dy));
+                    for (int c = 0; c < channels; ++c) o[5 + c] += fabs(w * v_out[c]);
+                    continue;
+                }
                 o[0] += 0.5f * vs * dx * dx;
                 o[1] += vs * dx * dy;
                 o[2] += 0.5f * vs * dy * dy;
@@ -430,13 +440,13 @@ static void raster_bwd_part(void *arg, int part_begin, int part_end) {
     }
 }
 
-void orc_raster_bwd(int img_h, int img_w, int channels, int n, const float *xys, const float *conics, const float *colors,
-                    const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors) {
+static void raster_bwd_sums(int img_h, int img_w, int channels, int n, const float *xys, const float *conics, const float *colors,
+                            const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors, int absolute) {
     const int nv = 5 + channels;
     /* static pixel ranges per part, each with its own accumulator, summed in part order: deterministic for a given thread count */
     const int parts = g_threads;
     double *acc = (double *)calloc((size_t)parts * n * nv, sizeof(double));
-    bwd_ctx ctx = {img_h, img_w, channels, n, parts, xys, conics, colors, v_output, pixel_topk, acc};
+    bwd_ctx ctx = {img_h, img_w, channels, n, parts, xys, conics, colors, v_output, pixel_topk, acc, absolute};
     parallel_for(parts, 1, raster_bwd_part, &ctx);
     for (int g = 0; g < n; ++g) {
         double o[5 + ORC_MAX_CHANNELS] = {0.0};
@@ -450,6 +460,21 @@ void orc_raster_bwd(int img_h, int img_w, int channels, int n, const float *xys,
         for (int c = 0; c < channels; ++c) v_colors[(size_t)g * channels + c] = (float)o[5 + c];
     }
     free(acc);
+}
+
+void orc_raster_bwd(int img_h, int img_w, int channels, int n, const float *xys, const float *conics, const float *colors,
+                    const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors) {
+    raster_bwd_sums(img_h, img_w, channels, n, xys, conics, colors, v_output, pixel_topk, v_xy, v_conic, v_colors, 0);
+}
+
+/*
+ * The magnitudes of the same per-pixel terms summed per Gaussian: sum |term| for each value of v_xy, v_conic, v_colors. Two float
+ * summations of one gradient in different orders differ by up to a small multiple of the unit roundoff times this sum, however much the
+ * terms cancel; the tests use it as the scale of that rounding.
+ */
+void orc_raster_bwd_abs(int img_h, int img_w, int channels, int n, const float *xys, const float *conics, const float *colors,
+                        const float *v_output, const int *pixel_topk, float *v_xy, float *v_conic, float *v_colors) {
+    raster_bwd_sums(img_h, img_w, channels, n, xys, conics, colors, v_output, pixel_topk, v_xy, v_conic, v_colors, 1);
 }
 
 /*
