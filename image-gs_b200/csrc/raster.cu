@@ -609,6 +609,7 @@ struct PairSmem {
     float4 geo[kPairStage];         // x, y, conic a / 2, conic b
     float cc[kPairStage];           // conic c / 2
     float col[kPairStage * kMaxC];  // features
+    int gid[kPairStage];            // Gaussian IDs
     union {
         int pos[kTopK][kThreads];  // the selection's slots: positions in the tile's list (-1 empty), read into registers before step 2
         struct {
@@ -618,9 +619,9 @@ struct PairSmem {
         } g;
     };
     float alpha[kTopK][kThreads];                // d_k = exp(-sigma_k) of each slot (the selection's alphas)
-    float4 pix[kThreads];                        // x, y, 1 / D, S
-    float4 vout4[kPackedOut ? kThreads : 1];     // v_out (C <= 4)
-    float vout[kPackedOut ? 1 : kMaxC][kPackedOut ? 1 : kThreads];  // v_out per channel (C > 4)
+    float4 pix[kThreads];                        // x, y, S
+    float4 vout4[kPackedOut ? kThreads : 1];     // v_out / D (C <= 4)
+    float vout[kPackedOut ? 1 : kMaxC][kPackedOut ? 1 : kThreads];  // v_out / D per channel (C > 4)
     int wsum[kThreads / 32];
 };
 
@@ -634,6 +635,7 @@ __device__ __forceinline__ void stage_pair_chunk(PairSmem<kMaxC> &sm, const int 
     for (int e = threadIdx.x; e < n; e += kThreads) {
         const int g = __ldg(&ids_sorted[range.x + chunk + e]);
         const float2 xy = __ldg(&xys[g]);
+        sm.gid[e] = g;
         sm.geo[e] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
         sm.cc[e] = 0.5f * __ldg(&conics[3 * g + 2]);
 #pragma unroll
@@ -654,20 +656,33 @@ __device__ __forceinline__ float2 pixel_terms(const float denom, const float (&u
     return make_float2(inv, -inv2 * vu);
 }
 
-// Step 1's per-pixel record: coordinates, 1 / D, S and v_out
+// Step 1's per-pixel record: coordinates, S and v_out / D (terms = (1 / D, S)). Step 3 forms dL/dsigma_k = -d_k (f_k . (v_out / D) + S)
+// and the colour gradient d_k (v_out / D): the reference's -d_k (s_k / D + S) and (d_k / D) v_out with the division applied to v_out.
 template <int kMaxC>
 __device__ __forceinline__ void store_pixel_grad(PairSmem<kMaxC> &sm, const int tid, const float px, const float py, const float2 terms,
                                                  const float (&v_out)[kMaxC]) {
-    sm.pix[tid] = make_float4(px, py, terms.x, terms.y);
+    sm.pix[tid] = make_float4(px, py, terms.y, 0.f);
     if constexpr (PairSmem<kMaxC>::kPackedOut) {
         float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < kMaxC; ++c) v4[c] = v_out[c];
+        for (int c = 0; c < kMaxC; ++c) v4[c] = v_out[c] * terms.x;
         sm.vout4[tid] = make_float4(v4[0], v4[1], v4[2], v4[3]);
     } else {
 #pragma unroll
-        for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c];
+        for (int c = 0; c < kMaxC; ++c) sm.vout[c][tid] = v_out[c] * terms.x;
     }
+}
+
+// Transpose of a 32 x 32 bit matrix held one row per lane (bit j of lane l's word = M[l][j]): lane j returns column j (bit l = M[l][j]).
+// Five exchanges of off-diagonal blocks between lanes l and l ^ s.
+__device__ __forceinline__ unsigned transpose_bits(unsigned x, const int lane) {
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const unsigned left = s == 16 ? 0x0000FFFFu : s == 8 ? 0x00FF00FFu : s == 4 ? 0x0F0F0F0Fu : s == 2 ? 0x33333333u : 0x55555555u;
+        const unsigned y = __shfl_xor_sync(0xffffffffu, x, s);
+        x = (lane & s) ? ((x & ~left) | ((y >> s) & left)) : ((x & left) | ((y << s) & ~left));
+    }
+    return x;
 }
 
 // Steps 2 and 3 of the pairs-grouped backward pass for one tile (every thread of the CTA calls it, after a CTA barrier that follows the
@@ -682,6 +697,10 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    // the gradient value this lane adds after each entry's reduce-scatter: v_conic (S_xx / 2, S_xy, S_yy / 2), v_xy, v_colors
+    float *const target = value_index < 3 ? v_conic + value_index : value_index < 5 ? v_xy + (value_index - 3) : v_colors + (value_index - 5);
+    const int target_stride = value_index < 3 ? 3 : value_index < 5 ? 2 : channels;
+    const float target_scale = (value_index == 0 || value_index == 2) ? 0.5f : 1.f;
     for (int chunk = 0; chunk < len; chunk += kPairStage) {
         const int n_entries = min(kPairStage, len - chunk);
         if (chunk > 0 || restage_first) {
@@ -689,25 +708,46 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             stage(chunk);
             __syncthreads();
         }
-        // 2. counting sort of this chunk's pairs by entry without atomics: per slot, the lanes of a warp holding the same entry are grouped
-        //    with __match_any_sync; each warp counts its pairs per entry in its own row of wcnt (a group's leader adds the group, so no
-        //    two lanes write one counter), which also gives each pair its place among the warp's pairs of that entry (< 32: 5 bits)
-        for (int e = lane; e < n_entries; e += 32) sm.g.wcnt[warp][e] = 0;
-        __syncwarp();
+        // 2. counting sort of this chunk's pairs by entry without atomics. Each warp counts its pairs per entry in its own row of wcnt and
+        //    gives each pair its place among the warp's pairs of that entry (< 32: 5 bits). A pixel holds an entry at most once, so for a
+        //    chunk of at most 32 entries the warp's (lane, entry) incidence is a 32 x 32 bit matrix: transposed, lane e holds the lanes that
+        //    hold entry e, whose count is the warp's count and among which a lane's rank is its place. Longer chunks group, per slot, the
+        //    lanes holding the same entry with __match_any_sync, and the group's leader adds the group to the counter.
+        const unsigned lanes_below = (1u << lane) - 1u;
         unsigned off_lo = 0u, off_hi = 0u;  // the pairs' places, 5 bits per slot
+        if (n_entries <= 32) {
+            unsigned held = 0u;
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            const int e = key[k] - chunk;
-            const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
-            const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
-            const unsigned below = peers & ((1u << lane) - 1u);
-            const int base = mine ? (int)sm.g.wcnt[warp][e] : 0;
+            for (int k = 0; k < kTopK; ++k) {
+                const int e = key[k] - chunk;
+                if (key[k] >= 0 && e >= 0 && e < n_entries) held |= 1u << e;
+            }
+            const unsigned holders = transpose_bits(held, lane);  // lanes holding entry `lane`
+            if (lane < n_entries) sm.g.wcnt[warp][lane] = (uint16_t)__popc(holders);
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const unsigned of_entry = __shfl_sync(0xffffffffu, holders, (key[k] - chunk) & 31);
+                const unsigned off = (unsigned)__popc(of_entry & lanes_below) & 31u;
+                if (k < 6) off_lo |= off << (5 * k);
+                else off_hi |= off << (5 * (k - 6));
+            }
+        } else {
+            for (int e = lane; e < n_entries; e += 32) sm.g.wcnt[warp][e] = 0;
             __syncwarp();
-            if (mine && below == 0u) sm.g.wcnt[warp][e] = (uint16_t)(base + __popc(peers));
-            __syncwarp();
-            const unsigned off = (unsigned)(base + __popc(below)) & 31u;
-            if (k < 6) off_lo |= off << (5 * k);
-            else off_hi |= off << (5 * (k - 6));
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const int e = key[k] - chunk;
+                const bool mine = key[k] >= 0 && e >= 0 && e < n_entries;
+                const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
+                const unsigned below = peers & lanes_below;
+                const int base = mine ? (int)sm.g.wcnt[warp][e] : 0;
+                __syncwarp();
+                if (mine && below == 0u) sm.g.wcnt[warp][e] = (uint16_t)(base + __popc(peers));
+                __syncwarp();
+                const unsigned off = (unsigned)(base + __popc(below)) & 31u;
+                if (k < 6) off_lo |= off << (5 * k);
+                else off_hi |= off << (5 * (k - 6));
+            }
         }
         __syncthreads();
         {
@@ -767,8 +807,8 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
                 const unsigned rec = sm.g.pairs[b + i];
                 const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
                 const float d = sm.alpha[slot][pix];
-                const float4 pr = sm.pix[pix];  // x, y, 1 / D, S
-                float vo[kMaxC];
+                const float4 pr = sm.pix[pix];  // x, y, S
+                float vo[kMaxC];                 // v_out / D
                 if constexpr (PairSmem<kMaxC>::kPackedOut) {
                     const float4 v4 = sm.vout4[pix];
                     const float va[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -778,39 +818,27 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
 #pragma unroll
                     for (int c = 0; c < kMaxC; ++c) vo[c] = c < channels ? sm.vout[c][pix] : 0.f;
                 }
-                float sk = 0.f;  // f_k . v_out in the reference's channel order
+                float sk = 0.f;  // f_k . v_out / D in the reference's channel order
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c) sk = fmaf(f[c], vo[c], sk);
-                const float vs = -d * fmaf(sk, pr.z, pr.w);  // dL/dsigma
-                const float wk = d * pr.z;                   // the colour weight d / D
+                const float vs = -d * (sk + pr.z);  // dL/dsigma
                 const float dx = q.x - pr.x, dy = q.y - pr.y;
                 const float tx = vs * dx, ty = vs * dy;
                 acc[0] = fmaf(tx, dx, acc[0]);
                 acc[1] = fmaf(tx, dy, acc[1]);
                 acc[2] = fmaf(ty, dy, acc[2]);
-                // v_xy per pair, v (a dx + b dy) and v (b dx + c dy) as the reference sums them: with the conic factored out of the
-                // sums, a Sx and b Sy can cancel to a few parts in 10^4 of themselves and lose the result's accuracy
-                acc[3] = fmaf(vs, fmaf(ca, dx, cb * dy), acc[3]);
-                acc[4] = fmaf(vs, fmaf(cb, dx, cc * dy), acc[4]);
+                // v_xy per pair, a v dx + b v dy and b v dx + c v dy, as the reference sums v (a dx + b dy): with the conic factored out of
+                // the sums, a Sx and b Sy can cancel to a few parts in 10^4 of themselves and lose the result's accuracy
+                acc[3] = fmaf(ca, tx, fmaf(cb, ty, acc[3]));
+                acc[4] = fmaf(cb, tx, fmaf(cc, ty, acc[4]));
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c)
-                    if (c < channels) acc[5 + c] = fmaf(wk, vo[c], acc[5 + c]);
+                    if (c < channels) acc[5 + c] = fmaf(d, vo[c], acc[5 + c]);
             }
             const float total = warp_sum_scatter<NV>(acc, lane);
             if (holds_total) {
-                const int g = __ldg(&ids_sorted[range.x + chunk + e]);
-                float value, *target;
-                if (value_index < 3) {
-                    value = value_index == 1 ? total : 0.5f * total;
-                    target = v_conic + 3 * (size_t)g + value_index;
-                } else if (value_index < 5) {
-                    value = total;
-                    target = v_xy + 2 * (size_t)g + (value_index - 3);
-                } else {
-                    value = total;
-                    target = v_colors + (size_t)g * channels + (value_index - 5);
-                }
-                if (value != 0.f) atomicAdd(target, value);
+                const float value = target_scale * total;
+                if (value != 0.f) atomicAdd(target + (size_t)target_stride * sm.gid[e], value);
             }
         }
     }
@@ -946,6 +974,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     if (one_chunk) {
         for (int e = tid; e < len; e += kThreads) {
             const int g = __ldg(&ids_sorted[range.x + e]);
+            sm.gid[e] = g;
 #pragma unroll
             for (int c = 0; c < kMaxC; ++c)
                 if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
