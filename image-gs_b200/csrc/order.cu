@@ -5,23 +5,18 @@
 //      rejected as the reference rejects them);
 //   2. keys_kernel: one 64-bit key per Gaussian, the coarse Morton code above the fine one (their order is the lexicographic order of
 //      the pair), with its index;
-//   3. a stable least-significant-digit radix sort of the keys, 8 bits a pass and only as many passes as the key is wide: per block of
-//      2048 keys a digit histogram (count_kernel), one scan of all (digit, block) counts (scan_kernel), and a stable scatter
-//      (scatter_kernel: within a block, keys are ranked in order with per-warp __match_any_sync groups and a scan over the warps).
+//   3. a stable least-significant-digit radix sort of the keys over the key's width only (radix_sort.cuh).
 // A pair of codes wider than 64 bits in all (coordinates spanning more than 2^16 coarse and fine levels together) is reported as
 // IGS_ERR_UNSUPPORTED for the caller's host sort.
 #include <climits>
 
 #include "igs_common.cuh"
+#include "radix_sort.cuh"
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kItems = 8;                       // keys per thread and pass
-constexpr int kTileKeys = kThreads * kItems;    // keys per block
-constexpr int kBins = 256;                      // 8-bit digits
-constexpr int kScanThreads = 1024;
+using radix::kThreads;
+using radix::kWarps;
 
 struct Range {
     long long min_x, min_y, max_x, max_y;
@@ -87,102 +82,9 @@ __global__ void __launch_bounds__(kThreads) keys_kernel(const int n, const long 
     idx[i] = i;
 }
 
-__global__ void __launch_bounds__(kThreads) count_kernel(const int n, const unsigned long long *__restrict__ keys, const int shift,
-                                                         int *__restrict__ counts) {
-    __shared__ int hist[kBins];
-    hist[threadIdx.x] = 0;  // kThreads == kBins
-    __syncthreads();
-    const int base = blockIdx.x * kTileKeys;
-    for (int e = base + threadIdx.x; e < min(n, base + kTileKeys); e += kThreads) atomicAdd(&hist[(keys[e] >> shift) & (kBins - 1)], 1);
-    __syncthreads();
-    counts[(size_t)threadIdx.x * gridDim.x + blockIdx.x] = hist[threadIdx.x];  // digit-major
-}
-
-// exclusive scan of counts[0, total) in place, one CTA in chunks of kScanThreads
-__global__ void __launch_bounds__(kScanThreads) scan_kernel(const int total, int *__restrict__ counts) {
-    __shared__ int warp_sums[kScanThreads / 32];
-    __shared__ int carry;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int base = 0; base < total; base += kScanThreads) {
-        const int i = base + threadIdx.x;
-        const int v = i < total ? counts[i] : 0;
-        int incl = v;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-        }
-        if (lane == 31) warp_sums[warp] = incl;
-        __syncthreads();
-        if (warp == 0) {
-            int w = warp_sums[lane];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, w, o);
-                if (lane >= o) w += t;
-            }
-            warp_sums[lane] = w;
-        }
-        __syncthreads();
-        const int before = carry + (warp > 0 ? warp_sums[warp - 1] : 0);
-        if (i < total) counts[i] = before + incl - v;
-        __syncthreads();
-        if (threadIdx.x == 0) carry += warp_sums[kScanThreads / 32 - 1];
-        __syncthreads();
-    }
-}
-
-__global__ void __launch_bounds__(kThreads) scatter_kernel(const int n, const unsigned long long *__restrict__ keys_in,
-                                                           const int *__restrict__ idx_in, const int shift, const int *__restrict__ offsets,
-                                                           unsigned long long *__restrict__ keys_out, int *__restrict__ idx_out) {
-    __shared__ int running[kBins];          // the next place of each digit for this block
-    __shared__ int wcount[kWarps][kBins];   // per warp and digit: the count, then the warp's first place
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    running[threadIdx.x] = offsets[(size_t)threadIdx.x * gridDim.x + blockIdx.x];
-    const int base = blockIdx.x * kTileKeys;
-    for (int s = 0; s < kItems; ++s) {
-        const int e = base + s * kThreads + threadIdx.x;
-        const bool valid = e < n;
-        const unsigned long long key = valid ? keys_in[e] : 0ull;
-        const int d = valid ? (int)((key >> shift) & (kBins - 1)) : kBins;  // kBins: no key
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) wcount[w][threadIdx.x] = 0;
-        __syncthreads();
-        const unsigned peers = __match_any_sync(0xffffffffu, d);
-        const int rank = __popc(peers & ((1u << lane) - 1u));
-        if (valid && rank == 0) wcount[warp][d] = __popc(peers);
-        __syncthreads();
-        {
-            int acc = running[threadIdx.x];
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const int c = wcount[w][threadIdx.x];
-                wcount[w][threadIdx.x] = acc;
-                acc += c;
-            }
-            running[threadIdx.x] = acc;
-        }
-        __syncthreads();
-        if (valid) {
-            const int place = wcount[warp][d] + rank;
-            keys_out[place] = key;
-            idx_out[place] = idx_in[e];
-        }
-        __syncthreads();
-    }
-}
-
 __global__ void __launch_bounds__(kThreads) widen_kernel(const int n, const int *__restrict__ idx, long long *__restrict__ order) {
     const int i = blockIdx.x * kThreads + threadIdx.x;
     if (i < n) order[i] = idx[i];
-}
-
-int bit_length(unsigned long long v) {
-    int b = 0;
-    while (v) ++b, v >>= 1;
-    return b;
 }
 
 struct Layout {
@@ -191,7 +93,6 @@ struct Layout {
 
 Layout layout(int n) {
     const size_t num = n > 0 ? (size_t)n : 1;
-    const size_t blocks = (num + kTileKeys - 1) / kTileKeys;
     auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
     Layout l;
     size_t off = 0;
@@ -200,7 +101,7 @@ Layout layout(int n) {
     l.keys1 = off, off += up(sizeof(unsigned long long) * num);
     l.idx0 = off, off += up(sizeof(int) * num);
     l.idx1 = off, off += up(sizeof(int) * num);
-    l.counts = off, off += up(sizeof(int) * kBins * blocks);
+    l.counts = off, off += up(radix::counts_bytes((int)num));
     l.total = off;
     return l;
 }
@@ -242,21 +143,14 @@ int igs_bitstream_order(int num_points, const int64_t *positions, int refine_bit
     IGS_REQUIRE(coarse_span < (1ull << 32), "%s: the positions must have at most 2^32 quantization levels per coordinate", who);
     const unsigned long long fine_span = (unsigned long long)std::max(r.max_x - r.min_x, r.max_y - r.min_y);
     if (refine_bits > 0 && fine_span >= (1ull << 32)) return igs::set_error(IGS_ERR_UNSUPPORTED, "%s: fine positions over 2^32 levels", who);
-    const int fine_bits = 2 * bit_length(fine_span);
-    const int key_bits = refine_bits == 0 ? fine_bits : 2 * bit_length(coarse_span) + fine_bits;
+    const int fine_bits = 2 * radix::bit_length(fine_span);
+    const int key_bits = refine_bits == 0 ? fine_bits : 2 * radix::bit_length(coarse_span) + fine_bits;
     if (key_bits > 64) return igs::set_error(IGS_ERR_UNSUPPORTED, "%s: a %d-bit sort key (sort on the host)", who, key_bits);
 
     // 2. keys and indices
     keys_kernel<<<elem_blocks, kThreads, 0, s>>>(num_points, pos, refine_bits, cx0, cy0, r.min_x, r.min_y, fine_bits, keys[0], idx[0]);
     // 3. stable radix passes over the key's width
-    const int tile_blocks = igs::ceil_div(num_points, kTileKeys);
-    int cur = 0;
-    for (int shift = 0; shift < key_bits; shift += 8) {
-        count_kernel<<<tile_blocks, kThreads, 0, s>>>(num_points, keys[cur], shift, counts);
-        scan_kernel<<<1, kScanThreads, 0, s>>>(kBins * tile_blocks, counts);
-        scatter_kernel<<<tile_blocks, kThreads, 0, s>>>(num_points, keys[cur], idx[cur], shift, counts, keys[1 - cur], idx[1 - cur]);
-        cur = 1 - cur;
-    }
+    const int cur = radix::sort_pairs(num_points, key_bits, keys, idx, counts, s);
     widen_kernel<<<elem_blocks, kThreads, 0, s>>>(num_points, idx[cur], reinterpret_cast<long long *>(order));
     return igs::check_launch(who);
 }

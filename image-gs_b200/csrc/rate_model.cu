@@ -10,7 +10,10 @@
 // Float operations follow the reference's float32 order one rounding at a time (__fmul_rn / __fadd_rn / __fdiv_rn: no contraction); the
 // two means are of integers (rounded residuals, rotation indices) and are summed exactly in 64-bit integers, then divided as the
 // reference's float32 mean does. IEEE build (no fast-math).
+#include <climits>
+
 #include "igs_common.cuh"
+#include "radix_sort.cuh"
 
 namespace {
 
@@ -178,53 +181,49 @@ __global__ void __launch_bounds__(kThreads) rot_kernel(const int n, const unsign
     if (i < n) inv_rot[i] = acc->class_inv[class_of[i]];
 }
 
-// each valid (Gaussian, neighbour) at a free place of its neighbour's list (arbitrary order; sort_sources_kernel orders each list)
-__global__ void __launch_bounds__(kThreads) place_sources_kernel(const int n, const long long *__restrict__ neighbors,
-                                                                 const int *__restrict__ offsets, int *__restrict__ cursor,
-                                                                 int *__restrict__ sources) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-#pragma unroll
-    for (int k = 0; k < kNeighbors; ++k) {
-        const long long j = neighbors[(size_t)i * kNeighbors + k];
-        if (j < 0 || j >= n) continue;
-        sources[offsets[j] + atomicAdd(&cursor[j], 1)] = i;
-    }
+// The in-neighbour lists (compress/rate.py:116-128, predicting_sources: the rows of the neighbour matrix stably sorted by target): every
+// (Gaussian i, neighbour slot k) entry in row-major order keyed by its neighbour j (invalid ones by num_points, after all valid ones), for
+// a stable radix sort by key, which leaves each list in increasing i without a per-list sort (whose cost grows with the square of a
+// list's length, and one Gaussian can be a neighbour of thousands)
+__global__ void __launch_bounds__(kThreads) source_keys_kernel(const int n, const long long *__restrict__ neighbors,
+                                                               unsigned long long *__restrict__ keys, int *__restrict__ values) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n * kNeighbors) return;
+    const long long j = neighbors[t];
+    keys[t] = (j < 0 || j >= n) ? (unsigned long long)n : (unsigned long long)j;
+    values[t] = t / kNeighbors;
 }
 
-// one thread per Gaussian: its list of predicting Gaussians in increasing order (the reference's stable sort of row-major entries) and
-// their weights of it, 1 / their neighbour counts
-__global__ void __launch_bounds__(kThreads) sort_sources_kernel(const int n, const int *__restrict__ offsets, const unsigned char *__restrict__ counts,
-                                                                int *__restrict__ sources, float *__restrict__ source_weights) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n) return;
-    const int b = offsets[j], e = offsets[j + 1];
-    for (int x = b + 1; x < e; ++x) {  // insertion sort: the lists are short (a Gaussian predicts few others)
-        const int v = sources[x];
-        int y = x - 1;
-        while (y >= b && sources[y] > v) {
-            sources[y + 1] = sources[y];
-            --y;
-        }
-        sources[y + 1] = v;
-    }
-    for (int x = b; x < e; ++x) source_weights[x] = __fdiv_rn(1.f, (float)counts[sources[x]]);
+// the sorted entries' Gaussians and their weights, 1 / their neighbour counts: the first offsets[n] entries are the valid ones
+__global__ void __launch_bounds__(kThreads) sources_kernel(const int n, const int *__restrict__ offsets, const int *__restrict__ sorted,
+                                                           const unsigned char *__restrict__ counts, int *__restrict__ sources,
+                                                           float *__restrict__ source_weights) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= offsets[n]) return;
+    const int i = sorted[t];
+    sources[t] = i;
+    source_weights[t] = __fdiv_rn(1.f, (float)counts[i]);
 }
 
 size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 struct Layout {
-    size_t acc, in_degree, cursor, counts, classes, cum, total;
+    size_t acc, in_degree, counts, classes, keys0, keys1, vals0, vals1, radix_counts, cum, total;
 };
 
 Layout layout(int n) {
+    const size_t entries = (size_t)n * kNeighbors;
     Layout l;
     size_t off = 0;
     l.acc = off, off += round256(sizeof(Accumulators));
     l.in_degree = off, off += round256(sizeof(int) * (size_t)n);
-    l.cursor = off, off += round256(sizeof(int) * (size_t)n);
     l.counts = off, off += round256((size_t)n);
     l.classes = off, off += round256((size_t)n);
+    l.keys0 = off, off += round256(sizeof(unsigned long long) * entries);
+    l.keys1 = off, off += round256(sizeof(unsigned long long) * entries);
+    l.vals0 = off, off += round256(sizeof(int) * entries);
+    l.vals1 = off, off += round256(sizeof(int) * entries);
+    l.radix_counts = off, off += round256(radix::counts_bytes((int)entries));
     l.cum = off, off += round256(igs_cumsum_workspace(n));
     l.total = off;
     return l;
@@ -242,7 +241,8 @@ int igs_rate_model(int num_points, int channels, const int64_t *neighbors, const
                    float *inv_rot, int32_t *offsets, int32_t *sources, float *source_weights, void *workspace, size_t workspace_bytes,
                    void *stream) {
     const char *who = "igs_rate_model";
-    IGS_REQUIRE(num_points >= 0, "%s: negative size", who);
+    IGS_REQUIRE(num_points >= 0 && num_points <= INT_MAX / kNeighbors, "%s: %d Gaussians (at most %d)", who, num_points,
+                INT_MAX / kNeighbors);
     IGS_REQUIRE(channels >= 1 && channels <= kMaxChannels, "%s: 1 to %d channels (got %d)", who, kMaxChannels, channels);
     IGS_REQUIRE(color_refs && pred_refs, "%s: null channel references", who);
     Refs refs;
@@ -266,11 +266,12 @@ int igs_rate_model(int num_points, int channels, const int64_t *neighbors, const
     char *ws = static_cast<char *>(workspace);
     Accumulators *acc = reinterpret_cast<Accumulators *>(ws + l.acc);
     int *in_degree = reinterpret_cast<int *>(ws + l.in_degree);
-    int *cursor = reinterpret_cast<int *>(ws + l.cursor);
     unsigned char *counts = reinterpret_cast<unsigned char *>(ws + l.counts);
     unsigned char *classes = reinterpret_cast<unsigned char *>(ws + l.classes);
-    // accumulators, in-degrees and cursors start at zero (one memset: they are the first bytes of the workspace)
-    if (cudaMemsetAsync(ws, 0, l.counts, s) != cudaSuccess) return igs::check_launch(who);
+    unsigned long long *keys[2] = {reinterpret_cast<unsigned long long *>(ws + l.keys0), reinterpret_cast<unsigned long long *>(ws + l.keys1)};
+    int *vals[2] = {reinterpret_cast<int *>(ws + l.vals0), reinterpret_cast<int *>(ws + l.vals1)};
+    // accumulators and in-degrees start at zero (one memset: they are the first bytes of the workspace)
+    if (cudaMemsetAsync(ws, 0, l.counts, s) != cudaSuccess) return igs::check_launch(who);  // acc and in_degree
     if (cudaMemsetAsync(offsets, 0, sizeof(int32_t), s) != cudaSuccess) return igs::check_launch(who);
     const int blocks = igs::ceil_div(num_points > 0 ? num_points : 1, kThreads);
     if (num_points > 0) {
@@ -283,9 +284,12 @@ int igs_rate_model(int num_points, int channels, const int64_t *neighbors, const
     scalars_kernel<<<1, 32, 0, s>>>(num_points, channels, steps, channel_weights, inv_steps, inv_feat, feat_coeffs, acc);
     if (num_points > 0) {
         rot_kernel<<<blocks, kThreads, 0, s>>>(num_points, classes, acc, inv_rot);
-        place_sources_kernel<<<blocks, kThreads, 0, s>>>(num_points, reinterpret_cast<const long long *>(neighbors), offsets, cursor,
-                                                         sources);
-        sort_sources_kernel<<<blocks, kThreads, 0, s>>>(num_points, offsets, counts, sources, source_weights);
+        const int entries = num_points * kNeighbors;
+        const int entry_blocks = igs::ceil_div(entries, kThreads);
+        source_keys_kernel<<<entry_blocks, kThreads, 0, s>>>(num_points, reinterpret_cast<const long long *>(neighbors), keys[0], vals[0]);
+        const int cur = radix::sort_pairs(entries, radix::bit_length((unsigned long long)num_points),
+                                          keys, vals, reinterpret_cast<int *>(ws + l.radix_counts), s);
+        sources_kernel<<<entry_blocks, kThreads, 0, s>>>(num_points, offsets, vals[cur], counts, sources, source_weights);
     }
     return igs::check_launch(who);
 }

@@ -91,22 +91,63 @@ def rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, chan
                      pred_channels)
 
 
+MAX_CHANNELS = 12  # IGS_MAX_CHANNELS of include/igs_b200.h: feature channels igs_rate_model handles
+
+
+def runs_on_gpu(feat, device, dtype=torch.float32) -> bool:
+    """Whether rate_model's arguments are ones the GPU version handles: float32, a CUDA device and at most MAX_CHANNELS feature channels.
+    Anything else (a texture stack of more channels, the CPU) is the reference's own code's."""
+    if dtype != torch.float32 or not torch.cuda.is_available():
+        return False
+    dev = torch.device(device) if device is not None else getattr(feat, "device", torch.device("cpu"))
+    channels = feat.shape[-1] if hasattr(feat, "shape") and len(feat.shape) == 2 else MAX_CHANNELS + 1
+    return dev.type == "cuda" and channels <= MAX_CHANNELS
+
+
+def routed_rate_model(original):
+    """compress.rate.rate_model with the reference's signature, on the GPU where runs_on_gpu holds and by `original` otherwise"""
+
+    def rate_model_routed(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, channel_weights, dtype, device, refine_bits=0):
+        if runs_on_gpu(feat, device, dtype):
+            return rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, channel_weights, dtype, device, refine_bits)
+        return original(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, channel_weights, dtype, device, refine_bits)
+
+    rate_model_routed.original = original
+    return rate_model_routed
+
+
+def routed_bitstream_neighbors(original):
+    """compress.rate.bitstream_neighbors with the reference's signature, on the GPU when there is one and by `original` otherwise"""
+
+    def bitstream_neighbors_routed(q_xy, refine_bits=0):
+        if torch.cuda.is_available():
+            return bitstream_neighbors(q_xy, refine_bits)
+        return original(q_xy, refine_bits)
+
+    bitstream_neighbors_routed.original = original
+    return bitstream_neighbors_routed
+
+
 def install(*module_names):
-    """Route the reference's calls of compress.rate.rate_model and bitstream_neighbors to these GPU versions (same signatures): the names
+    """Route the reference's calls of compress.rate.rate_model and bitstream_neighbors to the GPU versions (same signatures): the names
     are replaced in each named module that is imported or importable (default: compress.rate and model, which binds rate_model when it is
-    imported, model.py:43). Returns {(module, name): original} for restore()."""
+    imported, model.py:43). Calls the GPU versions do not handle (more than MAX_CHANNELS feature channels, a CPU device or no GPU, a
+    dtype other than float32) go to the replaced functions, so training that ran with the reference runs the same. Returns
+    {(module, name): original} for restore()."""
     import importlib
 
+    routes = {"rate_model": routed_rate_model, "bitstream_neighbors": routed_bitstream_neighbors}
     replaced = {}
     for name in module_names or ("compress.rate", "model"):
         try:
             module = importlib.import_module(name)
         except ImportError:
             continue
-        for attr, new in (("rate_model", rate_model), ("bitstream_neighbors", bitstream_neighbors)):
+        for attr, route in routes.items():
             if hasattr(module, attr):
-                replaced[(name, attr)] = getattr(module, attr)
-                setattr(module, attr, new)
+                original = getattr(module, attr)
+                replaced[(name, attr)] = original
+                setattr(module, attr, route(getattr(original, "original", original)))
     return replaced
 
 

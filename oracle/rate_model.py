@@ -16,6 +16,20 @@ BOUNDARIES = np.array([0.25, 0.5, 1.0, 2.0], dtype=np.float32)  # aspect-ratio c
 LN2 = np.float32(math.log(2.0))
 
 
+def predicting_sources(nbrs):
+    """predicting_sources (compress/rate.py:116-128): for neighbours [P, K] (-1 for none), the Gaussians predicting from each one, as CSR
+    lists in increasing order (the rows of the valid entries stably sorted by target), and their weights 1 / their neighbour counts."""
+    num = len(nbrs)
+    valid = nbrs >= 0
+    count = valid.sum(axis=1)
+    rows = np.repeat(np.arange(num), nbrs.shape[1]).reshape(num, nbrs.shape[1])[valid]
+    targets = nbrs[valid]
+    sources = rows[np.argsort(targets, kind="stable")]
+    offsets = np.zeros(num + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum(np.bincount(targets, minlength=num))
+    return offsets, sources, (np.float32(1.0) / count[sources].astype(np.float32)).astype(np.float32)
+
+
 def rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, channel_weights, refine_bits=0):
     """A dict of the RateModel fields (neighbors, weights, slope, inv_steps, inv_feat, feat_coeffs, inv_rot, offsets, sources,
     source_weights, pred_channels) from numpy inputs: q_xy [P, 2] int64, feat [P, C], log2_scale [P, 2], q_rot [P] (float32)."""
@@ -29,13 +43,7 @@ def rate_model(q_xy, feat, log2_scale, q_rot, color_refs, pred_refs, steps, chan
     weights = (valid.astype(f32) / np.maximum(count.astype(f32), f32(1.0))[:, None]).astype(f32)
     clamped = np.where(valid, nbrs, 0)
 
-    # the Gaussians predicting from each one: rows in increasing order per target
-    rows = np.repeat(np.arange(num), nb.NUM_NEIGHBORS).reshape(num, nb.NUM_NEIGHBORS)[valid]
-    targets = nbrs[valid]
-    sources = rows[np.argsort(targets, kind="stable")]
-    offsets = np.zeros(num + 1, dtype=np.int64)
-    offsets[1:] = np.cumsum(np.bincount(targets, minlength=num))
-    source_weights = (f32(1.0) / count[sources].astype(f32)).astype(f32)
+    offsets, sources, source_weights = predicting_sources(nbrs)
 
     # colour-reference subtraction and prediction references
     own = np.arange(channels)

@@ -74,17 +74,36 @@ def test_roofline_bytes_of_the_raster_kernels():
 
 
 def test_rate_model_install_replaces_and_restores(monkeypatch):
-    """igs_b200.rate_model.install routes a module's rate_model / bitstream_neighbors to the GPU versions and restore undoes it."""
+    """igs_b200.rate_model.install routes a module's rate_model / bitstream_neighbors to the GPU versions, what they do not handle to the
+    module's own functions, and restore undoes it."""
     import sys
     import types
+
+    import numpy as np
+    import torch
 
     from igs_b200 import neighbors, rate_model
 
     fake = types.ModuleType("fake_compress_rate")
     fake.rate_model, fake.bitstream_neighbors, fake.other = "ref_rate_model", "ref_neighbors", "untouched"
     monkeypatch.setitem(sys.modules, "fake_compress_rate", fake)
+    calls = []
+    fake.rate_model = lambda *a: calls.append(("rate_model", a)) or "reference"
+    fake.bitstream_neighbors = lambda *a: calls.append(("bitstream_neighbors", a)) or "reference"
+    originals = (fake.rate_model, fake.bitstream_neighbors)
     replaced = rate_model.install("fake_compress_rate", "no_such_module_here")
-    assert fake.rate_model is rate_model.rate_model and fake.bitstream_neighbors is neighbors.bitstream_neighbors
+    assert fake.rate_model.original is originals[0] and fake.bitstream_neighbors.original is originals[1]
     assert fake.other == "untouched" and len(replaced) == 2
+    # what the GPU versions do not handle goes to the reference's functions: here no GPU, a CPU device, 13 channels
+    feat13 = torch.zeros(4, 13)
+    args = (np.zeros((4, 2), np.int64), feat13, torch.zeros(4, 2), torch.zeros(4), [-1] * 13, [-1] * 13, torch.ones(13), torch.ones(13),
+            torch.float32, torch.device("cpu"))
+    assert fake.rate_model(*args) == "reference" and calls[-1][0] == "rate_model" and calls[-1][1][-1] == 0
+    assert fake.bitstream_neighbors(np.zeros((4, 2), np.int64)) == "reference"
+    assert not rate_model.runs_on_gpu(feat13, "cuda:0") and not rate_model.runs_on_gpu(torch.zeros(4, 3), "cpu")
+    # installing twice wraps the reference's functions, not the routes
+    again = rate_model.install("fake_compress_rate")
+    assert fake.rate_model.original is originals[0]
+    rate_model.restore(again)
     rate_model.restore(replaced)
-    assert fake.rate_model == "ref_rate_model" and fake.bitstream_neighbors == "ref_neighbors"
+    assert (fake.rate_model, fake.bitstream_neighbors) == originals
