@@ -175,9 +175,12 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
 #pragma unroll
         for (int q = 0; q < PPT; ++q) start[q] = 0;
         if (base == 0) {
-            // fast fill, per pixel: all of the first ten entries valid -> slots 0..9 in order, the half minima from registers; any other
-            // pixel starts from empty slots
-            float sig[PPT][kTopK];
+            // fast fill, per pixel: all of the first ten entries valid -> slots 0..9 in order, with the half minima kept as the slots are
+            // written; a pixel with an invalid entry among them (or a shorter list, or outside the image) clears them and starts from
+            // empty slots below
+            bool fast[PPT];
+#pragma unroll
+            for (int q = 0; q < PPT; ++q) fast[q] = count >= kTopK && inside[q];
             if (count >= kTopK) {
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) {
@@ -186,36 +189,22 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                     float sk[PPT];
                     column_sigma<PPT>(g4, cc, px, py, sk);
 #pragma unroll
-                    for (int q = 0; q < PPT; ++q) sig[q][k] = sk[q];
+                    for (int q = 0; q < PPT; ++q) {
+                        fast[q] = fast[q] && sigma_valid(sk[q]);
+                        const float a = __expf(-sk[q]);
+                        s_val[k * kThreads + pc[q].tid] = a;
+                        s_pos[k * kThreads + pc[q].tid] = k;
+                        const int h = k / kHalf;
+                        if (k % kHalf == 0 || a < gv[q][h]) gv[q][h] = a, gs[q][h] = k;
+                    }
                 }
             }
 #pragma unroll
             for (int q = 0; q < PPT; ++q) {
-                bool fast = count >= kTopK && inside[q];
-                if (fast) {
-#pragma unroll
-                    for (int k = 0; k < kTopK; ++k) fast = fast && sigma_valid(sig[q][k]);
-                }
-                if (!fast) {
+                if (!fast[q]) {
                     clear_slots(q);
                     if (!inside[q] && count >= kTopK) start[q] = kTopK;  // never inserts: keeps the pixels' starts equal below
                     continue;
-                }
-                float a[kTopK];
-#pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    a[k] = __expf(-sig[q][k]);
-                    s_val[k * kThreads + pc[q].tid] = a[k];
-                    s_pos[k * kThreads + pc[q].tid] = k;
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float m = a[h * kHalf];
-                    int ms = h * kHalf;
-#pragma unroll
-                    for (int k = 1; k < kHalf; ++k)
-                        if (a[h * kHalf + k] < m) m = a[h * kHalf + k], ms = h * kHalf + k;
-                    gv[q][h] = m, gs[q][h] = ms;
                 }
                 min_val[q] = fminf(gv[q][0], gv[q][1]);
                 filled[q] = kTopK;
@@ -697,10 +686,6 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int value_index = halving_index<NV>(lane);
     const bool holds_total = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
-    // the gradient value this lane adds after each entry's reduce-scatter: v_conic (S_xx / 2, S_xy, S_yy / 2), v_xy, v_colors
-    float *const target = value_index < 3 ? v_conic + value_index : value_index < 5 ? v_xy + (value_index - 3) : v_colors + (value_index - 5);
-    const int target_stride = value_index < 3 ? 3 : value_index < 5 ? 2 : channels;
-    const float target_scale = (value_index == 0 || value_index == 2) ? 0.5f : 1.f;
     for (int chunk = 0; chunk < len; chunk += kPairStage) {
         const int n_entries = min(kPairStage, len - chunk);
         if (chunk > 0 || restage_first) {
@@ -837,8 +822,13 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
             }
             const float total = warp_sum_scatter<NV>(acc, lane);
             if (holds_total) {
-                const float value = target_scale * total;
-                if (value != 0.f) atomicAdd(target + (size_t)target_stride * sm.gid[e], value);
+                // the gradient value this lane adds: v_conic (S_xx / 2, S_xy, S_yy / 2), v_xy, v_colors
+                const int g = sm.gid[e];
+                float *const target = value_index < 3 ? v_conic + 3 * (size_t)g + value_index
+                                    : value_index < 5 ? v_xy + 2 * (size_t)g + (value_index - 3)
+                                                      : v_colors + (size_t)g * channels + (value_index - 5);
+                const float value = (value_index == 0 || value_index == 2) ? 0.5f * total : total;
+                if (value != 0.f) atomicAdd(target, value);
             }
         }
     }
