@@ -68,30 +68,64 @@ __device__ __forceinline__ PixelCoord tile_pixel(int tile, int tiles_x, int row_
 // The reference skips an entry whose sigma is negative, NaN or infinite (forward.cu:301)
 __device__ __forceinline__ bool sigma_valid(const float sigma) { return !(sigma < 0.f || isnan(sigma) || isinf(sigma)); }
 
-// sigma of PPT pixels of one column (px) from a Gaussian's centre and halved conic (ha = a / 2, b, hc = c / 2): the same roundings as
-// igs::gaussian_sigma, since halving is exact (0.5 fma(a dx, dx, (c dy) dy) = fma(ha dx, dx, (hc dy) dy)); dx, ha dx and b dx are shared
-template <int PPT>
-__device__ __forceinline__ void column_sigma(const float4 g4, const float hc, const float px, const float (&py)[PPT], float (&sigma)[PPT]) {
-    const float dx = __fsub_rn(g4.x, px);
-    const float adx = __fmul_rn(g4.z, dx), bdx = __fmul_rn(g4.w, dx);
-#pragma unroll
-    for (int q = 0; q < PPT; ++q) {
-        const float dy = __fsub_rn(g4.y, py[q]);
-        sigma[q] = __fmaf_rn(bdx, dy, __fmaf_rn(adx, dx, __fmul_rn(__fmul_rn(hc, dy), dy)));
-    }
-}
-
-// sigma of one pixel from a Gaussian's centre and halved conic (g4 = x, y, a / 2, b; hc = c / 2), as column_sigma
+// sigma of one pixel from a Gaussian's centre and halved conic (g4 = x, y, a / 2, b; hc = c / 2): the same roundings as
+// igs::gaussian_sigma, since halving is exact (0.5 fma(a dx, dx, (c dy) dy) = fma(ha dx, dx, (hc dy) dy))
 __device__ __forceinline__ float halved_sigma(const float4 g4, const float hc, const float px, const float py) {
     const float dx = __fsub_rn(g4.x, px), dy = __fsub_rn(g4.y, py);
     return __fmaf_rn(__fmul_rn(g4.w, dx), dy, __fmaf_rn(__fmul_rn(g4.z, dx), dx, __fmul_rn(__fmul_rn(hc, dy), dy)));
 }
 
+// The selection stages a chunk of the tile's list in pairs of entries, so that one packed (f32x2) instruction serves two entries: pair i
+// (entries 2i, 2i + 1) is geo[2i] = (x0, x1, y0, y1) and geo[2i + 1] = (a0 / 2, a1 / 2, b0, b1); cc[e] = c / 2 of entry e. The packed
+// instructions round each component like their scalar forms, so the sigma values are those of halved_sigma bit for bit.
+__device__ __forceinline__ void stage_paired(float4 *geo, float *cc, const int e, const float2 xy, const float a, const float b,
+                                             const float c) {
+    float *g = reinterpret_cast<float *>(geo) + 8 * (e >> 1) + (e & 1);
+    g[0] = xy.x;
+    g[2] = xy.y;
+    g[4] = 0.5f * a;
+    g[6] = b;
+    cc[e] = 0.5f * c;
+}
+
+// one entry of the paired layout: (x, y, a / 2, b)
+__device__ __forceinline__ float4 paired_geo(const float4 *geo, const int e) {
+    const float *g = reinterpret_cast<const float *>(geo) + 8 * (e >> 1) + (e & 1);
+    return make_float4(g[0], g[2], g[4], g[6]);
+}
+
+// sigma of two consecutive entries (a pair of the paired layout: p = (x0, x1, y0, y1), h = (a0 / 2, a1 / 2, b0, b1), hc = (c0 / 2,
+// c1 / 2)) at PPT pixels of one column; npx = (-px, -px) and npy[q] = (-py, -py) (x - p is x + (-p) exactly)
+template <int PPT>
+__device__ __forceinline__ void pair_sigma(const float4 p, const float4 h, const float2 hc, const float2 npx, const float2 (&npy)[PPT],
+                                           float2 (&sigma)[PPT]) {
+    const float2 dx = __fadd2_rn(make_float2(p.x, p.y), npx);
+    const float2 adx = __fmul2_rn(make_float2(h.x, h.y), dx), bdx = __fmul2_rn(make_float2(h.z, h.w), dx);
+#pragma unroll
+    for (int q = 0; q < PPT; ++q) {
+        const float2 dy = __fadd2_rn(make_float2(p.z, p.w), npy[q]);
+        sigma[q] = __ffma2_rn(bdx, dy, __ffma2_rn(adx, dx, __fmul2_rn(__fmul2_rn(hc, dy), dy)));
+    }
+}
+
+// u += d f over the channels, in pairs of channels with packed instructions (each component rounded as fmaf)
+template <int kMaxC>
+__device__ __forceinline__ void add_weighted(const float d, const float (&f)[kMaxC], float (&u)[kMaxC]) {
+#pragma unroll
+    for (int c = 0; c + 1 < kMaxC; c += 2) {
+        const float2 r = __ffma2_rn(make_float2(d, d), make_float2(f[c], f[c + 1]), make_float2(u[c], u[c + 1]));
+        u[c] = r.x, u[c + 1] = r.y;
+    }
+    if (kMaxC & 1) u[kMaxC - 1] = fmaf(d, f[kMaxC - 1], u[kMaxC - 1]);
+}
+
 // The top-K selection of PPT pixels per thread over their tile's list (range into ids_sorted), in list order, with the slot rule of the
 // reference: free slots take valid entries in order, then an entry whose alpha exceeds the minimum replaces the first slot holding it.
 // The first ten entries fill the slots with fixed indices when all of them are valid for a pixel (what the rule does while slots are
-// free); only a pixel that cannot take that path starts from empty slots. The list is staged through s_geo / s_cc in chunks of kChunk
-// entries by the CTA's kThreads / PPT threads, with CTA barriers: every thread must call it. The slots live in shared memory, alpha in
+// free); only a pixel that cannot take that path starts from empty slots. The list is staged through s_geo / s_cc (paired layout, see
+// stage_paired) in chunks of kChunk entries by the CTA's kThreads / PPT threads, with CTA barriers: every thread must call it; a chunk of
+// odd length gets a NaN entry after its last, which no pixel takes. The entries are evaluated two at a time with packed instructions,
+// then tested in list order. The slots live in shared memory, alpha in
 // s_val and the list position in s_pos (both [k * kThreads + lid], position -1 for empty), so an insertion is two dynamic stores instead
 // of a select over ten registers; each pixel keeps the minimum of each half of its slots (0-4, 5-9) and the first slot holding it in
 // registers, so that an insertion rescans only the half it wrote (the first slot of the strict minimum over all ten is the second
@@ -104,10 +138,13 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
                                             float4 *s_geo, float *s_cc, int *s_pos, float *s_val, float (&val)[PPT][kTopK]) {
     constexpr int kStagers = kThreads / PPT;
     constexpr int kHalf = kTopK / 2;
+    static_assert(kTopK % 2 == 0 && kChunk % 2 == 0, "entries are evaluated in pairs");
     const int tid = threadIdx.x;
     const int len = range.y - range.x;
     const float px = (float)pc[0].j;  // the pixels share a column
-    float py[PPT], min_val[PPT];
+    const float2 npx = make_float2(-px, -px);
+    float2 npy[PPT];
+    float min_val[PPT];
     int filled[PPT];
     float gv[PPT][2];  // per half of the slots (0-4, 5-9): its minimum and the first slot holding it
     int gs[PPT][2];
@@ -120,7 +157,7 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
     };
 #pragma unroll
     for (int q = 0; q < PPT; ++q) {
-        py[q] = (float)pc[q].i;
+        npy[q] = make_float2(-(float)pc[q].i, -(float)pc[q].i);
         filled[q] = inside[q] ? 0 : kTopK;  // a pixel outside the image counts as full with an unbeatable minimum
         min_val[q] = inside[q] ? -1.f : INFINITY;
         if (len <= 0) clear_slots(q);  // no chunk below: the slots stay empty
@@ -166,12 +203,11 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         __syncthreads();
         for (int i = tid; i < count; i += kStagers) {
             const int g = __ldg(&ids_sorted[range.x + base + i]);
-            const float2 xy = __ldg(&xys[g]);
-            s_geo[i] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-            s_cc[i] = 0.5f * __ldg(&conics[3 * g + 2]);
+            stage_paired(s_geo, s_cc, i, __ldg(&xys[g]), __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2]));
         }
+        if ((count & 1) && tid == 0) stage_paired(s_geo, s_cc, count, make_float2(NAN, NAN), NAN, NAN, NAN);  // odd length: a NaN entry
         __syncthreads();
-        int start[PPT];  // first entry of the chunk each pixel still has to consider
+        int start[PPT];  // first entry of the chunk each pixel still has to consider (0 or kTopK: even)
 #pragma unroll
         for (int q = 0; q < PPT; ++q) start[q] = 0;
         if (base == 0) {
@@ -183,19 +219,22 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
             for (int q = 0; q < PPT; ++q) fast[q] = count >= kTopK && inside[q];
             if (count >= kTopK) {
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    const float4 g4 = s_geo[k];
-                    const float cc = s_cc[k];
-                    float sk[PPT];
-                    column_sigma<PPT>(g4, cc, px, py, sk);
+                for (int k = 0; k < kTopK; k += 2) {
+                    float2 s2[PPT];
+                    pair_sigma<PPT>(s_geo[k], s_geo[k + 1], *reinterpret_cast<const float2 *>(&s_cc[k]), npx, npy, s2);
 #pragma unroll
                     for (int q = 0; q < PPT; ++q) {
-                        fast[q] = fast[q] && sigma_valid(sk[q]);
-                        const float a = __expf(-sk[q]);
-                        s_val[k * kThreads + pc[q].tid] = a;
-                        s_pos[k * kThreads + pc[q].tid] = k;
-                        const int h = k / kHalf;
-                        if (k % kHalf == 0 || a < gv[q][h]) gv[q][h] = a, gs[q][h] = k;
+#pragma unroll
+                        for (int o = 0; o < 2; ++o) {
+                            const int kk = k + o;
+                            const float sk = o ? s2[q].y : s2[q].x;
+                            fast[q] = fast[q] && sigma_valid(sk);
+                            const float a = __expf(-sk);
+                            s_val[kk * kThreads + pc[q].tid] = a;
+                            s_pos[kk * kThreads + pc[q].tid] = kk;
+                            const int h = kk / kHalf;
+                            if (kk % kHalf == 0 || a < gv[q][h]) gv[q][h] = a, gs[q][h] = kk;
+                        }
                     }
                 }
             }
@@ -216,39 +255,37 @@ __device__ __forceinline__ void select_topk(const int2 range, const int *__restr
         for (int q = 1; q < PPT; ++q) e = min(e, start[q]);
         if (all_full()) {
             // the common case: every pixel full (all starts equal), only the replacement rule
-#pragma unroll 2
-            for (; e < count; ++e) {
-                const float4 g4 = s_geo[e];
-                const float cc = s_cc[e];
-                float sk[PPT];
-                column_sigma<PPT>(g4, cc, px, py, sk);
+            for (; e < count; e += 2) {
+                float2 s2[PPT];
+                pair_sigma<PPT>(s_geo[e], s_geo[e + 1], *reinterpret_cast<const float2 *>(&s_cc[e]), npx, npy, s2);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
                     // every slot holds an alpha >= 0 (the minimum of a pixel outside the image is infinite), so sigma >= 0 suffices: an
-                    // infinite sigma gives alpha = 0, which replaces nothing, and NaN fails the test
-                    const float sigma = sk[q];
-                    const float alpha = __expf(-sigma);
-                    if (sigma >= 0.f && alpha > min_val[q]) insert(q, alpha, base + e);
+                    // infinite sigma gives alpha = 0, which replaces nothing, and NaN (also the padding entry) fails the test
+                    const float a0 = __expf(-s2[q].x), a1 = __expf(-s2[q].y);
+                    if (s2[q].x >= 0.f && a0 > min_val[q]) insert(q, a0, base + e);
+                    if (s2[q].y >= 0.f && a1 > min_val[q]) insert(q, a1, base + e + 1);
                 }
             }
         } else {
-            for (; e < count; ++e) {
-                const float4 g4 = s_geo[e];
-                const float cc = s_cc[e];
-                float sk[PPT];
-                column_sigma<PPT>(g4, cc, px, py, sk);
+            for (; e < count; e += 2) {
+                float2 s2[PPT];
+                pair_sigma<PPT>(s_geo[e], s_geo[e + 1], *reinterpret_cast<const float2 *>(&s_cc[e]), npx, npy, s2);
 #pragma unroll
                 for (int q = 0; q < PPT; ++q) {
-                    if (e < start[q]) continue;
-                    const float sigma = sk[q];
-                    if (!sigma_valid(sigma)) continue;
-                    const float alpha = __expf(-sigma);
-                    if (filled[q] < kTopK) {
-                        s_val[filled[q] * kThreads + pc[q].tid] = alpha;
-                        s_pos[filled[q] * kThreads + pc[q].tid] = base + e;
-                        if (++filled[q] == kTopK) rescan(q);
-                    } else if (alpha > min_val[q]) {
-                        insert(q, alpha, base + e);
+                    if (e < start[q]) continue;  // starts are even: both entries of the pair or neither
+#pragma unroll
+                    for (int o = 0; o < 2; ++o) {
+                        const float sigma = o ? s2[q].y : s2[q].x;
+                        if (!sigma_valid(sigma)) continue;  // also the padding entry
+                        const float alpha = __expf(-sigma);
+                        if (filled[q] < kTopK) {
+                            s_val[filled[q] * kThreads + pc[q].tid] = alpha;
+                            s_pos[filled[q] * kThreads + pc[q].tid] = base + e + o;
+                            if (++filled[q] == kTopK) rescan(q);
+                        } else if (alpha > min_val[q]) {
+                            insert(q, alpha, base + e + o);
+                        }
                     }
                 }
             }
@@ -318,7 +355,7 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
     constexpr int kMaxC = C > 0 ? C : kMaxChannels;
     const int channels = C > 0 ? C : channels_rt;
     __shared__ float4 s_geo[kChunk];         // x, y, conic a / 2, conic b; then the colours of a one-chunk list
-    __shared__ float s_cc[kChunk];           // conic c / 2
+    __shared__ __align__(16) float s_cc[kChunk];  // conic c / 2
     __shared__ int s_ids[kThreads * kTopK];  // the slots' list positions during the selection, then the IDs of [H, W, 10] lists
 
     const int tile = blockIdx.x;
@@ -367,10 +404,12 @@ __global__ void __launch_bounds__(kFwdThreads, 8)
                 if (pos[k] < 0) continue;
                 const float d = val[q][k];
                 denom += d;
-                const float4 f = s_geo[pos[k]];
-                const float fc[4] = {f.x, f.y, f.z, f.w};
+                const float4 f4 = s_geo[pos[k]];
+                const float fa[4] = {f4.x, f4.y, f4.z, f4.w};
+                float f[kMaxC];
 #pragma unroll
-                for (int c = 0; c < kMaxC && c < 4; ++c) pix[c] = fmaf(d, fc[c], pix[c]);
+                for (int c = 0; c < kMaxC; ++c) f[c] = fa[c < 4 ? c : 0];
+                add_weighted(d, f, pix);
             }
         } else {
 #pragma unroll
@@ -594,11 +633,12 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
 //      value: v_conic = (S_xx / 2, S_xy, S_yy / 2), v_xy = the next two sums, v_color = S_c.
 template <int kMaxC>
 struct PairSmem {
-    static constexpr bool kPackedOut = kMaxC <= 4;  // a pixel's v_out as one float4
-    float4 geo[kPairStage];         // x, y, conic a / 2, conic b
-    float cc[kPairStage];           // conic c / 2
-    float col[kPairStage * kMaxC];  // features
-    int gid[kPairStage];            // Gaussian IDs
+    static constexpr bool kPackedOut = kMaxC <= 4;  // a pixel's v_out and an entry's features as one float4 each
+    float4 geo[kPairStage];  // x, y, conic a / 2, conic b: per entry, or in pairs of entries (the selection's layout, stage_paired)
+    float cc[kPairStage];    // conic c / 2
+    float4 col4[kPackedOut ? kPairStage : 1];           // features (C <= 4, zero-padded)
+    float col[kPackedOut ? 1 : kPairStage * kMaxC];      // features (C > 4)
+    int gid[kPairStage];                                 // Gaussian IDs
     union {
         int pos[kTopK][kThreads];  // the selection's slots: positions in the tile's list (-1 empty), read into registers before step 2
         struct {
@@ -608,15 +648,52 @@ struct PairSmem {
         } g;
     };
     float alpha[kTopK][kThreads];                // d_k = exp(-sigma_k) of each slot (the selection's alphas)
-    float4 pix[kThreads];                        // x, y, S
+    float4 pix[kThreads];                        // -x, -y, S
     float4 vout4[kPackedOut ? kThreads : 1];     // v_out / D (C <= 4)
     float vout[kPackedOut ? 1 : kMaxC][kPackedOut ? 1 : kThreads];  // v_out / D per channel (C > 4)
     int wsum[kThreads / 32];
 };
 
-// Stage entries [chunk, chunk + kPairStage) of a tile's list for the backward pass (every thread of the CTA calls it): centres, the conic
-// halved as the selection stages it (a / 2, b, c / 2) and the colours
+// An entry's features into shared memory (zero beyond the channel count)
 template <int kMaxC>
+__device__ __forceinline__ void stage_colors(PairSmem<kMaxC> &sm, const int e, const float *__restrict__ f, const int channels) {
+    if constexpr (PairSmem<kMaxC>::kPackedOut) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) v[c] = __ldg(&f[c]);
+        sm.col4[e] = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c)
+            if (c < channels) sm.col[e * kMaxC + c] = __ldg(&f[c]);
+    }
+}
+
+// A staged entry's features (zero beyond the channel count)
+template <int kMaxC>
+__device__ __forceinline__ void staged_colors(const PairSmem<kMaxC> &sm, const int e, const int channels, float (&f)[kMaxC]) {
+    if constexpr (PairSmem<kMaxC>::kPackedOut) {
+        const float4 v = sm.col4[e];
+        const float va[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) f[c] = va[c];
+    } else {
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) f[c] = c < channels ? sm.col[e * kMaxC + c] : 0.f;
+    }
+}
+
+// Staged geometry of entry e, (x, y, a / 2, b), from either layout
+template <bool kPaired>
+__device__ __forceinline__ float4 staged_geo(const float4 *geo, const int e) {
+    if constexpr (kPaired) return paired_geo(geo, e);
+    else return geo[e];
+}
+
+// Stage entries [chunk, chunk + kPairStage) of a tile's list for the backward pass (every thread of the CTA calls it): centres, the conic
+// halved as the selection stages it (a / 2, b, c / 2), per entry or in the selection's paired layout, and the colours
+template <bool kPaired, int kMaxC>
 __device__ __forceinline__ void stage_pair_chunk(PairSmem<kMaxC> &sm, const int chunk, const int len, const int2 range,
                                                  const int *__restrict__ ids_sorted, const float2 *__restrict__ xys,
                                                  const float *__restrict__ conics, const float *__restrict__ colors, const int channels) {
@@ -625,11 +702,13 @@ __device__ __forceinline__ void stage_pair_chunk(PairSmem<kMaxC> &sm, const int 
         const int g = __ldg(&ids_sorted[range.x + chunk + e]);
         const float2 xy = __ldg(&xys[g]);
         sm.gid[e] = g;
-        sm.geo[e] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
-        sm.cc[e] = 0.5f * __ldg(&conics[3 * g + 2]);
-#pragma unroll
-        for (int c = 0; c < kMaxC; ++c)
-            if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+        if constexpr (kPaired) {
+            stage_paired(sm.geo, sm.cc, e, xy, __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]), __ldg(&conics[3 * g + 2]));
+        } else {
+            sm.geo[e] = make_float4(xy.x, xy.y, 0.5f * __ldg(&conics[3 * g]), __ldg(&conics[3 * g + 1]));
+            sm.cc[e] = 0.5f * __ldg(&conics[3 * g + 2]);
+        }
+        stage_colors(sm, e, colors + (size_t)g * channels, channels);
     }
 }
 
@@ -645,12 +724,13 @@ __device__ __forceinline__ float2 pixel_terms(const float denom, const float (&u
     return make_float2(inv, -inv2 * vu);
 }
 
-// Step 1's per-pixel record: coordinates, S and v_out / D (terms = (1 / D, S)). Step 3 forms dL/dsigma_k = -d_k (f_k . (v_out / D) + S)
-// and the colour gradient d_k (v_out / D): the reference's -d_k (s_k / D + S) and (d_k / D) v_out with the division applied to v_out.
+// Step 1's per-pixel record: the negated coordinates, S and v_out / D (terms = (1 / D, S)). Step 3 forms dL/dsigma_k =
+// -d_k (f_k . (v_out / D) + S) and the colour gradient d_k (v_out / D): the reference's -d_k (s_k / D + S) and (d_k / D) v_out with the
+// division applied to v_out.
 template <int kMaxC>
 __device__ __forceinline__ void store_pixel_grad(PairSmem<kMaxC> &sm, const int tid, const float px, const float py, const float2 terms,
                                                  const float (&v_out)[kMaxC]) {
-    sm.pix[tid] = make_float4(px, py, terms.y, 0.f);
+    sm.pix[tid] = make_float4(-px, -py, terms.y, 0.f);
     if constexpr (PairSmem<kMaxC>::kPackedOut) {
         float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -678,7 +758,7 @@ __device__ __forceinline__ unsigned transpose_bits(unsigned x, const int lane) {
 // last read of sm.pos): sm.alpha and sm.pix / sm.vout hold step 1's per-slot and per-pixel values, key[k] the list position of the
 // thread's slot k (-1 empty). The staged chunk of the list is used for chunk 0 unless restage_first; every other chunk is staged by
 // stage(chunk).
-template <int NV, int kMaxC, typename Stage>
+template <int NV, bool kPaired, int kMaxC, typename Stage>
 __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const int (&key)[kTopK], const int len, const int2 range,
                                                    const int *__restrict__ ids_sorted, const int channels, const bool restage_first,
                                                    Stage stage, float *__restrict__ v_xy, float *__restrict__ v_conic,
@@ -776,23 +856,27 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
         }
         __syncthreads();
 
-        // 3. one warp per entry
+        // 3. one warp per entry. Packed instructions take two sums at a time: (dx, dy) = (x, y) + (-px, -py), (tx, ty) = v (dx, dy),
+        //    (S_xx, S_xy) += tx (dx, dy), the two v_xy sums += (b, c) ty then (a, b) tx, and channel pairs += d (v_out / D); each component
+        //    is rounded as the scalar fmaf / fadd / fmul would round it.
         for (int e = warp; e < n_entries; e += kThreads / 32) {
             const int b = sm.g.start[e], n = sm.g.start[e + 1] - b;
             if (n == 0) continue;  // no pixel kept this Gaussian (uniform over the warp)
-            const float4 q = sm.geo[e];
+            const float4 q = staged_geo<kPaired>(sm.geo, e);
             const float ca = 2.f * q.z, cb = q.w, cc = 2.f * sm.cc[e];  // the staged conic is halved; doubling it back is exact
+            const float2 qxy = make_float2(q.x, q.y), cbc = make_float2(cb, cc), cab = make_float2(ca, cb);
             float f[kMaxC];
+            staged_colors(sm, e, channels, f);
+            float2 s01 = make_float2(0.f, 0.f), s34 = make_float2(0.f, 0.f);
+            float s2 = 0.f;
+            float sc[kMaxC];
 #pragma unroll
-            for (int c = 0; c < kMaxC; ++c) f[c] = c < channels ? sm.col[e * kMaxC + c] : 0.f;
-            float acc[NV];
-#pragma unroll
-            for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+            for (int c = 0; c < kMaxC; ++c) sc[c] = 0.f;
             for (int i = lane; i < n; i += 32) {
                 const unsigned rec = sm.g.pairs[b + i];
                 const int slot = (int)(rec >> 8), pix = (int)(rec & 255u);
                 const float d = sm.alpha[slot][pix];
-                const float4 pr = sm.pix[pix];  // x, y, S
+                const float4 pr = sm.pix[pix];  // -x, -y, S
                 float vo[kMaxC];                 // v_out / D
                 if constexpr (PairSmem<kMaxC>::kPackedOut) {
                     const float4 v4 = sm.vout4[pix];
@@ -807,19 +891,20 @@ __device__ __forceinline__ void pairs_grouped_sums(PairSmem<kMaxC> &sm, const in
 #pragma unroll
                 for (int c = 0; c < kMaxC; ++c) sk = fmaf(f[c], vo[c], sk);
                 const float vs = -d * (sk + pr.z);  // dL/dsigma
-                const float dx = q.x - pr.x, dy = q.y - pr.y;
-                const float tx = vs * dx, ty = vs * dy;
-                acc[0] = fmaf(tx, dx, acc[0]);
-                acc[1] = fmaf(tx, dy, acc[1]);
-                acc[2] = fmaf(ty, dy, acc[2]);
+                const float2 dxy = __fadd2_rn(qxy, make_float2(pr.x, pr.y));
+                const float2 t = __fmul2_rn(make_float2(vs, vs), dxy);
+                s01 = __ffma2_rn(make_float2(t.x, t.x), dxy, s01);
+                s2 = fmaf(t.y, dxy.y, s2);
                 // v_xy per pair, a v dx + b v dy and b v dx + c v dy, as the reference sums v (a dx + b dy): with the conic factored out of
                 // the sums, a Sx and b Sy can cancel to a few parts in 10^4 of themselves and lose the result's accuracy
-                acc[3] = fmaf(ca, tx, fmaf(cb, ty, acc[3]));
-                acc[4] = fmaf(cb, tx, fmaf(cc, ty, acc[4]));
-#pragma unroll
-                for (int c = 0; c < kMaxC; ++c)
-                    if (c < channels) acc[5 + c] = fmaf(d, vo[c], acc[5 + c]);
+                s34 = __ffma2_rn(cbc, make_float2(t.y, t.y), s34);
+                s34 = __ffma2_rn(cab, make_float2(t.x, t.x), s34);
+                add_weighted(d, vo, sc);
             }
+            float acc[NV];
+            acc[0] = s01.x, acc[1] = s01.y, acc[2] = s2, acc[3] = s34.x, acc[4] = s34.y;
+#pragma unroll
+            for (int v = 5; v < NV; ++v) acc[v] = v - 5 < kMaxC && v - 5 < channels ? sc[v - 5 < kMaxC ? v - 5 : 0] : 0.f;
             const float total = warp_sum_scatter<NV>(acc, lane);
             if (holds_total) {
                 // the gradient value this lane adds: v_conic (S_xx / 2, S_xy, S_yy / 2), v_xy, v_colors
@@ -883,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
 
     // stage the first chunk of the list (lists longer than kPairStage are processed in chunks; their other entries are read from global
     // memory in step 1)
-    auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
+    auto stage = [&](int chunk) { stage_pair_chunk<false>(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
     stage(0);
     __syncthreads();
 
@@ -899,9 +984,9 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
             if (key[k] < kPairStage) {
                 const int e = key[k];
                 d = __expf(-halved_sigma(sm.geo[e], sm.cc[e], px, py));
-#pragma unroll
-                for (int c = 0; c < kMaxC; ++c)
-                    if (c < channels) u[c] = fmaf(d, sm.col[e * kMaxC + c], u[c]);
+                float f[kMaxC];
+                staged_colors(sm, e, channels, f);
+                add_weighted(d, f, u);
             } else {
                 // past the staged chunk of a longer list
                 const int g = __ldg(&ids_sorted[range.x + key[k]]);
@@ -918,7 +1003,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     }
     store_pixel_grad(sm, tid, px, py, pixel_terms<kMaxC>(denom, u, v_out), v_out);
 
-    pairs_grouped_sums<NV>(sm, key, len, range, ids_sorted, channels, false, stage, v_xy, v_conic, v_colors);
+    pairs_grouped_sums<NV, false>(sm, key, len, range, ids_sorted, channels, false, stage, v_xy, v_conic, v_colors);
 }
 
 // ---- the training step's rasterization in one kernel -------------------------------------------------------------------------------
@@ -965,9 +1050,7 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
         for (int e = tid; e < len; e += kThreads) {
             const int g = __ldg(&ids_sorted[range.x + e]);
             sm.gid[e] = g;
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) sm.col[e * kMaxC + c] = __ldg(&colors[(size_t)g * channels + c]);
+            stage_colors(sm, e, colors + (size_t)g * channels, channels);
         }
     }
     __syncthreads();  // the colours are staged, and every slot position is read (sm.pos is step 2's space)
@@ -985,16 +1068,15 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
         if (key[k] < 0) continue;
         const float d = val[0][k];
         denom += d;
+        float f[kMaxC];
         if (one_chunk) {
-#pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) u[c] = fmaf(d, sm.col[key[k] * kMaxC + c], u[c]);
+            staged_colors(sm, key[k], channels, f);
         } else {
-            const float *f = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
+            const float *fg = colors + (size_t)__ldg(&ids_sorted[range.x + key[k]]) * channels;
 #pragma unroll
-            for (int c = 0; c < kMaxC; ++c)
-                if (c < channels) u[c] = fmaf(d, __ldg(&f[c]), u[c]);
+            for (int c = 0; c < kMaxC; ++c) f[c] = c < channels ? __ldg(&fg[c]) : 0.f;
         }
+        add_weighted(d, f, u);
     }
     const float inv_denom = 1.f / denom;
     float v_out[kMaxC];
@@ -1019,8 +1101,8 @@ __global__ void __launch_bounds__(kThreads, NV > 8 ? 3 : C > 0 ? 5 : 4)
     store_pixel_grad(sm, tid, (float)pc.j, (float)pc.i, terms, v_out);
 
     // 4. backward, steps 2 and 3
-    auto stage = [&](int chunk) { stage_pair_chunk(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
-    pairs_grouped_sums<NV>(sm, key, len, range, ids_sorted, channels, !one_chunk, stage, v_xy, v_conic, v_colors);
+    auto stage = [&](int chunk) { stage_pair_chunk<true>(sm, chunk, len, range, ids_sorted, xys, conics, colors, channels); };
+    pairs_grouped_sums<NV, true>(sm, key, len, range, ids_sorted, channels, !one_chunk, stage, v_xy, v_conic, v_colors);
 }
 
 template <int C, int NV>
