@@ -310,6 +310,7 @@ def run_ours(args, wl):
     hbm_peak, peak_kind = peaks()
     p, c, n, k = wl.num_pixels, wl.channels, wl.num_gaussians, pipeline.TOP_K
     roofline = raster_roofline(stage_ms, p, c, n, k, num_isect, wl.num_tiles, hbm_peak, peak_kind, wl.name)
+    kernels_per_step, capacity = step.kernels_per_step, step.capacity
     step_bytes = (p * (8 * c + 8 * k) + n * 4 * (5 + 7 + 2 * (5 + c) + (5 + c) + 5 + 5) + num_isect * 4 * 5 + wl.num_tiles * 16)
     loss_bytes = 12 * c * p
 
@@ -327,6 +328,19 @@ def run_ours(args, wl):
         cpu = {"value": rate, "unit": "steps/s", "cores": threads, "kind": "port",
                "sample": f"{steps} whole {wl.width}x{wl.height} steps of the C restatement on {threads} threads ({cpu_model()})"}
 
+    # the 2160p image split into tile-row bands over the same ranks (strong scaling; at N=1 the whole image on one GPU, the reference
+    # point of the scaling), reported beside the independent-image line
+    bands_leg = None
+    if not args.no_bands and wl.name == "cfg3_1080p":
+        del graph, step
+        torch.cuda.empty_cache()
+        b = measure_bands(args, workloads.get_workload("cfg4_2160p"), world, rank, local, exchange=args.exchange,
+                          steps=min(args.steps, 50), e2e=False, cpu=False, stages=False)
+        if rank == 0:
+            bands_leg = {k: b[k] for k in ("value", "unit", "n_gpus", "ms_per_step", "scaling", "exchange", "exchange_ms",
+                                            "band_ms_per_rank", "band_intersections", "gaussian_pixel_evals_per_s", "clocks")}
+            bands_leg["config"] = b["config"]
+
     if rank == 0:
         clk = clocks.summary()
         out = {
@@ -334,28 +348,30 @@ def run_ours(args, wl):
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded sinusoid target, random Gaussians; one independent image per GPU)",
             "config": workload_config(wl, num_isect, world),
-            "capacity": step.capacity, "graph": "one CUDA graph per step",
+            "capacity": capacity, "graph": "one CUDA graph per step",
             "gaussian_pixel_evals_per_step": evals, "gaussian_pixel_evals_per_s": evals * value,
             "stages_ms": stage_ms,
             "roofline": roofline,
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
-            "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
-            "clocks": clk,
+            "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph, "cpu_baseline": cpu,
+            "gpu_launches": kernels_per_step * args.steps, "clocks": clk, "bands_2160p": bands_leg,
         }
         print(json.dumps(out))
     if world > 1:
         torch.distributed.destroy_process_group()
 
 
-def run_bands(args, wl):
-    """One image in tile-row bands, one band per GPU (strong scaling): every rank projects all Gaussians, bins, renders and
-    back-propagates its rows; the partial gradients and loss are summed with one NCCL all-reduce; every rank finishes the projection
-    backward. value = whole-image steps/s; per-step time is the max over ranks."""
+def measure_bands(args, wl, world, rank, local, exchange="peer", steps=None, e2e=True, cpu=True, stages=True):
+    """One image in tile-row bands, one band per GPU (strong scaling), on an initialised process group: every rank projects all
+    Gaussians, bins, renders and back-propagates its rows; the partials are combined by the peer-memory exchange (igs_band_reduce: each
+    rank reduces one share of the Gaussians and runs its projection backward, the whole step one CUDA graph) or by an NCCL all-reduce
+    followed by the projection backward on every rank. value = whole-image steps/s; per-step time is the max over ranks. Returns rank
+    0's JSON dict (None on the other ranks)."""
     from igs_b200 import bands
 
-    world, rank, local = dist_setup(args.gpus)
+    steps = steps or args.steps
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     inp = workloads.make_inputs(wl)  # the same image on every rank
@@ -365,27 +381,28 @@ def run_bands(args, wl):
     r0, r1 = bands.band_rows(tiles_y, world, rank, [r + 32.0 * tiles_x for r in per_row])
     group = torch.distributed.group.WORLD if world > 1 else None
     step = bands.BandStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], wl.height, wl.width, r0, r1, group=group,
-                          fused=not args.split)
+                          fused=not args.split, exchange=exchange)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(args.warmup):
         step.replay()
     torch.cuda.synchronize()
+    step.check()
     band_isect = int(step.num_intersects.item())
     if band_isect > step.capacity:
         raise SystemExit(f"intersections {band_isect} exceed the capacity {step.capacity}")
     evals = torch.tensor([step.gaussian_pixel_evals()], device=device, dtype=torch.float64)
 
     barrier = (lambda: torch.distributed.barrier()) if world > 1 else (lambda: None)
-    # the ranks' steps are coupled by the all-reduce, so each L2 flush is followed by a one-float all-reduce that lines up the ranks'
+    # the ranks' steps are coupled by the exchange, so each L2 flush is followed by a one-float all-reduce that lines up the ranks'
     # start events: otherwise a rank's timed step would include waiting for the other ranks' flushes
     token = torch.zeros(1, device=device)
     align = (lambda: torch.distributed.all_reduce(token)) if world > 1 else (lambda: None)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
+        for i in range(steps):
             flush.zero_()
             align()
             starts[i].record()
@@ -393,26 +410,35 @@ def run_bands(args, wl):
             ends[i].record()
         torch.cuda.synchronize()
     barrier()
+    step.check()
     total_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(starts, ends))], device=device, dtype=torch.float64)
 
-    # the band's own work (one graph, no communication) and the all-reduce alone, per rank
-    local_ms = time_graph(step.local_graph, max(5, min(50, args.steps)), flush)
+    # the band's own work (one graph, no communication) and the exchange alone, per rank
+    local_graph = step._capture(step.LOCAL)
+    local_ms = time_graph(local_graph, max(5, min(50, steps)), flush)
+    del local_graph
     stage_ms = {}
-    for s_ in ((("_forward",), ("_backward",)) if args.split else (("_raster",),)) if not args.no_stages else ():
+    for s_ in ((("_forward",), ("_backward",)) if args.split else (("_raster",),)) if stages else ():
         g = step._capture(s_)
-        stage_ms[s_[0].strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
+        stage_ms[s_[0].strip("_")] = time_graph(g, max(5, min(50, steps)), flush)
         del g
-    ar_ms = 0.0
+    xchg_ms = 0.0
     if world > 1:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
+        torch.cuda.synchronize()
         a.record()
         for _ in range(20):
-            step.all_reduce()
+            if step.exchange == "peer":
+                step._exchange()
+            else:
+                step.all_reduce()
+                step._project_backward()
         b.record()
         torch.cuda.synchronize()
-        ar_ms = a.elapsed_time(b) / 20
-    per_rank = torch.tensor([local_ms, float(r1 - r0), float(band_isect)], device=device, dtype=torch.float64)
+        step.check()
+        xchg_ms = a.elapsed_time(b) / 20
+    per_rank = torch.tensor([local_ms, float(r0), float(r1), float(band_isect)], device=device, dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(evals)
@@ -421,19 +447,20 @@ def run_bands(args, wl):
     else:
         gathered = [per_rank]
     total_ms = float(total_ms.item())
-    ms_per_step = total_ms / args.steps
-    value = args.steps / (total_ms / 1e3)
+    ms_per_step = total_ms / steps
+    value = steps / (total_ms / 1e3)
 
-    e2e = None
-    if not args.no_e2e:
-        e2e = run_step_e2e(args, step, (step.means, step.scales, step.rotations, step.features), inp, device, world, "bands")
+    e2e_out = None
+    if e2e and not args.no_e2e:
+        e2e_out = run_step_e2e(args, step, (step.means, step.scales, step.rotations, step.features), inp, device, world, "bands")
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        rate, threads, steps = cpu_step_rate(wl, inp)
-        cpu = {"value": rate, "unit": "steps/s", "cores": threads, "kind": "port",
-               "sample": f"{steps} whole {wl.width}x{wl.height} steps of the C restatement on {threads} threads ({cpu_model()})"}
+    cpu_out = None
+    if cpu and rank == 0 and world == 1 and not args.no_cpu:
+        rate, threads, nsteps = cpu_step_rate(wl, inp)
+        cpu_out = {"value": rate, "unit": "steps/s", "cores": threads, "kind": "port",
+                   "sample": f"{nsteps} whole {wl.width}x{wl.height} steps of the C restatement on {threads} threads ({cpu_model()})"}
 
+    out = None
     if rank == 0:
         hbm_peak, peak_kind = peaks()
         c, n, k = wl.channels, wl.num_gaussians, 10
@@ -442,22 +469,36 @@ def run_bands(args, wl):
         if stage_ms:
             roofline = raster_roofline(stage_ms, p, c, n, k, band_isect, step.num_tiles, hbm_peak, peak_kind, None, " (rank 0's band)")
         total_evals = float(evals.item())
+        how = ("peer-memory exchange (igs_band_reduce: each rank sums one share of the Gaussians from every rank's partials over NVLink "
+               "and runs its projection backward)" if step.exchange == "peer" else
+               f"NCCL all-reduce of {step.reduced.numel()} floats, projection backward on every rank") if world > 1 else "one band"
         out = {
-            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded sinusoid target, random Gaussians; one image split into tile-row bands)",
             "config": {"workload": wl.name, "height": wl.height, "width": wl.width, "gaussians": wl.num_gaussians, "channels": wl.channels,
-                       "tile": 16, "top_k": 10, "parallelism": f"{world} tile-row bands + NCCL all-reduce of {step.reduced.numel()} floats",
+                       "tile": 16, "top_k": 10, "parallelism": f"{world} tile-row bands + {how}",
                        "bands": [[int(g[1].item()), int(g[2].item())] for g in gathered],
                        "l2": "flushed between timed steps (256 MB write outside the event intervals)",
-                       "graph": "band work as one CUDA graph, NCCL all-reduce, projection backward as a second graph"},
+                       "graph": ("the whole step as one CUDA graph" if step.exchange == "peer" or world == 1 else
+                                 "band work as one CUDA graph, NCCL all-reduce, projection backward as a second graph")},
+            "exchange": step.exchange if world > 1 else None,
             "gaussian_pixel_evals_per_step": total_evals, "gaussian_pixel_evals_per_s": total_evals * value,
-            "band_ms_per_rank": [float(g[0].item()) for g in gathered], "all_reduce_ms": ar_ms, "stages_ms": stage_ms,
-            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": step.kernels_per_step * args.steps,
+            "band_ms_per_rank": [float(g[0].item()) for g in gathered],
+            "band_intersections": [int(g[3].item()) for g in gathered], "exchange_ms": xchg_ms, "stages_ms": stage_ms,
+            "roofline": roofline, "e2e": e2e_out, "cpu_baseline": cpu_out, "gpu_launches": step.kernels_per_step * steps,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(out))
     step.release()
+    return out
+
+
+def run_bands(args, wl):
+    """`--workload cfg4_2160p`: the band split as the JSON line's own measurement."""
+    world, rank, local = dist_setup(args.gpus)
+    out = measure_bands(args, wl, world, rank, local, exchange=args.exchange)
+    if rank == 0:
+        print(json.dumps(out))
     if world > 1:
         torch.distributed.destroy_process_group()
 
@@ -701,6 +742,8 @@ def main():
     ap.add_argument("--no-stages", action="store_true", help="skip the per-stage timing")
     ap.add_argument("--split", action="store_true", help="run the step with the separate top-K forward and backward kernels instead of "
                     "the fused step kernel (for comparison)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"], help="how the tile-row bands combine their gradients")
+    ap.add_argument("--no-bands", action="store_true", help="skip the 2160p tile-row band leg of the default workload")
     ap.add_argument("--aux", action="store_true", help="time the rows around the step (neighbour search, feature weights, LOO) instead")
     args = ap.parse_args()
     wl = workloads.get_workload(args.workload)

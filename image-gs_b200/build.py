@@ -19,7 +19,7 @@ OUT_DIR = os.path.join(HERE, "igs_b200")
 LIB = os.path.join(OUT_DIR, "libigs_b200.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 
-FAST_MATH = {"project.cu", "binning.cu", "raster.cu", "rate.cu", "loo.cu"}
+FAST_MATH = {"project.cu", "binning.cu", "raster.cu", "rate.cu", "loo.cu", "exchange.cu"}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-I", INCLUDE, "-Xptxas", "-v"]
 

@@ -1,44 +1,24 @@
 // 2D projection of the Gaussians: pixel centers, conics (inverse covariances), 3-sigma radii and tile footprints, and the backward pass to
 // means, scales and rotations. Compiled with --use_fast_math like the reference extension (gsplat/setup.py:70), because the radius
 // ceil(3 sqrt(lambda_max)) and the tile bounding box decide the tile binning, which must agree with the reference bit for bit: the same
-// approximate sqrt / reciprocal / sin / cos and the same product order (glm's mat2 product, which the M2 helper below reproduces so that
-// the compiler contracts the same multiply-adds).
+// approximate sqrt / reciprocal / sin / cos and the same product order (glm's mat2 product, which the M2 helper of project_math.cuh reproduces so
+// that the compiler contracts the same multiply-adds).
 //
 // One thread per Gaussian, parameters read as float2 vectors; every output element is written (the reference relies on zero-initialized
 // outputs instead), so callers need no memset.
 #include "igs_common.cuh"
+#include "project_math.cuh"
 
 namespace {
 
+using igs::diag;
 using igs::kTile;
-
-// 2x2 matrix stored [column][row]; product terms in glm's order: (a*b)[c][r] = a[0][r]*b[c][0] + a[1][r]*b[c][1]
-struct M2 {
-    float m[2][2];
-};
-
-__device__ __forceinline__ M2 mul(const M2 &a, const M2 &b) {
-    M2 o;
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) o.m[c][r] = a.m[0][r] * b.m[c][0] + a.m[1][r] * b.m[c][1];
-    return o;
-}
-
-__device__ __forceinline__ M2 transpose(const M2 &a) {
-    M2 o;
-    o.m[0][0] = a.m[0][0];
-    o.m[0][1] = a.m[1][0];
-    o.m[1][0] = a.m[0][1];
-    o.m[1][1] = a.m[1][1];
-    return o;
-}
-
-// Rotation by theta as in helpers.cuh:265-276 (cos on the diagonal, [0][1] = -sin), and its derivative (helpers.cuh:278-289)
-__device__ __forceinline__ M2 rotation(float cs, float sn) { return M2{{{cs, -sn}, {sn, cs}}}; }
-__device__ __forceinline__ M2 rotation_grad(float cs, float sn) { return M2{{{-sn, -cs}, {cs, -sn}}}; }
-__device__ __forceinline__ M2 diag(float a, float b) { return M2{{{a, 0.f}, {0.f, b}}}; }
+using igs::M2;
+using igs::mul;
+using igs::projection_grad;
+using igs::ProjectionGrad;
+using igs::rotation;
+using igs::transpose;
 
 // Tile rectangle [x0, x1) x [y0, y1) covered by a pixel center and radius, clamped to the grid (helpers.cuh:11-43)
 __device__ __forceinline__ void tile_rect(float cx, float cy, float radius, unsigned tiles_x, unsigned tiles_y, unsigned &x0, unsigned &y0,
@@ -115,39 +95,14 @@ __global__ void __launch_bounds__(256) project_bwd_kernel(const int n, const flo
         v_rot[i] = 0.f;
         return;
     }
-    const float x = conics[3 * i], y = conics[3 * i + 1], z = conics[3 * i + 2];
-    const float gx = v_conic[3 * i], gy = v_conic[3 * i + 1], gz = v_conic[3 * i + 2];
-    const M2 X{{{x, y}, {y, z}}};
-    const M2 G{{{gx, gy}, {gy, gz}}};
-    const M2 negX{{{-x, -y}, {-y, -z}}};
-    const M2 V = mul(mul(negX, G), X);
-    const float G11 = V.m[0][0], G12 = V.m[1][0] + V.m[0][1], G22 = V.m[1][1];
-
-    const float2 s = __ldg(&scales[i]);
-    const float theta = __ldg(&rotations[i]);
-    const float cs = cosf(theta), sn = sinf(theta);
-    const M2 R = rotation(cs, sn);
-    const M2 Rg = rotation_grad(cs, sn);
-    const M2 S = diag(s.x, s.y);
-    const M2 M = mul(R, S);
-    const M2 t1 = mul(mul(Rg, S), transpose(M));
-    const M2 t2 = mul(mul(M, transpose(S)), transpose(Rg));
-    M2 th;
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) th.m[c][r] = t1.m[c][r] + t2.m[c][r];
-    const M2 sxg = mul(mul(R, diag(2.f * s.x, 0.f)), transpose(R));
-    const M2 syg = mul(mul(R, diag(0.f, 2.f * s.y)), transpose(R));
-
-    v_cov2d[3 * i + 0] = G11;
-    v_cov2d[3 * i + 1] = G12;
-    v_cov2d[3 * i + 2] = G22;
-    v_scale[i] = make_float2(G11 * sxg.m[0][0] + 2 * G12 * sxg.m[0][1] + G22 * sxg.m[1][1],
-                             G11 * syg.m[0][0] + 2 * G12 * syg.m[0][1] + G22 * syg.m[1][1]);
-    v_rot[i] = G11 * th.m[0][0] + 2 * G12 * th.m[0][1] + G22 * th.m[1][1];
-    const float2 vxy = v_xy[i];
-    v_mean2d[i] = make_float2(vxy.x * img_w, vxy.y * img_h);
+    const ProjectionGrad pg = projection_grad(__ldg(&scales[i]), __ldg(&rotations[i]), img_w, img_h, conics + 3 * i, v_conic + 3 * i,
+                                              v_xy[i]);
+    v_cov2d[3 * i + 0] = pg.cov2d[0];
+    v_cov2d[3 * i + 1] = pg.cov2d[1];
+    v_cov2d[3 * i + 2] = pg.cov2d[2];
+    v_scale[i] = pg.scale;
+    v_rot[i] = pg.rot;
+    v_mean2d[i] = pg.mean2d;
 }
 
 }  // namespace

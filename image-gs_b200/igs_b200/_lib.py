@@ -42,6 +42,12 @@ SIGNATURES = {
     "igs_raster_fwd_topk_tiles_l1_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P,
                                                   P, P, c_size_t, P]),
     "igs_raster_bwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
+    "igs_ipc_export": (c_int, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "igs_ipc_open": (c_int, [P, ctypes.c_uint64, ctypes.POINTER(c_void_p)]),
+    "igs_ipc_close": (c_int, [P, ctypes.c_uint64]),
+    "igs_band_sync_bytes": (c_size_t, []),
+    "igs_band_results_floats": (c_size_t, [c_int, c_int]),
+    "igs_band_reduce": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, c_int, c_int, P, P, c_int, P]),
     "igs_loo_loss_increase": (c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, c_int, c_float, P, P]),
     "igs_feature_weights": (c_int, [c_int, c_int, c_int, P, P, P, c_double, P, P]),
     "igs_neighbors_workspace": (c_size_t, [c_int]),

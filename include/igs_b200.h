@@ -174,6 +174,43 @@ int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin,
                                    const float *colors, const float *v_output_band, const uint16_t *tile_topk, float *v_xy, float *v_conic,
                                    float *v_colors, void *stream);
 
+/* ---- the bands' gradient exchange over peer memory (NVLink / NVSwitch; one process per GPU of one machine; no counterpart in the
+ * reference) ------------------------------------------------------------------------------------------------------------------------ */
+
+#define IGS_MAX_BAND_RANKS 8
+#define IGS_IPC_HANDLE_BYTES 64
+#define IGS_BAND_SYNC_WORDS 32     /* uint32 words of a rank's synchronisation block (igs_band_sync_bytes) */
+#define IGS_BAND_SYNC_STEP 16      /* word index: exchanges this rank has completed */
+#define IGS_BAND_SYNC_ERROR 17     /* word index: nonzero once a wait gave up (IGS_BAND_TIMEOUT_* bits); later exchanges do nothing */
+#define IGS_BAND_TIMEOUT_READY 1u  /* a rank's partials did not arrive in time */
+#define IGS_BAND_TIMEOUT_DONE 2u   /* a rank's share of the results did not arrive in time */
+
+/* A CUDA IPC handle (IGS_IPC_HANDLE_BYTES bytes) for the device allocation that holds dev_ptr, and dev_ptr's offset in it: an allocation
+ * is exported whole, so any buffer inside one (a tensor of a caching allocator) can be shared. */
+int igs_ipc_export(const void *dev_ptr, void *handle, uint64_t *offset);
+/* Map another process's buffer (igs_ipc_export's handle and offset) on the current device, with peer access; *dev_ptr is the buffer's
+ * address here. Opening an allocation again returns the same mapping (reference-counted by CUDA); igs_ipc_close undoes one open. */
+int igs_ipc_open(const void *handle, uint64_t offset, void **dev_ptr);
+int igs_ipc_close(void *dev_ptr, uint64_t offset);
+
+/* Bytes of a rank's synchronisation block (zero it once before the first exchange; 16-byte aligned) and floats of its results buffer:
+ * v_cov2d [N,3], v_mean2d [N,2], v_scale [N,2], v_rot [N], v_colors [N,C] (summed over the bands), loss [1]. */
+size_t igs_band_sync_bytes(void);
+size_t igs_band_results_floats(int num_points, int channels);
+
+/* The exchange that ends a band step, after igs_raster_step_l1_band (or the band's forward and backward) on every rank, in place of an
+ * all-reduce of the partials followed by igs_project_bwd on every rank. partials[q] is rank q's [N (5 + C) + 1] buffer (v_xy, v_conic,
+ * v_colors, loss: what the band kernels wrote), results[q] its results buffer, sync[q] its synchronisation block; entry `rank` is this
+ * rank's own memory, the others are peers' buffers mapped with igs_ipc_open (world <= IGS_MAX_BAND_RANKS). This rank announces that its
+ * partials are complete, waits for every rank's, sums the partials of its share of the Gaussians [N rank / world, N (rank + 1) / world)
+ * in rank order, runs the projection backward on them (igs_project_bwd's arithmetic) and stores the results into every rank's results
+ * buffer, adds the partial losses into its own, then announces and waits until every rank has stored its share. Every rank then holds
+ * the same complete results. A wait longer than timeout_ms sets bits in the rank's error word (IGS_BAND_SYNC_ERROR) instead of hanging
+ * the GPU; that step's results are invalid and later exchanges do nothing. Each rank's call must be on its own GPU. */
+int igs_band_reduce(int world, int rank, int num_points, int channels, const float *const *partials, float *const *results,
+                    void *const *sync, const float *scales2d, const float *rotation, int img_height, int img_width, const int32_t *radii,
+                    const float *conics, int timeout_ms, void *stream);
+
 /* topk_norm_loo_loss_increase (bindings.cu:895-936, kernel forward.cu:667-738): per Gaussian, the increase of the absolute (squared
  * when `squared`) error summed over pixels and channels when it alone leaves the top-K lists; targets [C,H,W]. IDs of N or more count
  * as empty slots. */

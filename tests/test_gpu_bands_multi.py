@@ -1,8 +1,9 @@
 """
-Tile-row bands across two GPUs over NCCL (one process per GPU, 127.0.0.1 rendezvous): each rank bins, renders and back-propagates its
-band, the partial gradients and loss are summed with one NCCL all-reduce, and every rank finishes the projection backward. Every rank's
-parameter gradients and loss must equal the single-GPU step's on the same inputs, both for eager launches and for the CUDA-graph replay.
-Skipped with fewer than two GPUs.
+Tile-row bands across two GPUs (one process per GPU, 127.0.0.1 rendezvous, NVLS off): each rank bins, renders and back-propagates its
+band; the partial gradients and loss are combined either by one NCCL all-reduce followed by the projection backward on every rank, or by
+the peer-memory exchange (igs_band_reduce over CUDA IPC mappings, plain peer loads and stores). Every rank's parameter gradients and loss
+must equal the single-GPU step's on the same inputs, for eager launches and for the CUDA-graph replay; with the peer exchange every rank
+must hold bit-identical gradients. Skipped with fewer than two GPUs.
 """
 import datetime
 import os
@@ -24,7 +25,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def band_rank(rank, port):
+def band_rank(rank, port, exchange):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -44,20 +45,29 @@ def band_rank(rank, port):
         full.launch()
         r0, r1 = bands.band_rows_balanced(d["means"], d["scales"], d["rotations"], h, w, WORLD, rank)
         step = bands.BandStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], h, w, r0, r1, group=dist.group.WORLD,
-                              capacity=full.capacity)
+                              capacity=full.capacity, exchange=exchange)
+        assert step.exchange == exchange
         for mode in ("launch", "replay", "replay"):
             getattr(step, mode)()
             torch.cuda.synchronize()
+            step.check()
             for key in ("v_colors", "v_mean2d", "v_scale", "v_rot"):
                 assert_close_grad(getattr(step, key), getattr(full, key), what=f"{key} ({mode})")
             assert abs(float(step.loss) - float(full.loss)) <= 1e-5 * float(full.loss)
+            mine = torch.cat([getattr(step, k).reshape(-1) for k in ("v_colors", "v_mean2d", "v_scale", "v_rot", "v_cov2d")])
+            gathered = [torch.empty_like(mine) for _ in range(WORLD)]
+            dist.all_gather(gathered, mine)
+            assert all(torch.equal(g, gathered[0]) for g in gathered)
+        if exchange == "peer":
+            assert step.peer.steps() == 3
         step.release()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.timeout(300)
-def test_bands_over_nccl_match_single_gpu():
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_bands_on_two_gpus_match_single_gpu(exchange):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
-    mp.spawn(band_rank, args=(free_port(),), nprocs=WORLD, join=True)
+    mp.spawn(band_rank, args=(free_port(), exchange), nprocs=WORLD, join=True)
