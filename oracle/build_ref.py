@@ -70,35 +70,48 @@ def load_module():
 
 
 PREDICTION = "igs_prediction"
+RANS = "igs_rans"
+# the reference's two pybind11 modules of compress/csrc (compress/csrc/setup.py:22-28): module name -> source file
+CPP_MODULES = {PREDICTION: "prediction.cpp", RANS: "rans.cpp"}
+
+
+def cpp_module_path(name):
+    """Path of one of the reference's C++ modules built into oracle/_ref, or None."""
+    hits = glob.glob(os.path.join(OUT, name + "*.so"))
+    return hits[0] if hits else None
 
 
 def prediction_module_path():
     """Path of the reference's C++ prediction module built into oracle/_ref, or None."""
-    hits = glob.glob(os.path.join(OUT, PREDICTION + "*.so"))
-    return hits[0] if hits else None
+    return cpp_module_path(PREDICTION)
 
 
-def build_prediction(root=None):
-    """Compiles the reference's compress/csrc/prediction.cpp (its neighbour search and predictor; a pybind11 module) where it lies, with
-    g++ (-O3 -ffp-contract=off -pthread, and the source hash define that compress/common.py:13-27 checks), into oracle/_ref/. It is the
-    CPU baseline and checker of the GPU neighbour search."""
+def build_cpp_module(name, root=None):
+    """Compiles one of the reference's compress/csrc modules where it lies, with g++ and compress/csrc/setup.py's flags (-O3
+    -ffp-contract=off -pthread, and the source hash define that compress/common.py:13-27 checks), into oracle/_ref/: igs_prediction (its
+    neighbour search and predictor: the CPU baseline and checker of the GPU neighbour search) and igs_rans (its rANS coder, which
+    compress/__init__.py imports, so that the reference's model.py can be imported here)."""
     import hashlib
     import subprocess
     import sysconfig
 
     from torch.utils.cpp_extension import include_paths
 
-    src = os.path.join(reference_root(root), "compress", "csrc", "prediction.cpp")
+    src = os.path.join(reference_root(root), "compress", "csrc", CPP_MODULES[name])
     if not os.path.exists(src):
         raise FileNotFoundError(src)
     os.makedirs(OUT, exist_ok=True)
     with open(src, "rb") as f:
         digest = hashlib.sha256(f.read()).hexdigest()[:16]
-    out = os.path.join(OUT, PREDICTION + sysconfig.get_config_var("EXT_SUFFIX"))
+    out = os.path.join(OUT, name + sysconfig.get_config_var("EXT_SUFFIX"))
     gxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
     subprocess.run([gxx, "-O3", "-std=c++17", "-shared", "-fPIC", "-pthread", "-ffp-contract=off", f'-DSOURCE_HASH="{digest}"', "-I",
                     include_paths()[0], "-I", sysconfig.get_paths()["include"], src, "-o", out], check=True)
     return out
+
+
+def build_prediction(root=None):
+    return build_cpp_module(PREDICTION, root)
 
 
 def load_prediction():
@@ -117,4 +130,5 @@ def load_prediction():
 if __name__ == "__main__":
     root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
     print(build(root, verbose=True))
-    print(build_prediction(root))
+    for name in CPP_MODULES:
+        print(build_cpp_module(name, root))
