@@ -330,19 +330,27 @@ def run_ours(args, wl):
 
     # the 2160p image split into tile-row bands over the same ranks (strong scaling; at N=1 the whole image on one GPU, the reference
     # point of the scaling), reported beside the independent-image line
-    bands_leg = None
+    bands_leg = bands_leg_other = None
     if not args.no_bands and wl.name == "cfg3_1080p":
         del graph, step
         torch.cuda.empty_cache()
-        try:
-            b = measure_bands(args, workloads.get_workload("cfg4_2160p"), world, rank, local, exchange=args.exchange,
-                              steps=min(args.steps, 50), e2e=False, cpu=False, stages=False)
-            if rank == 0:
-                bands_leg = {k: b[k] for k in ("value", "unit", "n_gpus", "ms_per_step", "scaling", "exchange", "exchange_ms",
-                                                "band_ms_per_rank", "band_intersections", "gaussian_pixel_evals_per_s", "clocks")}
-                bands_leg["config"] = b["config"]
-        except Exception as err:  # the band leg is reported beside the main line; its failure must not lose the main measurement
-            bands_leg = {"error": f"{type(err).__name__}: {err}"[:500]}
+        # with several GPUs both exchanges are measured: the peer-memory exchange (the default) and NCCL's all-reduce
+        exchanges = [args.exchange] + ([x for x in ("peer", "nccl") if x != args.exchange] if world > 1 else [])
+        for ex in exchanges:
+            try:
+                b = measure_bands(args, workloads.get_workload("cfg4_2160p"), world, rank, local, exchange=ex, steps=min(args.steps, 50),
+                                  e2e=False, cpu=False, stages=False)
+                leg = None
+                if rank == 0:
+                    leg = {k: b[k] for k in ("value", "unit", "n_gpus", "ms_per_step", "scaling", "exchange", "exchange_ms",
+                                             "band_ms_per_rank", "band_intersections", "gaussian_pixel_evals_per_s", "clocks")}
+                    leg["config"] = b["config"]
+            except Exception as err:  # the band leg is reported beside the main line; its failure must not lose the main measurement
+                leg = {"error": f"{type(err).__name__}: {err}"[:500]}
+            if ex == args.exchange:
+                bands_leg = leg
+            else:
+                bands_leg_other = leg
 
     if rank == 0:
         clk = clocks.summary()
@@ -360,6 +368,7 @@ def run_ours(args, wl):
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
             "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph, "cpu_baseline": cpu,
             "gpu_launches": kernels_per_step * args.steps, "clocks": clk, "bands_2160p": bands_leg,
+            "bands_2160p_other_exchange": bands_leg_other,
         }
         print(json.dumps(out))
     if world > 1:
@@ -427,20 +436,21 @@ def measure_bands(args, wl, world, rank, local, exchange="peer", steps=None, e2e
         del g
     xchg_ms = 0.0
     if world > 1:
+        # the exchange alone: with the peer exchange, its two kernels as a CUDA graph (captured on every rank) replayed back to back;
+        # with NCCL, the all-reduce and the projection backward's graph
+        xgraph = step._capture(step.FINAL)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
         a.record()
         for _ in range(20):
-            if step.exchange == "peer":
-                step._exchange()
-            else:
-                step.all_reduce()
-                step._project_backward()
+            step.all_reduce()
+            xgraph.replay()
         b.record()
         torch.cuda.synchronize()
         step.check()
         xchg_ms = a.elapsed_time(b) / 20
+        del xgraph
     per_rank = torch.tensor([local_ms, float(r0), float(r1), float(band_isect)], device=device, dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)

@@ -11,10 +11,10 @@
 // Per rank and step this moves (world - 1) / world of the partials in and of the results out over NVLink, with two rank-wide waits. The
 // sums are formed by one rank each in a fixed order, so every rank holds bit-identical gradients.
 //
-// Synchronisation words (per rank, in its exchange buffer, written by the peers with release stores at system scope and read with acquire
-// loads): ready[q] and done[q] hold the last step for which rank q announced; step counts this rank's completed exchanges. Every wait
-// polls with a deadline (%globaltimer) and, past it, records IGS_BAND_TIMEOUT_* in the rank's error word and returns without touching
-// peer data, so a missing rank makes the step fail instead of hanging the GPU. The ranks' kernels never wait on one another on one GPU:
+// Synchronisation words (per rank, in its exchange buffer, written by the peers with relaxed stores at system scope, polled with relaxed
+// loads and read once more with acquire loads): ready[q] and done[q] hold the last step for which rank q announced; step counts this
+// rank's completed exchanges. Every wait polls with a deadline (%globaltimer) and, past it, records IGS_BAND_TIMEOUT_* in the rank's
+// error word and returns without touching peer data, so a missing rank makes the step fail instead of hanging the GPU. The ranks' kernels never wait on one another on one GPU:
 // each rank is its own GPU.
 //
 // The buffers are exported and mapped with CUDA IPC (igs_ipc_export / igs_ipc_open): an allocation is exported whole, so the offset of
@@ -48,9 +48,10 @@ struct Peers {
     SyncWords *sync[kMaxRanks];
 };
 
-__device__ __forceinline__ void store_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+// Synchronisation with the other ranks: relaxed stores of the flags, relaxed polling, then one acquire load per flag; the stores a flag
+// announces are fenced (release, system scope) by the blocks that made them. System-scope fences cost microseconds each, so the protocol
+// has one per block of band_reduce_kernel and none in the waits.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ unsigned load_acquire_sys(const unsigned *p) {
     unsigned v;
@@ -58,10 +59,26 @@ __device__ __forceinline__ unsigned load_acquire_sys(const unsigned *p) {
     return v;
 }
 
-// a peer's value, fetched from its memory (no stale line from an earlier step in this SM's L1)
+__device__ __forceinline__ void store_relaxed_sys(unsigned *p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned load_relaxed_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// a peer's values, fetched from its memory (no stale line from an earlier step in this SM's L1)
 __device__ __forceinline__ float load_peer(const float *p) {
     float v;
-    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float2 load_peer2(const float *p) {
+    float2 v;
+    asm volatile("ld.volatile.global.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
     return v;
 }
 
@@ -75,24 +92,27 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // words reaches `value`. One thread. Returns false (and records `code` in the error word) past the deadline.
 __device__ bool announce_and_wait(const Peers &peers, const int world, const int rank, const bool done_words, const unsigned value,
                                   const unsigned long long timeout_ns, const unsigned code) {
-    __threadfence_system();
+    // No fence before the flags: what they announce was written by kernels that have completed (the band's raster step before
+    // band_reduce_kernel; band_reduce_kernel, whose blocks each end with a release fence, before band_done_kernel)
     for (int q = 0; q < world; ++q) {
         SyncWords *w = peers.sync[q];
-        store_release_sys(done_words ? &w->done[rank] : &w->ready[rank], value);
+        store_relaxed_sys(done_words ? &w->done[rank] : &w->ready[rank], value);
     }
     SyncWords *me = peers.sync[rank];
     const unsigned *words = done_words ? me->done : me->ready;
     const unsigned long long deadline = global_ns() + timeout_ns;
     for (int q = 0; q < world; ++q) {
         // the counters only grow; a difference of at most 2^31 compares steps across a wrap of the 32-bit count
-        while ((int)(load_acquire_sys(&words[q]) - value) < 0) {
+        while ((int)(load_relaxed_sys(&words[q]) - value) < 0) {
             if (global_ns() > deadline) {
                 atomicOr(&me->error, code);
                 return false;
             }
-            __nanosleep(128);
+            __nanosleep(64);
         }
     }
+    // acquire: the data each rank wrote before its flag is read after it
+    for (int q = 0; q < world; ++q) (void)load_acquire_sys(&words[q]);
     return true;
 }
 
@@ -103,11 +123,42 @@ struct ResultsLayout {
         : cov(0), mean(3 * n), scale(5 * n), rot(7 * n), colors(8 * n), loss((8 + (size_t)c) * n) {}
 };
 
+// One Gaussian's partials from kGroup ranks, every load issued before the first addition (peer loads take an NVLink round trip each)
+template <int kMaxC, int kGroup>
+__device__ __forceinline__ void add_partials(const Peers &peers, const int q0, const int world, const size_t nn, const int g,
+                                             const int channels, float (&vxy)[2], float (&vcon)[3], float (&vcol)[kMaxC]) {
+    float t[kGroup][5 + kMaxC];
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j) {
+        if (q0 + j >= world) continue;
+        const float *p = peers.partials[q0 + j];
+        const float2 xy = load_peer2(p + 2 * (size_t)g);
+        t[j][0] = xy.x;
+        t[j][1] = xy.y;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) t[j][2 + k] = load_peer(p + 2 * nn + 3 * (size_t)g + k);
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) t[j][5 + c] = c < channels ? load_peer(p + 5 * nn + (size_t)g * channels + c) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j) {
+        if (q0 + j >= world) continue;
+        vxy[0] += t[j][0];
+        vxy[1] += t[j][1];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) vcon[k] += t[j][2 + k];
+#pragma unroll
+        for (int c = 0; c < kMaxC; ++c) vcol[c] += t[j][5 + c];
+    }
+}
+
+template <int kMaxC>
 __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers, const int world, const int rank, const int n,
                                                                const int channels, const int share_begin, const int share_end,
                                                                const float2 *__restrict__ scales, const float *__restrict__ rotations,
                                                                const float img_w, const float img_h, const int *__restrict__ radii,
                                                                const float *__restrict__ conics, const unsigned long long timeout_ns) {
+    constexpr int kGroup = kMaxC <= 4 ? kMaxRanks : 2;  // ranks whose loads are in flight together (registers: kGroup (5 + kMaxC))
     igs::wait_for_predecessor();  // this rank's partials are complete (the band's raster step ran before this kernel)
     __shared__ int s_go;
     SyncWords *me = peers.sync[rank];
@@ -123,19 +174,11 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
     const ResultsLayout out(nn, channels);
     const int g = share_begin + blockIdx.x * kThreads + threadIdx.x;
     if (g < share_end) {
-        float vxy[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[igs::kMaxChannels];
+        // the sums in rank order (the same on every rank: each Gaussian is summed by one rank only)
+        float vxy[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[kMaxC];
 #pragma unroll
-        for (int c = 0; c < igs::kMaxChannels; ++c) vcol[c] = 0.f;
-        for (int q = 0; q < world; ++q) {
-            const float *p = peers.partials[q];
-            vxy[0] += load_peer(p + 2 * (size_t)g);
-            vxy[1] += load_peer(p + 2 * (size_t)g + 1);
-#pragma unroll
-            for (int k = 0; k < 3; ++k) vcon[k] += load_peer(p + 2 * nn + 3 * (size_t)g + k);
-#pragma unroll
-            for (int c = 0; c < igs::kMaxChannels; ++c)
-                if (c < channels) vcol[c] += load_peer(p + 5 * nn + (size_t)g * channels + c);
-        }
+        for (int c = 0; c < kMaxC; ++c) vcol[c] = 0.f;
+        for (int q0 = 0; q0 < world; q0 += kGroup) add_partials<kMaxC, kGroup>(peers, q0, world, nn, g, channels, vxy, vcon, vcol);
         igs::ProjectionGrad pg;
         if (__ldg(&radii[g]) > 0) {
             pg = igs::projection_grad(__ldg(&scales[g]), __ldg(&rotations[g]), img_w, img_h, conics + 3 * (size_t)g, vcon,
@@ -155,7 +198,7 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
             r[out.scale + 2 * (size_t)g + 1] = pg.scale.y;
             r[out.rot + g] = pg.rot;
 #pragma unroll
-            for (int c = 0; c < igs::kMaxChannels; ++c)
+            for (int c = 0; c < kMaxC; ++c)
                 if (c < channels) r[out.colors + (size_t)g * channels + c] = vcol[c];
         }
     }
@@ -165,7 +208,10 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
         for (int q = 0; q < world; ++q) loss += load_peer(peers.partials[q] + (5 + (size_t)channels) * nn);
         peers.results[rank][out.loss] = loss;
     }
-    __threadfence_system();  // this thread's peer stores are visible before the done announcement (band_done_kernel, next)
+    // the block's peer stores are performed at system scope before it ends, so before the done announcement (band_done_kernel, next):
+    // the barrier orders every thread's stores before thread 0's fence, which is cumulative over them
+    __syncthreads();
+    if (threadIdx.x == 0) fence_acq_rel_sys();
 }
 
 __global__ void __launch_bounds__(32) band_done_kernel(const Peers peers, const int world, const int rank,
@@ -262,7 +308,8 @@ int igs_band_reduce(int world, int rank, int num_points, int channels, const flo
     const int blocks = std::max(1, igs::ceil_div(share_end - share_begin, kThreads));
     const unsigned long long timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
     cudaStream_t s = igs::as_stream(stream);
-    igs::launch(band_reduce_kernel, blocks, kThreads, 0, s, peers, world, rank, num_points, channels, share_begin, share_end,
+    const auto kernel = channels <= 4 ? band_reduce_kernel<4> : band_reduce_kernel<igs::kMaxChannels>;
+    igs::launch(kernel, blocks, kThreads, 0, s, peers, world, rank, num_points, channels, share_begin, share_end,
                 reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width, (float)img_height, radii, conics, timeout_ns);
     igs::launch(band_done_kernel, 1, 32, 0, s, peers, world, rank, timeout_ns);
     return igs::check_launch(who);
