@@ -301,7 +301,7 @@ def run_ours(args, wl):
 
     # per-stage breakdown and the dominant kernel's roofline (graphs of single stages, same flush discipline)
     stage_ms = {}
-    for s in step.STAGES if not args.no_stages else ():
+    for s in step.BREAKDOWN_STAGES if not args.no_stages else ():
         g = step.capture([s])
         stage_ms[s.strip("_")] = time_graph(g, max(5, min(50, args.steps)), flush)
         del g

@@ -16,6 +16,7 @@
 #include <algorithm>
 
 #include "igs_common.cuh"
+#include "igs_internal.cuh"
 
 namespace {
 
@@ -135,12 +136,15 @@ __global__ void __launch_bounds__(kCumThreads) cumsum_partials_kernel(const int 
     if (threadIdx.x == 0) partials[blockIdx.x] = t;
 }
 
+// partials: one sum per partials_per_block-th of a block of kCumBlock elements (1: cumsum_partials_kernel's; kCumBlock / 256: the
+// training step's projection kernel's sums per 256 Gaussians)
 __global__ void __launch_bounds__(kCumThreads) cumsum_scan_kernel(const int n, const int *__restrict__ in, const unsigned *__restrict__ partials,
-                                                                  int *__restrict__ out, int *__restrict__ total_out) {
+                                                                  const int partials_per_block, int *__restrict__ out,
+                                                                  int *__restrict__ total_out) {
     igs::wait_for_predecessor();
     __shared__ unsigned scratch[kCumThreads / 32];
     unsigned before = 0u;
-    for (int b = threadIdx.x; b < (int)blockIdx.x; b += kCumThreads) before += partials[b];
+    for (int b = threadIdx.x; b < (int)blockIdx.x * partials_per_block; b += kCumThreads) before += partials[b];
     before = block_sum_u32(before, scratch);
     const int first = blockIdx.x * kCumBlock + threadIdx.x * kCumItems;
     unsigned v[kCumItems], run = 0u;
@@ -338,7 +342,7 @@ int igs_cumsum(int n, const int32_t *num_tiles_hit, int32_t *cum_tiles_hit, int3
     const int blocks = igs::ceil_div(n, kCumBlock);
     unsigned *partials = static_cast<unsigned *>(workspace);
     igs::launch(cumsum_partials_kernel, blocks, kCumThreads, 0, s, n, num_tiles_hit, partials);
-    igs::launch(cumsum_scan_kernel, blocks, kCumThreads, 0, s, n, num_tiles_hit, partials, cum_tiles_hit, total);
+    igs::launch(cumsum_scan_kernel, blocks, kCumThreads, 0, s, n, num_tiles_hit, partials, 1, cum_tiles_hit, total);
     return igs::check_launch("igs_cumsum");
 }
 
@@ -346,7 +350,7 @@ size_t igs_sort_workspace(int capacity, int tiles_x, int tiles_y) { return sort_
 
 static int sort_band(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit, int tiles_x,
                      int tiles_y, int row_begin, int row_end, int32_t *gaussian_ids_sorted, int32_t *tile_bins, void *workspace,
-                     size_t workspace_bytes, void *stream, const char *who) {
+                     size_t workspace_bytes, void *stream, const char *who, bool counters_zeroed = false) {
     IGS_REQUIRE(num_points >= 0 && tiles_x >= 0 && tiles_y >= 0, "%s: negative size", who);
     IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
                 row_end, tiles_y);
@@ -377,7 +381,7 @@ static int sort_band(int num_points, int capacity, const float *xys, const int32
     ws += round256(sizeof(int) * (size_t)capacity);
     int *unsorted = reinterpret_cast<int *>(ws);
 
-    if (cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch(who);
+    if (!counters_zeroed && cudaMemsetAsync(tile_count, 0, sizeof(int) * (size_t)num_tiles, s) != cudaSuccess) return igs::check_launch(who);
     // slots are bounded by the capacity; a grid-stride loop over them reads the true count on the device
     const int slot_blocks = std::min(igs::ceil_div(capacity, 256), 148 * 16);
     if (num_points > 0) {
@@ -424,6 +428,29 @@ int igs_sort_intersects_band(int num_points, int capacity, const float *xys, con
 }
 
 }  // extern "C"
+
+namespace igs {
+
+int cumsum_from_block_sums(int n, const int32_t *tiles_hit, const unsigned *block_sums, int32_t *cum, int32_t *total, cudaStream_t s) {
+    static_assert(kCumBlock % 256 == 0, "block sums of 256 elements");
+    if (n == 0) {
+        if (total && cudaMemsetAsync(total, 0, sizeof(int), s) != cudaSuccess) return check_launch("prefix sum (training step)");
+        return IGS_OK;
+    }
+    launch(cumsum_scan_kernel, ceil_div(n, kCumBlock), kCumThreads, 0, s, n, tiles_hit, block_sums, kCumBlock / 256, cum, total);
+    return check_launch("prefix sum (training step)");
+}
+
+int sort_band_counters_zeroed(int num_points, int capacity, const float *xys, const int32_t *radii, const int32_t *cum_tiles_hit,
+                              int tiles_x, int tiles_y, int row_begin, int row_end, int32_t *gaussian_ids_sorted, int32_t *tile_bins,
+                              void *workspace, size_t workspace_bytes, cudaStream_t s) {
+    return sort_band(num_points, capacity, xys, radii, cum_tiles_hit, tiles_x, tiles_y, row_begin, row_end, gaussian_ids_sorted, tile_bins,
+                     workspace, workspace_bytes, s, "binning (training step)", true);
+}
+
+int *tile_counters(void *sort_workspace) { return static_cast<int *>(sort_workspace); }
+
+}  // namespace igs
 
 // ---- tile binning without device allocation -------------------------------------------------------------------------------------------
 //

@@ -31,6 +31,7 @@
 #include <cstddef>
 
 #include "igs_common.cuh"
+#include "igs_internal.cuh"
 
 namespace {
 
@@ -1235,7 +1236,8 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
 int raster_step(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, int num_points,
                 const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics, const float *colors,
                 const float *target, float ratio, float *out_img, float *loss, float *v_output, float *v_xy, float *v_conic, float *v_colors,
-                void *workspace, size_t workspace_bytes, void *stream, const char *who) {
+                void *workspace, size_t workspace_bytes, void *stream, const char *who, bool gradients_zeroed = false,
+                bool finish_loss = true) {
     IGS_REQUIRE(tiles_x >= 0 && tiles_y >= 0 && img_h >= 0 && img_w >= 0 && num_points >= 0, "%s: negative size", who);
     IGS_REQUIRE(channels >= 1 && channels <= kMaxChannels, "%s: 1 to %d channels (got %d)", who, kMaxChannels, channels);
     IGS_REQUIRE(tiles_x == igs::ceil_div(img_w, kTile) && tiles_y == igs::ceil_div(img_h, kTile),
@@ -1243,12 +1245,13 @@ int raster_step(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, i
     IGS_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= tiles_y, "%s: tile rows [%d, %d) outside [0, %d)", who, row_begin,
                 row_end, tiles_y);
     const int tiles = tiles_x * (row_end - row_begin);
-    IGS_REQUIRE(loss != nullptr, "%s: null loss", who);
+    IGS_REQUIRE(loss != nullptr || !finish_loss, "%s: null loss", who);
     IGS_REQUIRE(num_points == 0 || (v_xy && v_conic && v_colors), "%s: null gradient pointer", who);
     cudaStream_t s = igs::as_stream(stream);
-    if (num_points > 0 && zero_gradients(num_points, channels, v_xy, v_conic, v_colors, s) != cudaSuccess) return igs::check_launch(who);
+    if (num_points > 0 && !gradients_zeroed && zero_gradients(num_points, channels, v_xy, v_conic, v_colors, s) != cudaSuccess)
+        return igs::check_launch(who);
     if (tiles == 0) {  // no pixels (an empty band): no loss, zero gradients
-        if (cudaMemsetAsync(loss, 0, sizeof(float), s) != cudaSuccess) return igs::check_launch(who);
+        if (finish_loss && cudaMemsetAsync(loss, 0, sizeof(float), s) != cudaSuccess) return igs::check_launch(who);
         return IGS_OK;
     }
     IGS_REQUIRE(tile_bins && target && out_img && workspace, "%s: null pointer", who);
@@ -1273,7 +1276,7 @@ int raster_step(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, i
                                    reinterpret_cast<const int2 *>(tile_bins), reinterpret_cast<const float2 *>(xys), conics, colors, l1,
                                    out_img, v_xy, v_conic, v_colors, s);
     if (err != cudaSuccess) return igs::set_error(IGS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
-    igs::launch(l1_finish_kernel, 1, kFinishThreads, 0, s, l1.partials, tiles, ratio, numel, loss);
+    if (finish_loss) igs::launch(l1_finish_kernel, 1, kFinishThreads, 0, s, l1.partials, tiles, ratio, numel, loss);
     return igs::check_launch(who);
 }
 
@@ -1391,3 +1394,17 @@ int igs_raster_step_l1(int tiles_x, int tiles_y, int img_height, int img_width, 
 }
 
 }  // extern "C"
+
+namespace igs {
+
+int raster_step_fused(int tiles_x, int tiles_y, int img_h, int img_w, int row_begin, int row_end, int channels, int num_points,
+                      const int32_t *ids_sorted, const int32_t *tile_bins, const float *xys, const float *conics, const float *colors,
+                      const float *target, float ratio, float *out_img, float *loss, float *v_xy, float *v_conic, float *v_colors,
+                      void *workspace, size_t workspace_bytes, bool finish_loss, cudaStream_t s) {
+    return raster_step(tiles_x, tiles_y, img_h, img_w, row_begin, row_end, channels, num_points, ids_sorted, tile_bins, xys, conics, colors,
+                       target, ratio, out_img, loss, nullptr, v_xy, v_conic, v_colors, workspace, workspace_bytes, s, "raster (training step)",
+                       true, finish_loss);
+}
+
+}  // namespace igs
+

@@ -36,6 +36,8 @@ SIGNATURES = {
                                    P]),
     "igs_raster_step_l1_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P,
                                         P, P, P, P, c_size_t, P]),
+    "igs_train_step_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "igs_train_step_l1": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_int, c_int, c_int, c_int, c_int] + [P] * 18 + [c_size_t, P]),
     "igs_band_tiles_hit": (c_int, [c_int, P, P, c_int, c_int, c_int, c_int, P, P]),
     "igs_sort_intersects_band": (c_int, [c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, P, P, P, c_size_t, P]),
     "igs_raster_fwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P]),

@@ -229,6 +229,9 @@ class BandStep:
         self.sort_ws = torch.empty(self.sort_ws_bytes, device=dev, dtype=torch.uint8)
         self.max_list = min(self.n, self.capacity)
         self.topk = None if fused else torch.empty(max(1, self.num_tiles), TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        # the fused band step's workspace (igs_train_step_l1 over the band's rows, without the projection backward)
+        self.step_ws_bytes = self.lib.igs_train_step_workspace(n, self.capacity, self.tb[0], self.r1 - self.r0)
+        self.step_ws = torch.empty(self.step_ws_bytes, device=dev, dtype=torch.uint8) if fused else None
         self.local_graph = self.final_graph = None
 
     def _stream(self):
@@ -278,15 +281,26 @@ class BandStep:
                                             ptr(self.p_xy), ptr(self.p_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                             ptr(self.v_rot), self._stream()), "project_backward")
 
+    def _train_step(self):
+        """Projection (tiles hit counted over the band's rows), prefix sum, the band's binning and its fused raster step in one call
+        (igs_train_step_l1 without the projection backward): the band's partials and partial loss."""
+        _lib.check(self.lib.igs_train_step_l1(self.n, self.c, ptr(self.means), ptr(self.scales), ptr(self.rotations), ptr(self.features),
+                                              ptr(self.target), self.l1_ratio, self.h, self.w, self.r0, self.r1, self.capacity,
+                                              ptr(self.xys), ptr(self.radii), ptr(self.conics), ptr(self.band_hits), ptr(self.cum),
+                                              ptr(self.num_intersects), ptr(self.ids), ptr(self.bins), ptr(self.image), ptr(self.p_loss),
+                                              ptr(self.p_xy), ptr(self.p_conic), ptr(self.p_colors), None, None, None, None,
+                                              ptr(self.step_ws), self.step_ws_bytes, self._stream()), "band train step")
+
     def _exchange(self):
         self.peer.reduce(self.scales, self.rotations, self.h, self.w, self.radii, self.conics, self._stream())
 
     KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_raster": 2, "_forward": 2, "_backward": 1, "_project_backward": 1,
-               "_exchange": 2}
+               "_exchange": 2, "_train_step": 8}
 
     @property
     def LOCAL(self):
-        return ("_project", "_cumsum", "_bin") + (("_raster",) if self.fused else ("_forward", "_backward"))
+        """The band's own work: one igs_train_step_l1 call (fused), or the separate forward and backward kernels after the stages."""
+        return ("_train_step",) if self.fused else ("_project", "_cumsum", "_bin", "_forward", "_backward")
 
     @property
     def FINAL(self):

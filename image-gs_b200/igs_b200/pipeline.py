@@ -90,6 +90,9 @@ class RasterStep:
         # top-K lists in the 16-bit tile-list form between the separate kernels (tiles with 65535+ entries are selected again by the
         # backward pass)
         self.topk = None if fused else torch.empty(self.num_tiles, TOP_K, TILE * TILE, device=dev, dtype=torch.int16)
+        # the fused step's workspace (igs_train_step_l1: the stages below in one call, eight kernels, no memset)
+        self.step_ws_bytes = self.lib.igs_train_step_workspace(n, self.capacity, self.tb[0], self.tb[1])
+        self.step_ws = torch.empty(self.step_ws_bytes, device=dev, dtype=torch.uint8) if fused else None
         if self.rate is not None:
             m = self.rate["model"]
             self.rate_loss = torch.empty((), device=dev, dtype=f32)
@@ -182,14 +185,29 @@ class RasterStep:
                                              ptr(self.v_xy), ptr(self.v_conic), ptr(self.v_cov2d), ptr(self.v_mean2d), ptr(self.v_scale),
                                              ptr(self.v_rot), self._stream()), "project_backward")
 
+    def _train_step(self):
+        """Projection, prefix sum, binning, the fused raster step and the projection backward in one call (igs_train_step_l1)."""
+        self._check(self.lib.igs_train_step_l1(self.n, self.c, ptr(self.means), ptr(self.scales), ptr(self.rotations), ptr(self.features),
+                                               ptr(self.target), self.l1_ratio, self.h, self.w, 0, self.tb[1], self.capacity, ptr(self.xys),
+                                               ptr(self.radii), ptr(self.conics), ptr(self.hits), ptr(self.cum), ptr(self.num_intersects),
+                                               ptr(self.ids), ptr(self.bins), ptr(self.image), ptr(self.loss), ptr(self.v_xy),
+                                               ptr(self.v_conic), ptr(self.v_colors), ptr(self.v_cov2d), ptr(self.v_mean2d),
+                                               ptr(self.v_scale), ptr(self.v_rot), ptr(self.step_ws), self.step_ws_bytes, self._stream()),
+                    "train step")
+
     # kernels each stage launches (memsets excluded)
     KERNELS = {"_quantize": 1, "_project": 1, "_cumsum": 2, "_bin": 4, "_raster": 2, "_forward": 2, "_backward": 1, "_project_backward": 1,
-               "_rate_term": 2, "_feature_grads": 1}
+               "_rate_term": 2, "_feature_grads": 1, "_train_step": 8}
+
+    @property
+    def BREAKDOWN_STAGES(self):
+        """The step's stages as separate calls (the fused step's kernels, one stage at a time, for per-stage timing)."""
+        raster = ("_raster",) if self.fused else ("_forward", "_backward")
+        return ("_project", "_cumsum", "_bin") + raster + ("_project_backward",)
 
     @property
     def BASE_STAGES(self):
-        raster = ("_raster",) if self.fused else ("_forward", "_backward")
-        return ("_project", "_cumsum", "_bin") + raster + ("_project_backward",)
+        return ("_train_step",) if self.fused else self.BREAKDOWN_STAGES
 
     @property
     def STAGES(self):

@@ -131,6 +131,25 @@ int igs_raster_bwd_topk_tiles(int img_height, int img_width, int channels, int n
                               const int32_t *tile_bins, const float *xys, const float *conics, const float *colors, const float *v_output,
                               const uint16_t *tile_topk, float *v_xy, float *v_conic, float *v_colors, void *stream);
 
+/* ---- the training step in one call (no counterpart in the reference, whose step is the sequence of the calls above: model.py:956-976,
+ * 1224-1227 with gsplat's operators) --------------------------------------------------------------------------------------------- */
+
+/* Workspace bytes of igs_train_step_l1 for `tile_rows` tile rows (the image's tiles_y, or a band's row_end - row_begin). */
+size_t igs_train_step_workspace(int num_points, int capacity, int tiles_x, int tile_rows);
+/* igs_project_fwd -> igs_cumsum -> igs_sort_intersects -> igs_raster_step_l1 -> igs_project_bwd for the tile rows [row_begin, row_end)
+ * (the whole image: 0, tiles_y), with the stages' memsets and small passes folded into neighbouring kernels (eight kernels, no memset).
+ * target and out_img hold those rows ([C, band rows, W]); tiles_hit counts the tiles of those rows (num_tiles_hit for the whole image);
+ * tile_bins covers the band's tiles. v_xy, v_conic, v_colors are zeroed by the call and receive the band's gradients. With v_cov2d, v_mean2d,
+ * v_scale, v_rot non-NULL the projection backward runs too and *loss is the loss; with them NULL (a band whose partials are then
+ * combined across GPUs, e.g. by igs_band_reduce) *loss is the band's share. Workspace: igs_train_step_workspace, 256-byte aligned.
+ * Outputs equal the per-stage calls' (the loss up to the order of its float sum). */
+int igs_train_step_l1(int num_points, int channels, const float *means2d, const float *scales2d, const float *rotation, const float *colors,
+                      const float *target, float ratio, int img_height, int img_width, int row_begin, int row_end, int capacity,
+                      float *xys, int32_t *radii, float *conics, int32_t *tiles_hit, int32_t *cum_tiles_hit, int32_t *num_intersects,
+                      int32_t *gaussian_ids_sorted, int32_t *tile_bins, float *out_img, float *loss, float *v_xy, float *v_conic,
+                      float *v_colors, float *v_cov2d, float *v_mean2d, float *v_scale, float *v_rot, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
 /* ---- tile-row bands (one image split over several GPUs; no counterpart in the reference, which renders on one GPU) ------------------ */
 
 /* The tiles of rows [row_begin, row_end) that each Gaussian's rectangle covers: the band's num_tiles_hit, to prefix-sum for its binning */

@@ -94,6 +94,13 @@ def oracle_band_step_class():
             self.v_colors.copy_(torch.from_numpy(v_colors))
             self.loss.fill_(self.l1_ratio * float(np.abs(d.astype(np.float64)).sum() / image.size))
 
+        def _train_step(self):
+            # igs_train_step_l1 over the band's rows: the same buffers as the stages one by one
+            self._project()
+            self._cumsum()
+            self._bin()
+            self._raster()
+
         def _project_backward(self):
             v_cov2d, v_mean2d, v_scale, v_rot = cpu.project_bwd(arr(self.scales), arr(self.rotations), self.h, self.w, arr(self.radii),
                                                                 arr(self.conics), arr(self.v_xy), arr(self.v_conic))
