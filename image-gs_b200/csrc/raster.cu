@@ -524,9 +524,28 @@ __device__ __forceinline__ int halving_index(int lane) {
 //
 // The operator's lists hold Gaussian IDs, with no tile list to index, so each warp (an 8x4 patch) walks the union of its pixels' IDs in
 // increasing order (a warp-wide minimum per step); lanes whose pixel holds the current Gaussian contribute their values, the others
-// zeros; the warp sums the 5 + C values with one recursive-halving reduce-scatter and one global atomic per value. Nothing is staged:
-// the few Gaussians of a warp's union are read through the L1 cache.
+// zeros; the warp sums the 5 + C values with one recursive-halving reduce-scatter and one global atomic per value. Each pixel sorts its
+// ten slots by ID once (a 29-comparator network on registers) and keeps them in shared memory, so that at every step of the walk its
+// smallest unconsumed ID is at hand and its slot's values are two loads away, instead of a minimum and a select over ten registers.
+// The few Gaussians of a warp's union are read through the L1 cache.
 constexpr int kNoId = 0x7fffffff;
+
+// A sorting network for 10 keys (29 comparators, depth 8), checked exhaustively on 0/1 inputs
+__device__ __forceinline__ void sort10(int (&key)[kTopK]) {
+    constexpr int kPairs[29][2] = {{4, 9}, {3, 8}, {2, 7}, {1, 6}, {0, 5}, {1, 4}, {6, 9}, {0, 3}, {5, 8}, {0, 2}, {3, 6}, {7, 9},
+                                   {0, 1}, {2, 4}, {5, 7}, {8, 9}, {1, 2}, {4, 6}, {7, 8}, {3, 5}, {2, 5}, {6, 8}, {1, 3}, {4, 7},
+                                   {2, 3}, {6, 7}, {3, 4}, {5, 6}, {4, 5}};
+#pragma unroll
+    for (int c = 0; c < 29; ++c) {
+        const int i = kPairs[c][0], j = kPairs[c][1];
+        const int lo = min(key[i], key[j]), hi = max(key[i], key[j]);
+        key[i] = lo, key[j] = hi;
+    }
+}
+
+// The slot key of the walk: the Gaussian ID above the slot index (4 bits), so that sorting keys orders the slots by ID; IDs below 2^27
+constexpr int kSlotBits = 4;
+constexpr int kMaxWalkId = (1 << (31 - kSlotBits)) - 1;
 
 template <int C, int NV>
 __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
@@ -574,34 +593,44 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
             if (c < channels) s[k] += __ldg(&colors[(size_t)id[k] * channels + c]) * v_out[c];
         shared += -d[k] * inv2 * s[k];
     }
-    float w[kTopK], vsig[kTopK];
+    // the pixel's slots in increasing ID order (empty slots, kNoId, last): keys (ID, slot) sorted in registers and kept in shared memory
+    // with the slots' colour weight and dL/dsigma, so that each step of the walk finds the pixel's smallest unconsumed ID and its values
+    // with a few loads
+    __shared__ int s_key[kTopK][kThreads];
+    __shared__ float s_w[kTopK][kThreads], s_v[kTopK][kThreads];
+    const int tid = threadIdx.x;
+    int key[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        w[k] = d[k] * inv;
-        vsig[k] = -d[k] * (s[k] * inv + shared);
+        key[k] = id[k] == kNoId ? kNoId : (id[k] << kSlotBits) | k;
+        s_w[k][tid] = d[k] * inv;
+        s_v[k][tid] = -d[k] * (s[k] * inv + shared);
     }
+    sort10(key);
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) s_key[k][tid] = key[k];
 
     const int value_index = halving_index<NV>(lane);
     const bool adds = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
     float *const target = value_index < 3 ? v_conic + value_index : value_index < 5 ? v_xy + (value_index - 3) : v_colors + (value_index - 5);
     const int stride = value_index < 3 ? 3 : value_index < 5 ? 2 : channels;
-    while (true) {
-        int head = id[0];
-#pragma unroll
-        for (int k = 1; k < kTopK; ++k) head = min(head, id[k]);
-        const int cur = __reduce_min_sync(0xffffffffu, head);
-        if (cur == kNoId) break;
-        float ws = 0.f, vs = 0.f;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            if (id[k] == cur) {
-                ws = w[k];
-                vs = vsig[k];
-                id[k] = kNoId;
-            }
-        }
+    int pos = 0;
+    int head = key[0];
+    int low = __reduce_min_sync(0xffffffffu, head);
+    while (low != kNoId) {
+        const int cur = low >> kSlotBits;
+        // the Gaussian's parameters are requested first, and the next step's Gaussian is found before this step's sums
         const float2 xy = __ldg(&xys[cur]);
         const float a = __ldg(&conics[3 * cur]), b = __ldg(&conics[3 * cur + 1]), c = __ldg(&conics[3 * cur + 2]);
+        float ws = 0.f, vs = 0.f;
+        if ((head >> kSlotBits) == cur) {
+            const int k = head & ((1 << kSlotBits) - 1);
+            ws = s_w[k][tid];
+            vs = s_v[k][tid];
+            ++pos;
+            head = pos < kTopK ? s_key[pos][tid] : kNoId;
+        }
+        low = __reduce_min_sync(0xffffffffu, head);
         const float dx = xy.x - px, dy = xy.y - py;
         float val[NV];
         val[0] = 0.5f * vs * dx * dx;
@@ -1206,6 +1235,8 @@ int raster_bwd(int img_h, int img_w, int row_begin, int row_end, int channels, i
     if (tiles == 0 || num_points == 0) return IGS_OK;
     IGS_REQUIRE(xys && conics && (colors || channels == 0) && (v_output || channels == 0), "%s: null pointer", who);
     IGS_REQUIRE(pixel_topk || (tile_topk && tile_bins && ids_sorted), "%s: null top-K lists", who);
+    IGS_REQUIRE(pixel_topk == nullptr || num_points <= kMaxWalkId + 1, "%s: at most %d Gaussians with [H, W, 10] lists", who,
+                kMaxWalkId + 1);
     IGS_REQUIRE(igs::aligned(xys, 8), "%s: xys must be 8-byte aligned", who);
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
     const float2 *xy2 = reinterpret_cast<const float2 *>(xys);
