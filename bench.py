@@ -740,7 +740,71 @@ def run_aux(args):
     out["feature_weights_1080p"] = {"gpu_ms": gpu_ms(lambda: ops.topk_feature_weights_fixed(h, w, xys, conics, topk))}
     out["loo_1080p"] = {"gpu_ms": gpu_ms(lambda: ops.topk_norm_loo_loss_increase(h, w, xys, conics, d["features"], topk, d["target"],
                                                                                   False, 1e-4))}
+
+    # the bitstream of those 80,000 Gaussians (positions, scales, rotations, features in bitstream order): the rANS coder's encode
+    # (model search on host threads + one rANS pass) and decode against the reference's C++ coder built from source (oracle/_ref), on
+    # the same streams; and the size estimate of the rate decisions (histograms on the GPU) against the reference's
+    out["bitstream_80k"] = codec_aux(q, inp4, order)
     print(json.dumps(out))
+
+
+def codec_aux(q, inp, order):
+    """Encode / decode / estimate timings of the bitstream's streams of the 2160p/80k workload, ours against the reference's coder."""
+    from igs_b200 import bitstream, codec
+
+    rot = np.round(inp["rotations"].numpy()[:, :1] / (np.pi / 256)).astype(np.int64)
+    scale = np.round(np.log2(np.abs(inp["scales"].numpy())) / 0.03125).astype(np.int64)
+    feat = np.round(inp["features"].numpy() * 64).astype(np.int64)
+    _, _, codes = bitstream.bitstream_order(q, 3)
+    streams = [np.diff(codes, prepend=np.uint64(0)).astype(np.int64)] + [a[order][:, c].copy() for a in (scale, rot, feat)
+                                                                          for c in range(a.shape[1])]
+
+    def wall_ms(fn, reps=5):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            result = fn()
+        return 1e3 * (time.perf_counter() - t0) / reps, result
+
+    class Sink:  # a writer that only counts (the headers are written in Python by both sides)
+        num_bits = 0
+
+        def write(self, *a):
+            pass
+
+        def write_se(self, *a):
+            pass
+
+        def write_ue(self, *a):
+            pass
+
+    entry = {"gaussians": len(q), "streams": len(streams), "threads": len(os.sched_getaffinity(0))}
+    entry["encode_ms"], (payload, _) = wall_ms(lambda: codec.encode_streams([streams], Sink()))
+    entry["estimate_ms_gpu"], est = wall_ms(lambda: codec.estimate_stream_bits(streams))
+    sys.path.insert(0, ROOT)
+    try:
+        from oracle import build_ref
+
+        rans = build_ref.load_cpp_module(build_ref.RANS)
+        entry["reference_encode_ms"], (ref_payload, ref_models) = wall_ms(lambda: rans.encode_streams(streams))
+        entry["identical_payload"] = bytes(ref_payload) == payload
+        models = [(m[3], m[4], m[5], np.asarray(m[6], dtype=np.int64)) for m in ref_models]
+        entry["reference_decode_ms"], _ = wall_ms(lambda: rans.decode_streams(ref_payload, models, len(q)))
+        table = np.zeros((len(streams), codec.MAX_TOKENS), dtype=np.int64)
+        rows = np.zeros((len(streams), codec.MODEL_FIELDS), dtype=np.int64)
+        for k, (sp, msb, mb, cds) in enumerate(models):
+            rows[k, 3:7] = (sp, msb, mb, len(cds))
+            table[k, :len(cds)] = cds
+        buf = np.frombuffer(bytes(ref_payload), dtype=np.uint8).copy()
+        vals = np.zeros((len(streams), len(q)), dtype=np.int64)
+        lib = codec._lib.load()
+        p = lambda a: codec.ctypes.c_void_p(a.ctypes.data)  # noqa: E731
+        entry["decode_ms"], _ = wall_ms(lambda: lib.igs_rans_decode(len(streams), len(q), p(rows), p(table), p(buf), buf.size, p(vals)))
+        entry["reference_estimate_ms"], ref_est = wall_ms(lambda: [rans.estimate_stream_bits(x) for x in streams])
+        entry["identical_estimates"] = bool(np.array_equal(np.array(est), np.array(ref_est)))
+    except ImportError as e:
+        entry["reference_note"] = str(e)
+    return entry
 
 
 def main():

@@ -44,6 +44,11 @@ SIGNATURES = {
     "igs_raster_fwd_topk_tiles_l1_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_float, P, P, P,
                                                   P, P, c_size_t, P]),
     "igs_raster_bwd_topk_tiles_band": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P]),
+    "igs_rans_payload_bound": (c_size_t, [c_int, c_int64]),
+    "igs_rans_encode": (c_int, [c_int, c_int64, P, c_int, P, c_size_t, ctypes.POINTER(c_size_t), P, P, P]),
+    "igs_rans_decode": (c_int, [c_int, c_int64, P, P, P, c_size_t, P]),
+    "igs_estimate_bits_workspace": (c_size_t, [c_int]),
+    "igs_estimate_stream_bits": (c_int, [c_int, c_int64, P, P, P, c_size_t, P]),
     "igs_ipc_export": (c_int, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
     "igs_ipc_open": (c_int, [P, ctypes.c_uint64, ctypes.POINTER(c_void_p)]),
     "igs_ipc_close": (c_int, [P, ctypes.c_uint64]),

@@ -193,6 +193,32 @@ int igs_raster_bwd_topk_tiles_band(int img_height, int img_width, int row_begin,
                                    const float *colors, const float *v_output_band, const uint16_t *tile_topk, float *v_xy, float *v_conic,
                                    float *v_colors, void *stream);
 
+/* ---- entropy coding of the bitstream (compress/rans_codec.py:93-124 over compress/csrc/rans.cpp:330-554; the container of
+ * compress/__init__.py:104-156 is igs_b200/bitstream.py) ------------------------------------------------------------------------- */
+
+#define IGS_RANS_MAX_TOKENS 4608   /* count codes per stream, at most */
+#define IGS_RANS_MODEL_FIELDS 8    /* per stream: delta, zigzag_mapped, param, split_exp, msb_bits, mantissa_bits, number of codes, 0 */
+
+/* Bytes that the payload of num_streams streams of `count` values cannot exceed. */
+size_t igs_rans_payload_bound(int num_streams, int64_t count);
+/* encode_streams: host arrays. streams [num_streams, count] int64; each stream is coded as its values or their differences, shifted to
+ * its minimum or zigzagged around its rounded median, with the token model of the smallest estimated size, all with one rANS state;
+ * the candidates are fitted on num_threads host threads (0: all). Outputs: the payload (little-endian 32-bit words), models
+ * [num_streams, IGS_RANS_MODEL_FIELDS], codes [num_streams, IGS_RANS_MAX_TOKENS] (the first `number of codes` used) and each stream's
+ * estimated payload bits; the bytes equal the reference's. */
+int igs_rans_encode(int num_streams, int64_t count, const int64_t *streams, int num_threads, uint8_t *payload, size_t payload_capacity,
+                    size_t *payload_bytes, int64_t *models, int64_t *codes, double *payload_bits);
+/* decode_streams: host arrays. models and codes as igs_rans_encode writes them (only split_exp, msb_bits, mantissa_bits and the codes
+ * are read: the mapping and differences are undone by the caller); values [num_streams, count] the mapped values. */
+int igs_rans_decode(int num_streams, int64_t count, const int64_t *models, const int64_t *codes, const uint8_t *payload,
+                    size_t payload_size, int64_t *values);
+/* estimate_stream_bits (compress/rans_codec.py:83-90) of num_streams device streams [num_streams, count] int64 into bits [num_streams]
+ * (host): the histograms of their tokens on the GPU, the reference's formula on the host (synchronizes the stream). Workspace:
+ * igs_estimate_bits_workspace bytes, 16-byte aligned. */
+size_t igs_estimate_bits_workspace(int num_streams);
+int igs_estimate_stream_bits(int num_streams, int64_t count, const int64_t *streams, double *bits, void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 /* ---- the bands' gradient exchange over peer memory (NVLink / NVSwitch; one process per GPU of one machine; no counterpart in the
  * reference) ------------------------------------------------------------------------------------------------------------------------ */
 

@@ -114,17 +114,22 @@ def build_prediction(root=None):
     return build_cpp_module(PREDICTION, root)
 
 
-def load_prediction():
-    """Import the built prediction module (raises ImportError when it has not been built)."""
-    path = prediction_module_path()
+def load_cpp_module(name):
+    """Import one of the built C++ modules (raises ImportError when it has not been built)."""
+    path = cpp_module_path(name)
     if path is None:
-        raise ImportError("reference prediction module not built (python oracle/build_ref.py)")
+        raise ImportError(f"reference module {name} not built (python oracle/build_ref.py)")
     import importlib.util
 
-    spec = importlib.util.spec_from_file_location(PREDICTION, path)
+    spec = importlib.util.spec_from_file_location(name, path)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module
+
+
+def load_prediction():
+    """Import the built prediction module (raises ImportError when it has not been built)."""
+    return load_cpp_module(PREDICTION)
 
 
 if __name__ == "__main__":

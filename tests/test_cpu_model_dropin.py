@@ -21,7 +21,7 @@ sys.path.insert(0, ROOT)
 
 from oracle import build_ref  # noqa: E402
 
-CHILD = r'''
+PRELUDE = r'''
 import ast, importlib.abc, importlib.machinery, inspect, json, os, sys, types
 
 root, pkg, ref, out_dir = sys.argv[1:5]
@@ -75,7 +75,9 @@ sys.meta_path.insert(0, _StubFinder())
 
 import gsplat, gsplat.cuda, gsplat.utils  # this repository's package
 assert os.path.realpath(gsplat.__file__).startswith(os.path.realpath(pkg)), gsplat.__file__
+'''
 
+BIND = r'''
 modules = {"model": os.path.join(ref, "model.py"), "compress.rate": os.path.join(ref, "compress", "rate.py"),
            "compress.pruning": os.path.join(ref, "compress", "pruning.py")}
 report = {"resolved": [], "calls": []}
@@ -114,7 +116,7 @@ def test_reference_training_code_binds_to_the_dropin_package():
     import json
 
     ref = build_ref.reference_root()
-    proc = subprocess.run([sys.executable, "-c", CHILD, ROOT, os.path.join(ROOT, "image-gs_b200"), ref, build_ref.OUT],
+    proc = subprocess.run([sys.executable, "-c", PRELUDE + BIND, ROOT, os.path.join(ROOT, "image-gs_b200"), ref, build_ref.OUT],
                           capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert proc.returncode == 0, proc.stderr[-3000:]
     report = json.loads(proc.stdout.strip().splitlines()[-1])
@@ -127,3 +129,44 @@ def test_reference_training_code_binds_to_the_dropin_package():
     for name in ("model.project_gaussians_2d_scale_rot", "model.rasterize_gaussians_sum", "compress.pruning.topk_norm_loo_loss_increase",
                  "compress.rate.rate_loss_forward"):
         assert name in called, (name, sorted(called))
+
+
+CODEC = r'''
+import numpy as np
+
+import compress
+import compress.quantization
+import model
+from igs_b200 import bitstream
+
+originals = {"encode": compress.encode_bitstream, "decode": compress.decode_bitstream}
+replaced = bitstream.install()
+assert model.encode_bitstream is bitstream.encode_bitstream and model.decode_bitstream is bitstream.decode_bitstream
+assert model.bitstream_order is bitstream.bitstream_order and compress.quantization.estimate_bits is bitstream.estimate_bits
+assert compress.encode_bitstream is bitstream.encode_bitstream and compress.estimate_bits is bitstream.estimate_bits
+rng = np.random.default_rng(5)
+n = 700
+attrs = [(rng.integers(0, 4096, (n, 2)), np.full(2, 0.125), np.zeros(2)), (rng.integers(-40, 8, (n, 2)), np.full(2, 0.03125), np.zeros(2)),
+         (rng.integers(-128, 128, (n, 1)), np.full(1, np.float32(np.pi / 256)), np.zeros(1)),
+         (rng.integers(-200, 200, (n, 3)), np.full(3, 1 / 64), np.zeros(3))]
+ours = model.encode_bitstream(attrs, b"meta", channel_refs=[None, None, None, [1, -1, 1]])
+ref = originals["encode"](attrs, b"meta", channel_refs=[None, None, None, [1, -1, 1]])
+assert ours[0] == ref[0] and np.array_equal(ours[1], ref[1]) and ours[2] == ref[2]
+decoded, meta = model.decode_bitstream(ref[0])
+expected, _ = originals["decode"](ours[0])
+assert meta == b"meta" and all(np.array_equal(a[0], b[0]) for a, b in zip(decoded, expected))
+bitstream.restore(replaced)
+assert model.encode_bitstream is originals["encode"]
+print("ok")
+'''
+
+
+@pytest.mark.skipif(not _reference_ready(), reason="the reference tree or its C++ modules (oracle/build_ref.py) are not available")
+def test_reference_codec_calls_route_to_the_library():
+    """bitstream.install() replaces the names model.py and compress/quantization.py bound from compress; a bitstream written through
+    model.encode_bitstream afterwards is byte-identical to the replaced encoder's, and each side decodes the other's."""
+    ref = build_ref.reference_root()
+    proc = subprocess.run([sys.executable, "-c", PRELUDE + CODEC, ROOT, os.path.join(ROOT, "image-gs_b200"), ref, build_ref.OUT],
+                          capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    assert proc.stdout.strip().splitlines()[-1] == "ok"
