@@ -19,6 +19,7 @@
 #include <cmath>
 #include <cstring>
 #include <exception>
+#include <memory>
 #include <thread>
 #include <vector>
 
@@ -155,20 +156,33 @@ double numpy_sum(const double *v, size_t n) {
     return numpy_sum(v, half) + numpy_sum(v + half, n - half);
 }
 
-// the histogram of a coarser tokenizer (split_exp <= fine_split, msb_bits <= fine_msb) from a fine one: every value of a fine token has
-// the same coarse token and raw-bit count, those of the fine token's smallest value. Returns the raw bits.
-int64_t coarsen(const I64 &fine, int fine_split, int fine_msb, int split_exp, int msb_bits, I64 &counts) {
-    counts.clear();
-    int64_t raw_bits = 0;
+// the non-empty tokens of a fine histogram as (smallest value, count), in increasing order
+struct FineBin {
+    int64_t base, count;
+};
+
+std::vector<FineBin> fine_bins(const I64 &fine, int fine_split, int fine_msb) {
+    std::vector<FineBin> bins;
     for (size_t t = 0; t < fine.size(); ++t) {
         if (fine[t] == 0) continue;
         int64_t base;
         int nr;
         token_base((int64_t)t, fine_split, fine_msb, base, nr);
-        const Split sp = split_value(base, split_exp, msb_bits);
-        if (sp.token >= (int64_t)counts.size()) counts.resize(sp.token + 1, 0);
-        counts[sp.token] += fine[t];
-        raw_bits += fine[t] * sp.num_raw;
+        bins.push_back({base, fine[t]});
+    }
+    return bins;
+}
+
+// the histogram of a coarser tokenizer (split_exp <= fine_split, msb_bits <= fine_msb) from a fine one: every value of a fine token has
+// the same coarse token and raw-bit count, those of the fine token's smallest value, and coarse tokens increase with the value, so the
+// last bin gives the histogram's length. Returns the raw bits.
+int64_t coarsen(const std::vector<FineBin> &bins, int split_exp, int msb_bits, I64 &counts) {
+    counts.assign(bins.empty() ? 0 : (size_t)split_value(bins.back().base, split_exp, msb_bits).token + 1, 0);
+    int64_t raw_bits = 0;
+    for (const FineBin &b : bins) {
+        const Split sp = split_value(b.base, split_exp, msb_bits);
+        counts[sp.token] += b.count;
+        raw_bits += b.count * sp.num_raw;
     }
     return raw_bits;
 }
@@ -190,13 +204,14 @@ inline void fine_tokenizer(int64_t vmax, int &split, int &msb) {
 // (the entropy of its token counts plus the smallest header) cannot beat the best so far is skipped, as the reference does.
 TokenModel best_model(const I64 &fine, int fine_split, int fine_msb, int64_t n) {
     const std::vector<double> &len = symbol_bits();
+    const std::vector<FineBin> bins = fine_bins(fine, fine_split, fine_msb);
     TokenModel best;
     bool have = false;
     I64 counts, codes, weights, freqs;
     std::vector<double> terms;
     for (int split = 0; split <= fine_split; ++split) {
         for (int msb = 0; msb <= std::min(split, kMaxMsbBits); ++msb) {
-            const int64_t raw_bits = coarsen(fine, fine_split, fine_msb, split, msb, counts);
+            const int64_t raw_bits = coarsen(bins, split, msb, counts);
             const int64_t header = 4 + 2 + exp_golomb_bits((int64_t)counts.size() - 1) + 2;
             if (have) {
                 terms.clear();
@@ -231,78 +246,162 @@ TokenModel best_model(const I64 &fine, int fine_split, int fine_msb, int64_t n) 
     return best;
 }
 
-// int(np.round(np.median(values))): the middle value, or the mean of the two middle ones, rounded half to even
-int64_t median_rounded(I64 v) {
-    const size_t half = v.size() / 2;
-    std::nth_element(v.begin(), v.begin() + half, v.end());
-    double m = (double)v[half];
-    if (v.size() % 2 == 0) m = ((double)*std::max_element(v.begin(), v.begin() + half) + m) / 2.0;
+// int(np.round(np.median(values))) of the n values value(0) ... value(n - 1), all in [lo, hi]: the middle value, or the mean of the two
+// middle ones, rounded half to even. Exact selection in two passes: a histogram of the values' offsets from lo in at most 2^12 buckets
+// finds the buckets of the middle ranks, and only the values in those buckets are ordered.
+template <typename Value>
+int64_t median_rounded(size_t n, Value value, int64_t lo, int64_t hi) {
+    const size_t half = n / 2;
+    const uint64_t range = (uint64_t)hi - (uint64_t)lo;
+    const int width = range == 0 ? 0 : 64 - __builtin_clzll(range);
+    const int shift = std::max(0, width - 12);
+    std::vector<uint32_t> hist((size_t)(range >> shift) + 1, 0u);
+    for (size_t i = 0; i < n; ++i) ++hist[((uint64_t)value(i) - (uint64_t)lo) >> shift];
+    const size_t first_rank = n % 2 ? half : half - 1;  // the lower middle rank (the only one for odd n)
+    size_t below = 0, b_lo = 0;
+    while (below + hist[b_lo] <= first_rank) below += hist[b_lo++];
+    size_t b_hi = b_lo, below_hi = below;
+    while (below_hi + hist[b_hi] <= half) below_hi += hist[b_hi++];
+    I64 mid;
+    mid.reserve(below_hi + hist[b_hi] - below);
+    for (size_t i = 0; i < n; ++i) {
+        const int64_t x = value(i);
+        const size_t b = (size_t)(((uint64_t)x - (uint64_t)lo) >> shift);
+        if (b >= b_lo && b <= b_hi) mid.push_back(x);
+    }
+    std::nth_element(mid.begin(), mid.begin() + (half - below), mid.end());  // mid[i] holds the value of rank below + i
+    double m = (double)mid[half - below];
+    if (n % 2 == 0) m = ((double)*std::max_element(mid.begin(), mid.begin() + (half - below)) + m) / 2.0;
     return (int64_t)std::nearbyint(m);
 }
 
 struct Fit {
     double bits = 0.0;
-    bool zigzag_mapped = false;
+    bool delta = false, zigzag_mapped = false;
     int64_t param = 0;
-    I64 mapped;
     TokenModel model;
 };
 
-// The cheaper mapping of a stream to non-negative integers (shift to the minimum first, then zigzag around the median) with its model
-Fit fit_mapping(const I64 &values) {
-    Fit best;
-    for (int zz = 0; zz < 2; ++zz) {
-        const int64_t param = zz ? median_rounded(values) : *std::min_element(values.begin(), values.end());
-        I64 mapped(values.size());
-        int64_t vmax = 0;
-        for (size_t i = 0; i < values.size(); ++i) {
-            mapped[i] = zz ? zigzag(values[i] - param) : values[i] - param;
-            vmax = std::max(vmax, mapped[i]);
-        }
-        int split, msb;
-        fine_tokenizer(vmax, split, msb);
-        I64 fine;
-        for (int64_t m : mapped) {
-            const int64_t t = split_value(m, split, msb).token;
-            if (t >= (int64_t)fine.size()) fine.resize(t + 1, 0);
-            ++fine[t];
-        }
-        TokenModel model = best_model(fine, split, msb, (int64_t)values.size());
-        const double bits = (double)(1 + exp_golomb_bits(zigzag(param))) + model.bits;
-        if (!zz || bits < best.bits) {
-            best.bits = bits, best.zigzag_mapped = zz == 1, best.param = param;
-            best.mapped = std::move(mapped);
-            best.model = std::move(model);
-        }
-    }
-    return best;
-}
-
-struct Symbol {
-    uint32_t start, freq;
-    int prec;
+// The value of index i of a stream as coded: its raw value or its difference with the previous one, shifted or zigzagged around param
+struct Mapping {
+    const int64_t *v;
+    bool delta, zz;
+    int64_t param;
+    int64_t candidate(size_t i) const { return delta ? v[i] - (i > 0 ? v[i - 1] : 0) : v[i]; }
+    int64_t operator()(size_t i) const { return zz ? zigzag(candidate(i) - param) : candidate(i) - param; }
 };
 
-// rANS over symbols given in decoding order (encoded last to first); 32-bit words, the last emitted first, little-endian
-std::vector<uint8_t> rans_pack(const std::vector<Symbol> &symbols) {
+// One mapping of a stream's raw values (delta = false) or differences between consecutive values (delta = true) to non-negative
+// integers, a shift to the minimum (zz = false) or a zigzag around the rounded median (zz = true), with its best token model. The
+// encoder keeps, per stream, the first of the smallest size in the order (raw, shift), (raw, zigzag), (differences, shift),
+// (differences, zigzag), as the reference does. The mapped values are not stored: the rANS pass maps them again.
+Fit fit_one(const int64_t *v, size_t n, bool delta, bool zz) {
+    Mapping map{v, delta, zz, 0};
+    int64_t lo = map.candidate(0), hi = lo;
+    for (size_t i = 1; i < n; ++i) {
+        const int64_t x = map.candidate(i);
+        lo = std::min(lo, x), hi = std::max(hi, x);
+    }
+    map.param = zz ? median_rounded(n, [&](size_t i) { return map.candidate(i); }, lo, hi) : lo;
+    // the largest mapped value: zigzag grows with the distance from param on either side
+    const int64_t vmax = zz ? std::max(zigzag(hi - map.param), zigzag(lo - map.param)) : hi - lo;
+    int split, msb;
+    fine_tokenizer(vmax, split, msb);
+    I64 fine(split_value(vmax, split, msb).token + 1, 0);  // tokens increase with the value
+    for (size_t i = 0; i < n; ++i) ++fine[split_value(map(i), split, msb).token];
+    Fit f;
+    f.delta = delta, f.zigzag_mapped = zz, f.param = map.param;
+    f.model = best_model(fine, split, msb, (int64_t)n);
+    f.bits = (double)(1 + exp_golomb_bits(zigzag(f.param))) + f.model.bits;
+    return f;
+}
+
+// fn(0) ... fn(n - 1) on up to num_threads host threads (0: one per hardware thread), the calling thread included
+template <typename Fn>
+void parallel_for(size_t n, Fn fn, int num_threads = 0) {
+    std::atomic<size_t> next{0};
+    auto work = [&]() {
+        for (size_t t = next++; t < n; t = next++) fn(t);
+    };
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t threads = std::min<size_t>(n, num_threads > 0 ? (size_t)num_threads : hw);
+    std::vector<std::thread> pool;
+    for (size_t t = 1; t < threads; ++t) pool.emplace_back(work);
+    work();
+    for (std::thread &t : pool) t.join();
+}
+
+// One token of a stream's model as the encoder uses it: x / freq for 0 <= x < 2^63 and 1 <= freq <= 2^16 by a multiply-high and a
+// shift (Granlund and Montgomery, "Division by Invariant Integers using Multiplication", 1994, theorem 4.2 with N = 63: with
+// l = ceil(log2 freq) and m = ceil(2^(63 + l) / freq), which is below 2^64, floor(x / freq) = floor(m x / 2^(63 + l)), taken as the
+// high word of (2 x) m shifted right by l); the state before a token is below x_max <= 2^63. The update ((x / freq) << kPrec) +
+// x % freq + start is x + start + q (2^kPrec - freq).
+struct EncToken {
+    uint64_t x_max, rcp;
+    uint32_t start, cmpl;
+    int shift;
+};
+
+std::vector<EncToken> encoder_tokens(const I64 &freqs) {
+    std::vector<EncToken> tokens(freqs.size());
+    int64_t start = 0;
+    for (size_t t = 0; t < freqs.size(); ++t) {
+        const uint64_t f = (uint64_t)freqs[t];
+        EncToken &e = tokens[t];
+        e.start = (uint32_t)start, e.cmpl = (uint32_t)((uint64_t(1) << kPrec) - f);
+        start += freqs[t];
+        if (f == 0) continue;  // an unused token
+        e.x_max = ((kStateLow >> kPrec) << 32) * f;
+        const int l = f == 1 ? 0 : 64 - __builtin_clzll(f - 1);
+        e.shift = l;
+        const unsigned __int128 num = (unsigned __int128)1 << (63 + l);
+        e.rcp = (uint64_t)((num + f - 1) / f);
+    }
+    return tokens;
+}
+
+// The rANS state over every stream's symbols, encoded last to first (the decoder reads stream 0's first value first: its token, then
+// its raw bits in chunks of at most kRawChunk bits, most significant first, each a uniform symbol of that many bits). The 32-bit words
+// the state emits are written backward from the end of words[0, capacity); the payload is the final state's high and low words followed
+// by the emitted words, last emitted first. Returns the index of the payload's first word, or -1 when it does not fit.
+int64_t rans_pack(const std::vector<Mapping> &mapped, size_t n, const std::vector<std::vector<EncToken>> &tokens, const int *split_exp,
+                  const int *msb_bits, uint32_t *words, int64_t capacity) {
+    constexpr int kMaxWordsPerValue = 1 + (kMaxExponent + kRawChunk - 1) / kRawChunk;
     uint64_t x = kStateLow;
-    std::vector<uint32_t> out;
-    for (size_t k = symbols.size(); k-- > 0;) {
-        const Symbol &s = symbols[k];
-        if (x >= ((kStateLow >> s.prec) << 32) * (uint64_t)s.freq) {
-            out.push_back((uint32_t)x);
-            x >>= 32;
+    int64_t pos = capacity;
+    // emit the low word when x >= limit: the word is stored either way (a later one overwrites it when not emitted), no branch
+    auto renorm = [&](uint64_t limit) {
+        words[pos - 1] = (uint32_t)x;
+        const bool out = x >= limit;
+        pos -= out;
+        x = out ? x >> 32 : x;
+    };
+    for (size_t s = mapped.size(); s-- > 0;) {
+        const EncToken *tok = tokens[s].data();
+        const Mapping &map = mapped[s];
+        const int split = split_exp[s], msb = msb_bits[s];
+        for (size_t i = n; i-- > 0;) {
+            if (pos < kMaxWordsPerValue) return -1;
+            const Split sp = split_value(map(i), split, msb);
+            // raw chunks, least significant first: the last one the decoder reads (nr - 16 (k - 1) bits, 0 bits without raw bits,
+            // which leaves x as it is), then 16 bits each
+            int c = sp.num_raw - kRawChunk * ((sp.num_raw - 1) / kRawChunk);
+            renorm((kStateLow >> c) << 32);
+            x = (x << c) | (uint64_t)(sp.raw & ((int64_t(1) << c) - 1));
+            for (int at = c; at < sp.num_raw; at += kRawChunk) {
+                renorm((kStateLow >> kRawChunk) << 32);
+                x = (x << kRawChunk) | (uint64_t)((sp.raw >> at) & ((int64_t(1) << kRawChunk) - 1));
+            }
+            const EncToken &e = tok[sp.token];
+            renorm(e.x_max);
+            const uint64_t q = (uint64_t)(((unsigned __int128)(x << 1) * e.rcp) >> 64) >> e.shift;
+            x += e.start + q * e.cmpl;
         }
-        x = ((x / s.freq) << s.prec) + x % s.freq + s.start;
     }
-    out.push_back((uint32_t)x);
-    out.push_back((uint32_t)(x >> 32));
-    std::vector<uint8_t> bytes(4 * out.size());
-    for (size_t i = 0; i < out.size(); ++i) {
-        const uint32_t w = out[out.size() - 1 - i];
-        for (int b = 0; b < 4; ++b) bytes[4 * i + b] = (uint8_t)(w >> (8 * b));
-    }
-    return bytes;
+    if (pos < 2) return -1;
+    words[--pos] = (uint32_t)x;
+    words[--pos] = (uint32_t)(x >> 32);
+    return pos;
 }
 
 // ---- device: histograms of fine tokens for estimate_stream_bits --------------------------------------------------------------------
@@ -371,55 +470,35 @@ int igs_rans_encode(int num_streams, int64_t count, const int64_t *streams, int 
     IGS_REQUIRE(num_streams >= 1 && count >= 1, "%s: streams must be non-empty", who);
     IGS_REQUIRE(streams && payload && payload_bytes && models && codes && payload_bits, "%s: null pointer", who);
     const size_t n = (size_t)count;
-    // candidates: raw values and differences of every stream, fitted on host threads
-    std::vector<I64> cand(2 * (size_t)num_streams);
-    for (int s = 0; s < num_streams; ++s) {
-        const int64_t *v = streams + (size_t)s * n;
-        cand[2 * s].assign(v, v + n);
-        I64 &d = cand[2 * s + 1];
-        d.resize(n);
-        for (size_t i = 0; i < n; ++i) d[i] = v[i] - (i > 0 ? v[i - 1] : 0);
-    }
-    std::vector<Fit> fits(cand.size());
-    std::atomic<size_t> next{0};
-    auto work = [&]() {
-        for (size_t t = next++; t < cand.size(); t = next++) fits[t] = fit_mapping(cand[t]);
-    };
-    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const size_t threads = std::min<size_t>(cand.size(), num_threads > 0 ? (size_t)num_threads : hw);
-    std::vector<std::thread> pool;
-    for (size_t t = 1; t < threads; ++t) pool.emplace_back(work);
-    work();
-    for (std::thread &t : pool) t.join();
+    // the four mappings of every stream (raw values or differences, shift or zigzag), fitted on host threads
+    std::vector<Fit> fits(4 * (size_t)num_streams);
+    parallel_for(fits.size(), [&](size_t t) { fits[t] = fit_one(streams + (t / 4) * n, n, (t >> 1) & 1, t & 1); }, num_threads);
+    auto pick = [&](size_t a, size_t b) -> const Fit & { return fits[b].bits < fits[a].bits ? fits[b] : fits[a]; };
 
-    std::vector<Symbol> symbols;
-    symbols.reserve(n * num_streams * 2);
+    std::vector<Mapping> mapped(num_streams);
+    std::vector<std::vector<EncToken>> tokens(num_streams);
+    std::vector<int> split(num_streams), msb(num_streams);
     for (int s = 0; s < num_streams; ++s) {
-        const bool delta = fits[2 * s + 1].bits < fits[2 * s].bits;
-        const Fit &f = fits[2 * s + (delta ? 1 : 0)];
+        const Fit &raw = pick(4 * s, 4 * s + 1), &diff = pick(4 * s + 2, 4 * s + 3);
+        const bool delta = diff.bits < raw.bits;
+        const Fit &f = delta ? diff : raw;
         const TokenModel &m = f.model;
         if ((int)m.codes.size() > kMaxTokens) return igs::set_error(IGS_ERR_INVALID, "%s: more than %d tokens", who, kMaxTokens);
-        I64 starts(m.freqs.size(), 0);
-        for (size_t t = 1; t < starts.size(); ++t) starts[t] = starts[t - 1] + m.freqs[t - 1];
-        for (int64_t v : f.mapped) {
-            const Split sp = split_value(v, m.split_exp, m.msb_bits);
-            symbols.push_back({(uint32_t)starts[sp.token], (uint32_t)m.freqs[sp.token], kPrec});
-            for (int left = sp.num_raw; left > 0;) {  // raw bits as uniform symbols, most significant first
-                const int chunk = std::min(left, kRawChunk);
-                left -= chunk;
-                symbols.push_back({(uint32_t)((sp.raw >> left) & ((int64_t(1) << chunk) - 1)), 1u, chunk});
-            }
-        }
+        mapped[s] = Mapping{streams + (size_t)s * n, delta, f.zigzag_mapped, f.param}, tokens[s] = encoder_tokens(m.freqs), split[s] = m.split_exp, msb[s] = m.msb_bits;
         int64_t *row = models + (size_t)s * IGS_RANS_MODEL_FIELDS;
         row[0] = delta, row[1] = f.zigzag_mapped, row[2] = f.param, row[3] = m.split_exp, row[4] = m.msb_bits, row[5] = m.mantissa_bits;
         row[6] = (int64_t)m.codes.size();
         std::copy(m.codes.begin(), m.codes.end(), codes + (size_t)s * kMaxTokens);
         payload_bits[s] = m.payload_bits;
     }
-    const std::vector<uint8_t> bytes = rans_pack(symbols);
-    IGS_REQUIRE(bytes.size() <= payload_capacity, "%s: payload of %zu bytes exceeds the capacity %zu", who, bytes.size(), payload_capacity);
-    memcpy(payload, bytes.data(), bytes.size());
-    *payload_bytes = bytes.size();
+    // the words go backward into the caller's buffer, then to its start (little-endian words, the byte order of the format)
+    static_assert(__BYTE_ORDER__ == __ORDER_LITTLE_ENDIAN__, "the payload is written as host words");
+    const int64_t capacity = (int64_t)(payload_capacity / 4);
+    std::unique_ptr<uint32_t[]> words(new uint32_t[capacity > 0 ? capacity : 1]);
+    const int64_t first = rans_pack(mapped, n, tokens, split.data(), msb.data(), words.get(), capacity);
+    IGS_REQUIRE(first >= 0, "%s: the payload exceeds the capacity of %zu bytes", who, payload_capacity);
+    *payload_bytes = 4 * (size_t)(capacity - first);
+    memcpy(payload, words.get() + first, *payload_bytes);
     return IGS_OK;
 }
 
@@ -430,13 +509,21 @@ int igs_rans_decode(int num_streams, int64_t count, const int64_t *models, const
     IGS_REQUIRE(payload && (num_streams == 0 || (models && codes && values)), "%s: null pointer", who);
     IGS_REQUIRE(payload_size % 4 == 0 && payload_size >= 8, "%s: invalid rANS payload", who);
     const size_t num_words = payload_size / 4;
-    std::vector<uint32_t> words(num_words, 0u);
-    for (size_t i = 0; i < num_words; ++i)
-        for (int b = 0; b < 4; ++b) words[i] |= (uint32_t)payload[4 * i + b] << (8 * b);
+    auto word = [payload](size_t k) {  // little-endian words (the static_assert of the encoder)
+        uint32_t w;
+        memcpy(&w, payload + 4 * k, 4);
+        return w;
+    };
+    // per stream: the token of each slot of the state's low kPrec bits (16-bit entries: the table stays in the core's cache) and each
+    // token's frequency, first slot, smallest value and raw-bit count
+    struct Tok {
+        uint32_t freq, start;
+        int64_t base;
+        int num_raw;
+    };
     struct Table {
-        int split_exp, msb_bits;
-        I64 freqs, starts;
-        std::vector<uint32_t> token_of_slot;
+        std::vector<uint16_t> slot;
+        std::vector<Tok> tok;
     };
     std::vector<Table> tables(num_streams);
     for (int s = 0; s < num_streams; ++s) {
@@ -448,46 +535,48 @@ int igs_rans_decode(int num_streams, int64_t count, const int64_t *models, const
         const int64_t last = num_codes - 1;
         IGS_REQUIRE(!(last >= (int64_t(1) << split) && split + ((last - (int64_t(1) << split)) >> msb) > kMaxExponent),
                     "%s: invalid token model of stream %d", who, s);
-        Table &t = tables[s];
-        t.split_exp = split, t.msb_bits = msb;
-        I64 weights(num_codes);
+        I64 weights(num_codes), freqs;
         for (int64_t k = 0; k < num_codes; ++k)
             IGS_REQUIRE(code_to_weight(codes[(size_t)s * kMaxTokens + k], mb, weights[k]), "%s: invalid token count code", who);
-        IGS_REQUIRE(frequencies(weights, t.freqs), "%s: cannot normalize the token histogram of stream %d", who, s);
-        t.starts.assign(num_codes, 0);
+        IGS_REQUIRE(frequencies(weights, freqs), "%s: cannot normalize the token histogram of stream %d", who, s);
+        Table &t = tables[s];
+        t.slot.resize(size_t(1) << kPrec);
+        t.tok.resize(num_codes);
+        uint32_t start = 0;
         for (int64_t k = 0; k < num_codes; ++k) {
-            if (k > 0) t.starts[k] = t.starts[k - 1] + t.freqs[k - 1];
-            t.token_of_slot.insert(t.token_of_slot.end(), (size_t)t.freqs[k], (uint32_t)k);
+            Tok &o = t.tok[k];
+            token_base(k, split, msb, o.base, o.num_raw);
+            o.freq = (uint32_t)freqs[k], o.start = start;
+            std::fill(t.slot.begin() + start, t.slot.begin() + start + o.freq, (uint16_t)k);
+            start += o.freq;
         }
     }
-    uint64_t x = ((uint64_t)words[0] << 32) | words[1];
+    uint64_t x = ((uint64_t)word(0) << 32) | word(1);
     size_t pos = 2;
     for (int s = 0; s < num_streams; ++s) {
-        const Table &t = tables[s];
+        const uint16_t *slot = tables[s].slot.data();
+        const Tok *tok = tables[s].tok.data();
         int64_t *out = values + (size_t)s * (size_t)count;
         for (int64_t i = 0; i < count; ++i) {
-            const uint64_t slot = x & ((uint64_t(1) << kPrec) - 1);
-            const uint32_t token = t.token_of_slot[slot];
-            x = (uint64_t)t.freqs[token] * (x >> kPrec) + slot - (uint64_t)t.starts[token];
+            const uint32_t sl = (uint32_t)(x & ((uint64_t(1) << kPrec) - 1));
+            const Tok &o = tok[slot[sl]];
+            x = (uint64_t)o.freq * (x >> kPrec) + sl - o.start;
             if (x < kStateLow) {
                 IGS_REQUIRE(pos < num_words, "%s: truncated rANS payload", who);
-                x = (x << 32) | words[pos++];
+                x = (x << 32) | word(pos++);
             }
-            int64_t base;
-            int num_raw;
-            token_base(token, t.split_exp, t.msb_bits, base, num_raw);
             int64_t raw = 0;
-            for (int left = num_raw; left > 0;) {
+            for (int left = o.num_raw; left > 0;) {
                 const int chunk = std::min(left, kRawChunk);
                 left -= chunk;
                 raw = (raw << chunk) | (int64_t)(x & ((uint64_t(1) << chunk) - 1));
                 x >>= chunk;
                 if (x < kStateLow) {
                     IGS_REQUIRE(pos < num_words, "%s: truncated rANS payload", who);
-                    x = (x << 32) | words[pos++];
+                    x = (x << 32) | word(pos++);
                 }
             }
-            out[i] = base | raw;
+            out[i] = o.base | raw;
         }
     }
     return IGS_OK;
@@ -537,8 +626,9 @@ int igs_estimate_stream_bits(int num_streams, int64_t count, const int64_t *stre
             for (size_t b = 0; b < (size_t)kEstBins; ++b)
                 if (src[b]) used = b + 1;
             fine.assign(src, src + used);
+            const std::vector<FineBin> bins = fine_bins(fine, split, 0);
             for (int sp = 0; sp <= split; ++sp) {
-                const int64_t raw_bits = coarsen(fine, split, 0, sp, 0, counts);
+                const int64_t raw_bits = coarsen(bins, sp, 0, counts);
                 terms.clear();
                 for (int64_t c : counts)
                     if (c > 0) terms.push_back((double)c * std::log2((double)count / (double)c));

@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from igs_b200 import bitstream
+from igs_b200 import bitstream, codec
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "py_codec.npz")
 CASES = ["p500", "p3000_refine3", "p1", "p64_const", "p800_big"]
@@ -70,3 +70,64 @@ def test_truncated_payload_is_rejected(golden):
     data = golden["p500/bitstream"].tobytes()
     with pytest.raises(ValueError):
         bitstream.decode_bitstream(data[:len(data) - 40])
+
+
+def _reference_rans():
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    from oracle import build_ref
+
+    try:
+        return build_ref.load_cpp_module(build_ref.RANS)
+    except ImportError:
+        return None
+
+
+def _stream_sets():
+    """Seeded stream sets that reach the encoder's edge cases: wide and narrow ranges, 40-bit values (raw bits in three chunks), even
+    and odd lengths (the median of two middle values in different buckets), constant and two-valued streams, one value."""
+    rng = np.random.default_rng(11)
+    yield [rng.integers(-(1 << 40), 1 << 40, 1000, dtype=np.int64), rng.integers(-3, 4, 1000, dtype=np.int64)]
+    yield [np.sort(rng.integers(0, 1 << 30, 4096, dtype=np.int64)), rng.normal(0, 40, 4096).astype(np.int64)]
+    yield [np.r_[np.zeros(500, np.int64), np.full(500, 1 << 33, np.int64)], rng.geometric(0.001, 1000).astype(np.int64)]
+    yield [np.full(333, -7, np.int64), (rng.standard_cauchy(333) * 1000).astype(np.int64).clip(-(1 << 50), 1 << 50)]
+    yield [np.array([123456789], np.int64), np.array([-5], np.int64)]
+    yield [rng.integers(0, 2, 20001, dtype=np.int64) * (1 << 20) + rng.integers(0, 3, 20001, dtype=np.int64)]
+
+
+@pytest.mark.skipif(_reference_rans() is None, reason="the reference's igs_rans module (oracle/build_ref.py) is not built")
+@pytest.mark.parametrize("k", range(6))
+def test_payload_matches_reference_coder(k):
+    """The library's encoder against the reference's C++ coder (built from source into oracle/_ref) on the same streams: the same
+    payload bytes, the same mapping and model per stream, and the library decodes the payload to the mapped values."""
+    streams = list(_stream_sets())[k]
+    rans = _reference_rans()
+    ref_payload, ref_models = rans.encode_streams(streams)
+
+    class Writer:
+        num_bits = 0
+
+        def write(self, *a):
+            pass
+
+        write_se = write_ue = write
+
+    payload, _ = codec.encode_streams([streams], Writer())
+    assert payload == bytes(ref_payload)
+    count = len(streams[0])
+    rows = np.zeros((len(streams), codec.MODEL_FIELDS), dtype=np.int64)
+    table = np.zeros((len(streams), codec.MAX_TOKENS), dtype=np.int64)
+    for j, m in enumerate(ref_models):
+        rows[j, 3:7] = (m[3], m[4], m[5], len(m[6]))
+        table[j, :len(m[6])] = m[6]
+    buf = np.frombuffer(payload, dtype=np.uint8).copy()
+    values = np.zeros((len(streams), count), dtype=np.int64)
+    lib = codec._lib.load()
+    p = lambda a: codec.ctypes.c_void_p(a.ctypes.data)  # noqa: E731
+    assert lib.igs_rans_decode(len(streams), count, p(rows), p(table), p(buf), buf.size, p(values)) == 0
+    ref_values = rans.decode_streams(bytes(ref_payload), [(m[3], m[4], m[5], np.asarray(m[6], dtype=np.int64)) for m in ref_models],
+                                     count)
+    for j in range(len(streams)):
+        assert np.array_equal(values[j], np.asarray(ref_values[j]))
