@@ -316,11 +316,12 @@ def run_ours(args, wl):
 
     # end to end with host buffers: through the C ABI (the step as above, parameters copied in and the loss read back every step), and
     # through the drop-in gsplat API with autograd (what model.py calls)
-    e2e = e2e_autograd = e2e_autograd_graph = None
+    e2e = e2e_autograd = e2e_autograd_graph = e2e_autograd_graph_l1 = None
     if not args.no_e2e:
         e2e = run_step_e2e(args, step, step.raw, inp, device, world, "step")
         e2e_autograd = run_e2e(args, wl, inp, device, step.capacity, world)
         e2e_autograd_graph = run_e2e(args, wl, inp, device, step.capacity, world, graph=True)
+        e2e_autograd_graph_l1 = run_e2e(args, wl, inp, device, step.capacity, world, graph=True, routed_l1=True)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -366,7 +367,8 @@ def run_ours(args, wl):
             "step_roofline": {"algorithmic_bytes": step_bytes, "loss_bytes": loss_bytes,
                               "frac_raster": step_bytes / (ms_per_step * 1e-3) / 1e9 / hbm_peak,
                               "frac_with_loss": (step_bytes + loss_bytes) / (ms_per_step * 1e-3) / 1e9 / hbm_peak},
-            "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph, "cpu_baseline": cpu,
+            "e2e": e2e, "e2e_autograd": e2e_autograd, "e2e_autograd_graph": e2e_autograd_graph,
+            "e2e_autograd_graph_l1": e2e_autograd_graph_l1, "cpu_baseline": cpu,
             "gpu_launches": kernels_per_step * args.steps, "clocks": clk, "bands_2160p": bands_leg,
             "bands_2160p_other_exchange": bands_leg_other,
         }
@@ -567,15 +569,18 @@ def run_step_e2e(args, step, dev_params, inp, device, world, api):
                    (", both copies captured in the step's CUDA graph)" if api == "step" else ")")}
 
 
-def run_e2e(args, wl, inp, device, capacity, world, graph=False):
+def run_e2e(args, wl, inp, device, capacity, world, graph=False, routed_l1=False):
     """The step through the drop-in gsplat API with autograd and F.l1_loss, as model.py calls it, with the parameters copied in from
     pinned host memory and the loss read back every step: eagerly (graph=False), or captured in one CUDA graph with the copies, the
-    forward, the loss and the backward pass as model.py's CUDA-graph step does (model.py:1160-1209; the optimizer is outside the metric)."""
+    forward, the loss and the backward pass as model.py's CUDA-graph step does (model.py:1160-1209; the optimizer is outside the metric).
+    routed_l1: F.l1_loss as igs_b200.autograd.install_l1() routes model.py's call (the library's one-pass loss keeping the signs)."""
     import torch.nn.functional as F
 
     import gsplat
 
     from igs_b200 import autograd as ag
+
+    l1_loss = ag._routed_l1_loss if routed_l1 else F.l1_loss
 
     host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
     target = (inp["loss_target"] if "loss_target" in inp else inp["target"]).to(device)
@@ -598,7 +603,7 @@ def run_e2e(args, wl, inp, device, capacity, world, graph=False):
         xys, radii, conics, hits = gsplat.project_gaussians_2d_scale_rot(means, scales, rots, wl.height, wl.width, tb)
         img = gsplat.rasterize_gaussians_sum(xys, radii, conics, hits, feats, wl.height, wl.width, topk_norm=True, capacity=capacity)
         img = img.permute(2, 0, 1).contiguous()
-        loss = F.l1_loss(img, target)
+        loss = l1_loss(img, target)
         if "rate" in opts:  # model._get_total_loss (model.py:1235-1240)
             r = opts["rate"]
             loss = loss + ag.rate_loss(raw_feats, raw_rots, loss, r["model"], r["inv_rot_step"], 1.0, r["factor"])
@@ -648,7 +653,8 @@ def run_e2e(args, wl, inp, device, capacity, world, graph=False):
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     return {"value": value, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "api": ("igs_b200.autograd.quantize_ste + feat @ T.T + " if "quant" in opts else "") +
-                   "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + F.l1_loss" +
+                   "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum(topk_norm=True, capacity) + " +
+                   ("F.l1_loss routed by igs_b200.autograd.install_l1()" if routed_l1 else "F.l1_loss") +
                    (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward" +
                    (", copies, forward, loss and backward replayed as one CUDA graph (model.py's graph-captured step)" if graph else
                     ", eager")}

@@ -524,7 +524,8 @@ __device__ __forceinline__ int halving_index(int lane) {
 //
 // The operator's lists hold Gaussian IDs, with no tile list to index, so each warp (an 8x4 patch) walks the union of its pixels' IDs in
 // increasing order (a warp-wide minimum per step); lanes whose pixel holds the current Gaussian contribute their values, the others
-// zeros; the warp sums the 5 + C values with one recursive-halving reduce-scatter and one global atomic per value. Each pixel sorts its
+// zeros; the warp sums the 5 + C values (of two Gaussians at a time for C <= 3) with one recursive-halving reduce-scatter and one
+// global atomic per value. Each pixel sorts its
 // ten slots by ID once (a 29-comparator network on registers) and keeps them in shared memory, so that at every step of the walk its
 // smallest unconsumed ID is at hand and its slot's values are two loads away, instead of a minimum and a select over ten registers.
 // The few Gaussians of a warp's union are read through the L1 cache.
@@ -548,7 +549,7 @@ constexpr int kSlotBits = 4;
 constexpr int kMaxWalkId = (1 << (31 - kSlotBits)) - 1;
 
 template <int C, int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
+__global__ void __launch_bounds__(kThreads, NV <= 8 ? 5 : 3)
     raster_bwd_ids_kernel(const int tiles_x, const int img_h, const int img_w, const int channels_rt, const int num_points,
         const float2 *__restrict__ xys,
         const float *__restrict__ conics, const float *__restrict__ colors, const float *__restrict__ v_output,
@@ -597,51 +598,73 @@ __global__ void __launch_bounds__(kThreads, NV <= 8 ? 4 : 3)
     // with the slots' colour weight and dL/dsigma, so that each step of the walk finds the pixel's smallest unconsumed ID and its values
     // with a few loads
     __shared__ int s_key[kTopK][kThreads];
-    __shared__ float s_w[kTopK][kThreads], s_v[kTopK][kThreads];
+    __shared__ float2 s_wv[kTopK][kThreads];  // (colour weight, dL/dsigma)
     const int tid = threadIdx.x;
     int key[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
         key[k] = id[k] == kNoId ? kNoId : (id[k] << kSlotBits) | k;
-        s_w[k][tid] = d[k] * inv;
-        s_v[k][tid] = -d[k] * (s[k] * inv + shared);
+        s_wv[k][tid] = make_float2(d[k] * inv, -d[k] * (s[k] * inv + shared));
     }
     sort10(key);
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) s_key[k][tid] = key[k];
 
-    const int value_index = halving_index<NV>(lane);
-    const bool adds = (lane % (32 / NV)) == 0 && value_index < 5 + channels;
+    // The walk. With NV <= 8 each step takes the two smallest IDs of the union and sums their 2 NV values in one reduce-scatter (fewer
+    // shuffles and steps than one Gaussian at a time); wider value sets take one Gaussian per step.
+    constexpr int kPerStep = NV <= 8 ? 2 : 1;
+    constexpr int kValues = kPerStep * NV;
+    const int index = halving_index<kValues>(lane);
+    const int value_index = index % NV, which = index / NV;  // lane's value and its Gaussian of the step
+    const bool adds = (lane % (32 / kValues)) == 0 && value_index < 5 + channels;
     float *const target = value_index < 3 ? v_conic + value_index : value_index < 5 ? v_xy + (value_index - 3) : v_colors + (value_index - 5);
     const int stride = value_index < 3 ? 3 : value_index < 5 ? 2 : channels;
     int pos = 0;
     int head = key[0];
-    int low = __reduce_min_sync(0xffffffffu, head);
-    while (low != kNoId) {
-        const int cur = low >> kSlotBits;
-        // the Gaussian's parameters are requested first, and the next step's Gaussian is found before this step's sums
-        const float2 xy = __ldg(&xys[cur]);
-        const float a = __ldg(&conics[3 * cur]), b = __ldg(&conics[3 * cur + 1]), c = __ldg(&conics[3 * cur + 2]);
-        float ws = 0.f, vs = 0.f;
+    // the pixel's values for Gaussian cur (zero if it does not hold it); a pixel holding it moves to its next slot
+    auto take = [&](const int cur, float &ws, float &vs) {
+        ws = 0.f, vs = 0.f;
         if ((head >> kSlotBits) == cur) {
-            const int k = head & ((1 << kSlotBits) - 1);
-            ws = s_w[k][tid];
-            vs = s_v[k][tid];
+            const float2 wv = s_wv[head & ((1 << kSlotBits) - 1)][tid];
+            ws = wv.x, vs = wv.y;
             ++pos;
             head = pos < kTopK ? s_key[pos][tid] : kNoId;
         }
-        low = __reduce_min_sync(0xffffffffu, head);
+    };
+    auto values = [&](const int cur, const float ws, const float vs, float *val) {
+        const float2 xy = __ldg(&xys[cur]);
+        const float a = __ldg(&conics[3 * cur]), b = __ldg(&conics[3 * cur + 1]), c = __ldg(&conics[3 * cur + 2]);
         const float dx = xy.x - px, dy = xy.y - py;
-        float val[NV];
-        val[0] = 0.5f * vs * dx * dx;
+        val[0] = vs * dx * dx;  // halved after the sum (exact: a power of two)
         val[1] = vs * dx * dy;
-        val[2] = 0.5f * vs * dy * dy;
+        val[2] = vs * dy * dy;
         val[3] = vs * (a * dx + b * dy);
         val[4] = vs * (b * dx + c * dy);
 #pragma unroll
         for (int ch = 0; ch < NV - 5; ++ch) val[5 + ch] = ch < kMaxC ? ws * v_out[ch < kMaxC ? ch : 0] : 0.f;
-        const float total = warp_sum_scatter<NV>(val, lane);
-        if (adds) atomicAdd(target + (size_t)stride * cur, total);
+    };
+    int low = __reduce_min_sync(0xffffffffu, head);
+    while (low != kNoId) {
+        int cur[kPerStep];
+        float ws[kPerStep], vs[kPerStep];
+        bool valid[kPerStep];
+#pragma unroll
+        for (int q = 0; q < kPerStep; ++q) {
+            valid[q] = low != kNoId;  // uniform over the warp; the first always is
+            cur[q] = valid[q] ? low >> kSlotBits : cur[0];
+            ws[q] = 0.f, vs[q] = 0.f;
+            if (valid[q]) {
+                take(cur[q], ws[q], vs[q]);
+                low = __reduce_min_sync(0xffffffffu, head);
+            }
+        }
+        float val[kValues];
+#pragma unroll
+        for (int q = 0; q < kPerStep; ++q) values(cur[q], ws[q], vs[q], val + q * NV);
+        const float total = warp_sum_scatter<kValues>(val, lane);
+        const bool last = which == kPerStep - 1;  // selects, not a dynamic index (which would put the arrays in local memory)
+        if (adds && (last ? valid[kPerStep - 1] : valid[0]))
+            atomicAdd(target + (size_t)stride * (last ? cur[kPerStep - 1] : cur[0]), (value_index == 0 || value_index == 2) ? 0.5f * total : total);
     }
 }
 

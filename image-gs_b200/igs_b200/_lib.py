@@ -61,6 +61,8 @@ SIGNATURES = {
     "igs_nearest_neighbors": (c_int, [c_int, P, c_int, P, P, P, c_size_t, P]),
     "igs_l1_workspace": (c_size_t, [c_int64]),
     "igs_l1_loss": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
+    "igs_l1_loss_signs": (c_int, [c_int64, P, P, c_float, P, P, P, c_size_t, P]),
+    "igs_l1_grad_from_signs": (c_int, [c_int64, P, P, P, P]),
     "igs_quantize_ste": (c_int, [c_int, c_int, P, P, P, P, P, c_float, c_float, P, P, P, P, P, P, P, P, P, P, P, P]),
     "igs_feat_transform_bwd": (c_int, [c_int, c_int, P, P, P, P, P]),
     "igs_bitstream_order_workspace": (c_size_t, [c_int]),

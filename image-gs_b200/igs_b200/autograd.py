@@ -5,12 +5,13 @@ Differentiable operators of the training step, with the semantics of the referen
     as the reference) or with a fixed capacity (no host read; CUDA-graph capturable)
   - quantize_ste: the straight-through step quantization of model.py:993-1006
   - rate_loss (compress/rate.py:178-202)
-  - l1_loss: ratio * F.l1_loss with its gradient computed in the same pass
+  - l1_loss: ratio * F.l1_loss in one pass that keeps the signs for the backward pass; install_l1() routes model.py's F.l1_loss to it
 
 The rasterization's autograd path keeps each pixel's top-K lists in the 16-bit tile-list form (positions in the tile's list; a quarter of
 the bytes of the reference's [H, W, 10] int32 ids); the backward pass selects the lists of a tile again when its list reaches 65535
 entries.
 """
+import types
 from typing import Optional
 
 import torch
@@ -154,16 +155,73 @@ def rate_loss(feat, rot, l1_loss, model, inv_rot_step, l1_ratio, factor):
 class _L1Loss(Function):
     @staticmethod
     def forward(ctx, image, target, ratio):
-        loss, grad = ops.l1_loss_and_grad(image.contiguous(), target.contiguous(), ratio)
-        ctx.save_for_backward(grad)
+        loss, signs = ops.l1_loss_signs(image.contiguous(), target.contiguous(), ratio)
+        ctx.save_for_backward(signs)
+        ctx.ratio = ratio
         return loss
 
     @staticmethod
     def backward(ctx, grad_loss):
-        (grad,) = ctx.saved_tensors
-        return grad * grad_loss, None, None
+        (signs,) = ctx.saved_tensors
+        scale = grad_loss if ctx.ratio == 1.0 else grad_loss * ctx.ratio
+        return ops.l1_grad_from_signs(signs, scale), None, None
 
 
 def l1_loss(image, target, ratio=1.0):
-    """ratio * mean|image - target| (model.py:1224-1227), its gradient computed in the forward pass."""
+    """ratio * mean|image - target| (model.py:1224-1227) in one pass that keeps the signs; the backward pass forms
+    sign * (g / numel) from them, ATen's l1_loss gradient bit for bit for ratio 1 (F.l1_loss)."""
     return _L1Loss.apply(image, target, float(ratio))
+
+
+def _routed_l1_loss(input, target, size_average=None, reduce=None, reduction="mean"):
+    """F.l1_loss with the library's loss for what it computes (the mean over two float32 CUDA tensors of one shape, no gradient for the
+    target); anything else goes to torch's F.l1_loss."""
+    import torch.nn.functional as F
+
+    if (size_average is None and reduce is None and reduction == "mean" and isinstance(input, torch.Tensor)
+            and isinstance(target, torch.Tensor) and input.is_cuda and target.device == input.device
+            and input.dtype == torch.float32 and target.dtype == torch.float32 and input.shape == target.shape and input.numel() > 0
+            and not target.requires_grad):
+        return l1_loss(input, target)
+    return F.l1_loss(input, target, size_average, reduce, reduction)
+
+
+class _FunctionalWithL1(types.ModuleType):
+    """torch.nn.functional as seen by a module after install_l1(): l1_loss routed (_routed_l1_loss), every other name torch's."""
+
+    def __init__(self):
+        super().__init__("torch.nn.functional")
+        self.l1_loss = _routed_l1_loss
+
+    def __getattr__(self, name):
+        import torch.nn.functional as F
+
+        return getattr(F, name)
+
+
+def install_l1(*module_names):
+    """Route F.l1_loss in the named modules (default: model, whose training loss calls it, model.py:1226) to the library's loss: the
+    name F bound there to torch.nn.functional is replaced by a view of it with l1_loss routed. Returns {(module, "F"): original} for
+    restore()."""
+    import importlib
+
+    import torch.nn.functional as F
+
+    replaced = {}
+    for name in module_names or ("model",):
+        try:
+            module = importlib.import_module(name)
+        except ImportError:
+            continue
+        if getattr(module, "F", None) is F:
+            replaced[(name, "F")] = F
+            module.F = _FunctionalWithL1()
+    return replaced
+
+
+def restore(replaced):
+    """Undo install_l1()."""
+    import importlib
+
+    for (name, attr), original in replaced.items():
+        setattr(importlib.import_module(name), attr, original)

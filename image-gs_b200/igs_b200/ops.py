@@ -314,6 +314,40 @@ def l1_loss_and_grad(image: torch.Tensor, target: torch.Tensor, ratio: float = 1
     return loss, grad
 
 
+def l1_loss_signs(image: torch.Tensor, target: torch.Tensor, ratio: float = 1.0, workspace: Optional[torch.Tensor] = None):
+    """(ratio * mean|image - target| as a 0-dim tensor, sign(image - target) as int8), in one pass; see igs_l1_loss_signs."""
+    _check_input(image, "image", torch.float32)
+    _check_input(target, "target", torch.float32)
+    if image.shape != target.shape:
+        raise ValueError(f"image {tuple(image.shape)} and target {tuple(target.shape)} differ")
+    dev = image.device
+    loss = torch.empty((), device=dev, dtype=torch.float32)
+    signs = torch.empty(image.shape, device=dev, dtype=torch.int8)
+    ws_bytes = _lib.load().igs_l1_workspace(image.numel())
+    if workspace is None:
+        workspace = torch.zeros(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib_call("igs_l1_loss_signs", image.numel(), ptr(image), ptr(target), float(ratio), ptr(loss), ptr(signs), ptr(workspace),
+                  ws_bytes, stream_of(dev))
+    return loss, signs
+
+
+def l1_grad_from_signs(signs: torch.Tensor, grad_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """sign * (g / numel) as float32 (g = grad_scale, a device scalar, or 1): the gradient of mean|image - target|, as ATen forms it."""
+    _check_input(signs, "signs", torch.int8)
+    dev = signs.device
+    grad = torch.empty(signs.shape, device=dev, dtype=torch.float32)
+    scale = None
+    if grad_scale is not None:
+        scale = grad_scale.detach().to(device=dev, dtype=torch.float32).contiguous()
+        if scale.numel() != 1:
+            raise ValueError("grad_scale must hold one value")
+    with torch.cuda.device(dev):
+        _lib_call("igs_l1_grad_from_signs", signs.numel(), ptr(signs), ptr(scale) if scale is not None else None, ptr(grad),
+                  stream_of(dev))
+    return grad
+
+
 def quantize_ste_forward(xy, scale, rot, feat, pos_steps, scale_step, rot_step, feat_steps, feat_transform=None, with_symbols=False):
     """Straight-through step quantization values (and optionally symbols and loss-space features); see igs_quantize_ste."""
     for t, n in ((xy, "xy"), (scale, "scale"), (rot, "rot"), (feat, "feat"), (pos_steps, "pos_steps"), (feat_steps, "feat_steps")):

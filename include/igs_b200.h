@@ -288,6 +288,13 @@ size_t igs_l1_workspace(int64_t numel);
 int igs_l1_loss(int64_t numel, const float *image, const float *target, float ratio, float *loss, float *grad, void *workspace,
                 size_t workspace_bytes, void *stream);
 
+/* The same loss keeping sign(image - target) (int8: -1, 0, 1) instead of the gradient, for autograd (F.l1_loss, model.py:1226): the
+ * backward pass then forms grad = sign * (g / numel) with igs_l1_grad_from_signs from the loss's incoming gradient g (a device scalar;
+ * null for 1), which is ATen's l1_loss backward product bit for bit. workspace as igs_l1_loss. */
+int igs_l1_loss_signs(int64_t numel, const float *image, const float *target, float ratio, float *loss, int8_t *signs, void *workspace,
+                      size_t workspace_bytes, void *stream);
+int igs_l1_grad_from_signs(int64_t numel, const int8_t *signs, const float *grad_scale, float *grad, void *stream);
+
 /* Straight-through "step" quantization of the Gaussian parameters during optimization (model.py:993-1006 with
  * compress/quantization.py:36-46,61-74,151-172,188-199; quarter turns off, log-domain scales): symbols
  * q_xy = round(xy / pos_steps), q_scale = round(log2|scale| / scale_step), q_rot = round(rot / rot_step), q_feat = round(feat / feat_steps)

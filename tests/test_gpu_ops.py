@@ -49,6 +49,42 @@ def test_l1_loss_matches_torch(numel_shape, device):
     assert float(loss2) == float(loss)
 
 
+@pytest.mark.parametrize("shape,ratio", [((3, 37, 53), 1.0), ((3, 64, 64), 0.75), ((9, 16, 1), 1.0)])
+def test_l1_loss_with_signs_matches_torch_autograd(shape, ratio, device):
+    """igs_b200.autograd.l1_loss (signs kept, gradient formed in the backward pass) against model.py's ratio * F.l1_loss: the gradient
+    bit for bit, the loss within summation order; and model.py's F.l1_loss routed to it by install_l1()."""
+    import sys
+    import types
+
+    g = torch.Generator().manual_seed(5)
+    img = torch.rand(shape, generator=g).to(device)
+    tgt = torch.rand(shape, generator=g).to(device)
+    tgt.view(-1)[::5] = img.view(-1)[::5]  # exact ties: zero gradient
+    x, y = img.clone().requires_grad_(True), img.clone().requires_grad_(True)
+    ref = ratio * F.l1_loss(x, tgt)
+    ref.backward()
+    mine = ratio * ag.l1_loss(y, tgt)
+    mine.backward()
+    assert abs(float(mine) - float(ref)) <= 1e-6 * abs(float(ref))
+    torch.testing.assert_close(y.grad, x.grad, rtol=0, atol=0)
+
+    fake = types.ModuleType("igs_fake_model")
+    fake.F = F
+    sys.modules["igs_fake_model"] = fake
+    try:
+        replaced = ag.install_l1("igs_fake_model")
+        assert fake.F is not F and fake.F.relu is F.relu
+        z = img.clone().requires_grad_(True)
+        routed = ratio * fake.F.l1_loss(z, tgt)
+        routed.backward()
+        assert float(routed) == float(mine)
+        torch.testing.assert_close(z.grad, x.grad, rtol=0, atol=0)
+        ag.restore(replaced)
+        assert fake.F is F
+    finally:
+        del sys.modules["igs_fake_model"]
+
+
 @pytest.mark.parametrize("case", [dict(h=88, w=120, n=300, seed=11), dict(h=64, w=80, n=200, c=9, seed=13), dict(h=50, w=70, n=150, c=1, seed=12)])
 def test_forward_with_fused_l1_matches_separate_loss(case, device):
     """The forward kernel's fused L1 loss: render and lists identical to the plain forward, gradient identical to the L1 kernel's (and to
