@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
                                                                const float img_w, const float img_h, const int *__restrict__ radii,
                                                                const float *__restrict__ conics, const unsigned long long timeout_ns) {
     constexpr int kGroup = kMaxC <= 4 ? kMaxRanks : 2;  // ranks whose loads are in flight together (registers: kGroup (5 + kMaxC))
-    igs::wait_for_predecessor();  // this rank's partials are complete (the band's raster step ran before this kernel)
+    igs::wait_for_predecessor_only();  // this rank's partials are complete (the band's raster step ran before this kernel)
     __shared__ int s_go;
     SyncWords *me = peers.sync[rank];
     if (threadIdx.x == 0) {
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
 
 __global__ void __launch_bounds__(32) band_done_kernel(const Peers peers, const int world, const int rank,
                                                        const unsigned long long timeout_ns) {
-    igs::wait_for_predecessor();  // band_reduce_kernel has completed: this rank's share is stored everywhere
+    igs::wait_for_predecessor_only();  // band_reduce_kernel has completed: this rank's share is stored everywhere
     if (threadIdx.x != 0) return;
     SyncWords *me = peers.sync[rank];
     if (atomicOr(&me->error, 0u) != 0u) return;

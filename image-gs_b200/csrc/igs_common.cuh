@@ -42,10 +42,16 @@ __device__ __forceinline__ float gaussian_sigma(float gx, float gy, float a, flo
 }
 
 // Programmatic dependent launch (sm_90 and later): the kernels of the training step are launched with programmatic stream serialization,
-// so a kernel is scheduled while its predecessor on the stream drains instead of after it; each of them begins with
-// wait_for_predecessor() (griddepcontrol.wait: returns once the predecessor has completed and its writes are visible; a no-op for a
-// kernel launched without the attribute) before it reads or writes memory.
-__device__ __forceinline__ void wait_for_predecessor() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// and each of them begins with wait_for_predecessor(): griddepcontrol.wait (returns once the predecessor has completed and its writes
+// are visible; a no-op for a kernel launched without the attribute) before it reads or writes memory, then
+// griddepcontrol.launch_dependents, so that the next kernel on the stream is launched as soon as every CTA of this one has started:
+// its CTAs take the SM slots this kernel's finished CTAs free and wait there (in griddepcontrol.wait) for it to complete, instead of
+// being launched after it. wait_for_predecessor_only() leaves out the early launch (the peer exchange's kernels).
+__device__ __forceinline__ void wait_for_predecessor_only() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void wait_for_predecessor() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+}
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args) {
