@@ -102,25 +102,42 @@ class PeerExchange:
         self.partials = self.buf[:n_part]
         self.results = self.buf[self.res_off:self.res_off + n_res]
         self.sync = self.buf[self.sync_off:self.sync_off + sync_words].view(torch.int32)
+        # a failure on one rank is agreed on by all before anyone raises, so that every rank takes the same collective steps
+        failure = None
         handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
         offset = ctypes.c_uint64()
-        _lib.check(lib.igs_ipc_export(ptr(self.buf), handle, ctypes.byref(offset)), "igs_ipc_export")
+        try:
+            _lib.check(lib.igs_ipc_export(ptr(self.buf), handle, ctypes.byref(offset)), "igs_ipc_export")
+        except _lib.IgsError as err:
+            failure = err
         mine = torch.tensor(list(bytes(handle)) + list(int(offset.value).to_bytes(8, "little")), dtype=torch.uint8, device=device)
         gathered = [torch.empty_like(mine) for _ in range(self.world)]
         dist.all_gather(gathered, mine, group=group)
         self.opened = []  # (address, offset) of the peers' mapped buffers
         bases = []
-        for q, g in enumerate(gathered):
-            if q == self.rank:
-                bases.append(self.buf.data_ptr())
-                continue
-            raw = bytes(g.cpu().tolist())
-            peer = ctypes.c_void_p()
-            off = int.from_bytes(raw[IPC_HANDLE_BYTES:], "little")
-            _lib.check(lib.igs_ipc_open((ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(raw[:IPC_HANDLE_BYTES]), off,
-                                        ctypes.byref(peer)), "igs_ipc_open")
-            self.opened.append((peer.value, off))
-            bases.append(peer.value)
+        flag = torch.tensor([int(failure is not None)], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, group=group)
+        try:
+            for q, g in enumerate(gathered if int(flag.item()) == 0 else []):
+                if q == self.rank:
+                    bases.append(self.buf.data_ptr())
+                    continue
+                raw = bytes(g.cpu().tolist())
+                peer = ctypes.c_void_p()
+                off = int.from_bytes(raw[IPC_HANDLE_BYTES:], "little")
+                _lib.check(lib.igs_ipc_open((ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(raw[:IPC_HANDLE_BYTES]), off,
+                                            ctypes.byref(peer)), "igs_ipc_open")
+                self.opened.append((peer.value, off))
+                bases.append(peer.value)
+        except _lib.IgsError as err:
+            failure = failure or err
+        flag = torch.tensor([int(failure is not None)], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, group=group)
+        if int(flag.item()) != 0:
+            for address, off in self.opened:
+                lib.igs_ipc_close(ctypes.c_void_p(address), off)
+            self.opened = []
+            raise failure or RuntimeError("the peer exchange could not be set up on another rank")
         arr = ctypes.c_void_p * self.world
         self.partials_ptrs = arr(*bases)
         self.results_ptrs = arr(*[b + 4 * self.res_off for b in bases])
@@ -319,11 +336,16 @@ class BandStep:
             getattr(self, s)()
 
     def check(self):
-        """Raise if a wait of the peer exchange gave up (a rank missing or late by more than the timeout); synchronizes."""
+        """Raise on every rank if a wait of the peer exchange gave up on any rank (a rank missing or late by more than the timeout);
+        collective (the ranks agree before anyone raises, so they keep taking the same collective steps), synchronizes."""
         if self.peer is not None:
-            code = self.peer.error()
-            if code:
-                raise _lib.IgsError(f"band exchange on rank {self.peer.rank}: a wait for the other ranks timed out (code {code})")
+            import torch.distributed as dist
+
+            code = torch.tensor([self.peer.error()], dtype=torch.int32, device=self.device)
+            dist.all_reduce(code, op=dist.ReduceOp.MAX, group=self.peer.group)
+            if int(code.item()):
+                raise _lib.IgsError(f"band exchange: a wait for the other ranks timed out on some rank (code {int(code.item())}; "
+                                    f"rank {self.peer.rank}: {self.peer.error()})")
 
     def _capture(self, stages):
         stream = torch.cuda.Stream(self.device)
