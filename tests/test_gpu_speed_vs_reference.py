@@ -88,3 +88,38 @@ def test_faster_than_reference_kernels(device, ref_module):
     # none may be slower
     for name, (ref_ms, ours_ms) in rows.items():
         assert ours_ms <= ref_ms, f"{name}: ours {ours_ms:.3f} ms, reference {ref_ms:.3f} ms"
+
+
+@pytest.mark.parametrize("name", ["cfg4_2160p", "cfg5_tex9"])
+def test_faster_than_reference_kernels_at_other_sizes(name, device, ref_module):
+    """The top-K operators one to one at 3840x2160 with 80,000 Gaussians and at one 2048x2048 image of 9 channels with 50,000 Gaussians
+    (the reference's 16-value backward path), same inputs for both; ours must not be slower."""
+    wl = workloads.get_workload(name)
+    inp = workloads.make_inputs(wl)
+    d = {k: v.to(device) for k, v in inp.items()}
+    h, w, n = wl.height, wl.width, wl.num_gaussians
+    tb = ops.tile_grid(h, w)
+    xys, radii, conics, hits = ops.project_gaussians_2d_scale_rot_forward(n, d["means"], d["scales"], d["rotations"], h, w, tb)
+    cum = torch.cumsum(hits, dim=0, dtype=torch.int32)
+    total = int(cum[-1].item())
+    ids, bins = ops.sort_intersects_by_tile(n, total, xys, radii, cum, tb)
+    feats = d["features"]
+    _, topk = ops.nd_rasterize_forward_topk_norm(tb, (16, 16, 1), (w, h, 1), ids, bins, xys, conics, feats)
+    v_out = torch.sign(torch.randn(wl.channels, h, w, generator=torch.Generator().manual_seed(2))).to(device) / (wl.channels * h * w)
+    rows = {
+        "top-K forward, [H,W,10] lists": (
+            median_ms(lambda: ref_module.nd_rasterize_forward_topk_norm(tb, (16, 16, 1), (w, h, 1), ids, bins, xys, conics, feats)),
+            median_ms(lambda: ops.nd_rasterize_forward_topk_norm(tb, (16, 16, 1), (w, h, 1), ids, bins, xys, conics, feats))),
+        "top-K backward, [H,W,10] lists": (
+            median_ms(lambda: ref_module.nd_rasterize_backward_topk_norm(h, w, 16, 16, xys, conics, feats, v_out, topk)),
+            median_ms(lambda: ops.nd_rasterize_backward_topk_norm(h, w, 16, 16, xys, conics, feats, v_out, topk))),
+    }
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"])
+    graph = step.capture()
+    ours_step = median_ms(graph.replay)
+    print()
+    print(f"{name:40s} {'reference ms':>13s} {'ours ms':>9s} {'speed-up':>9s}   (our whole step {ours_step:.3f} ms)")
+    for row, (ref_ms, ours_ms) in rows.items():
+        print(f"{row:40s} {ref_ms:13.3f} {ours_ms:9.3f} {ref_ms / ours_ms:8.2f}x")
+    for row, (ref_ms, ours_ms) in rows.items():
+        assert ours_ms <= ref_ms, f"{name} {row}: ours {ours_ms:.3f} ms, reference {ref_ms:.3f} ms"
