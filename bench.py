@@ -526,6 +526,15 @@ def run_step_e2e(args, step, dev_params, inp, device, world, api):
     host = [inp[k].pin_memory() for k in keys]
     dev = list(dev_params)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    if api == "step":
+        # the parameters as the caller keeps them for this API: one pinned host buffer in the step's packed layout, one transfer per step
+        from igs_b200 import pipeline
+
+        offsets, length = pipeline.RasterStep.packed_layout(step.n, step.c)
+        flat_host = torch.zeros(length, dtype=torch.float32).pin_memory()
+        for t, at in zip(host, offsets):
+            flat_host[at:at + t.numel()] = t.reshape(-1)
+        dev, host = [step.pack_inputs()], [flat_host]
 
     def copy_in():
         for d, h in zip(dev, host):
@@ -566,7 +575,8 @@ def run_step_e2e(args, step, dev_params, inp, device, world, api):
             "unit": "steps/s", "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world,
             "api": ("igs_b200.bands.BandStep" if api == "bands" else "igs_b200.pipeline.RasterStep") +
                    " over the C ABI (host parameters copied in and the loss read back every step" +
-                   (", both copies captured in the step's CUDA graph)" if api == "step" else ")")}
+                   (", the parameters as one packed pinned buffer: one copy in and one out per step, both captured in the step's CUDA "
+                    "graph)" if api == "step" else ")")}
 
 
 def run_e2e(args, wl, inp, device, capacity, world, graph=False, routed_l1=False):
@@ -582,17 +592,29 @@ def run_e2e(args, wl, inp, device, capacity, world, graph=False, routed_l1=False
 
     l1_loss = ag._routed_l1_loss if routed_l1 else F.l1_loss
 
-    host = {k: inp[k].pin_memory() for k in ("means", "scales", "rotations", "features")}
+    from igs_b200 import pipeline
+
+    keys = ("means", "scales", "rotations", "features")
     target = (inp["loss_target"] if "loss_target" in inp else inp["target"]).to(device)
-    dev = {k: torch.empty_like(v, device=device).requires_grad_(True) for k, v in host.items()}
+    # the parameters packed as for the C-ABI leg (one pinned host buffer, one copy per step); the leaf tensors autograd sees are
+    # detached views of the device buffer
+    n, c = inp["features"].shape
+    offsets, length = pipeline.RasterStep.packed_layout(n, c)
+    flat_host = torch.zeros(length, dtype=torch.float32).pin_memory()
+    flat_dev = torch.empty(length, dtype=torch.float32, device=device)
+    dev = {}
+    for k, at in zip(keys, offsets):
+        t = inp[k]
+        flat_host[at:at + t.numel()] = t.reshape(-1)
+        dev[k] = flat_dev[at:at + t.numel()].view(t.shape).detach().requires_grad_(True)
+    host = {"packed": flat_host}
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
     tb = wl.tile_bounds
     opts = step_options(wl, device)
 
     def body():
         with torch.no_grad():
-            for k in dev:
-                dev[k].copy_(host[k], non_blocking=True)
+            flat_dev.copy_(flat_host, non_blocking=True)
         means, scales, rots, feats = [dev[k] for k in ("means", "scales", "rotations", "features")]
         raw_feats, raw_rots = feats, rots
         if "quant" in opts:  # model._get_params (model.py:993-1006) and the loss-space features (model.py:963-964)
@@ -657,7 +679,7 @@ def run_e2e(args, wl, inp, device, capacity, world, graph=False, routed_l1=False
                    ("F.l1_loss routed by igs_b200.autograd.install_l1()" if routed_l1 else "F.l1_loss") +
                    (" + igs_b200.autograd.rate_loss" if "rate" in opts else "") + " + backward" +
                    (", copies, forward, loss and backward replayed as one CUDA graph (model.py's graph-captured step)" if graph else
-                    ", eager")}
+                    ", eager") + "; the parameters as one packed pinned buffer, one copy in per step"}
 
 
 def run_aux(args):

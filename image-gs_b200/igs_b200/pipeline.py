@@ -226,6 +226,34 @@ class RasterStep:
     def kernels_per_step(self):
         return sum(self.KERNELS[s] for s in self.STAGES)
 
+    PACK_ALIGN = 64  # floats: each parameter array of the packed buffer starts on a 256-byte boundary
+
+    @classmethod
+    def packed_layout(cls, n, c):
+        """Offsets (in floats) of means [N,2], scales [N,2], rotations [N,1], features [N,C] in the packed buffer, and its length."""
+        offsets, at = [], 0
+        for size in (2 * n, 2 * n, n, c * n):
+            offsets.append(at)
+            at += -(-size // cls.PACK_ALIGN) * cls.PACK_ALIGN
+        return offsets, at
+
+    def pack_inputs(self):
+        """Move the four parameter arrays (means, scales, rotations, features; values kept) into one device buffer laid out as
+        packed_layout(), so that a caller holding its parameters on the host copies a step's inputs in with one transfer of that buffer.
+        Returns the buffer. Graphs captured afterwards read the packed arrays; graphs captured before keep the old ones."""
+        offsets, length = self.packed_layout(self.n, self.c)
+        flat = torch.empty(length, device=self.device, dtype=torch.float32)
+        views = []
+        for t, at in zip(self.raw, offsets):
+            v = flat[at:at + t.numel()].view(t.shape)
+            v.copy_(t)
+            views.append(v)
+        self.raw = tuple(views)
+        if self.quant is None:
+            self.means, self.scales, self.rotations, self.features = views
+        self.graph = None
+        return flat
+
     def capture(self, stages=None, before=None, after=None):
         """A CUDA graph of the step (or of the given stages); before() and after() issue extra work around them on the same stream (for
         example the copies of pinned host parameters in and of the loss out, which then run as nodes of the graph)."""

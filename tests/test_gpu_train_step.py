@@ -76,3 +76,31 @@ def test_fused_band_step_equals_the_band_calls(rows):
     for k in ("p_xy", "p_conic", "p_colors"):
         assert_close_grad(fused[k], staged[k], what=k)
     assert abs(float(fused["p_loss"]) - float(staged["p_loss"])) <= 2e-6 * max(abs(float(staged["p_loss"])), 1e-12)
+
+
+def test_packed_inputs_give_the_same_step():
+    """RasterStep.pack_inputs(): the parameters moved into one buffer in packed_layout() (one host-to-device copy per step for a
+    caller keeping them on the host) give the same step bit for bit, and a write to the buffer is what the next step reads."""
+    from igs_b200 import pipeline
+
+    wl, inp = make_case(96, 128, 500, c=3, seed=8)
+    d = to_dev(inp, DEV)
+    step = pipeline.RasterStep(d["means"], d["scales"], d["rotations"], d["features"], d["target"], capacity=64 * 500)
+    step.replay()
+    torch.cuda.synchronize()
+    before = snapshot(step, EXACT + ("loss",))
+    flat = step.pack_inputs()
+    offsets, length = pipeline.RasterStep.packed_layout(step.n, step.c)
+    assert flat.numel() == length and all(o % pipeline.RasterStep.PACK_ALIGN == 0 for o in offsets)
+    for t, at in zip((d["means"], d["scales"], d["rotations"], d["features"]), offsets):
+        assert torch.equal(flat[at:at + t.numel()].view(t.shape), t)
+    step.replay()  # captured again over the packed arrays
+    torch.cuda.synchronize()
+    after = snapshot(step, EXACT + ("loss",))
+    for k in EXACT:
+        assert torch.equal(before[k], after[k]), k
+    assert float(before["loss"]) == float(after["loss"])
+    flat[offsets[3]:offsets[3] + 3 * step.n].zero_()  # black features: a black image
+    step.replay()
+    torch.cuda.synchronize()
+    assert float(step.image.abs().max()) == 0.0
