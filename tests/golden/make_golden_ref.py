@@ -5,7 +5,7 @@ nd_rasterize_forward_topk_norm -> L1 gradient -> nd_rasterize_backward_topk_norm
 Small cases are stored whole (the L1 gradient is recomputed by the tests from image and target); large ones as SHA-256 digests of the
 integer outputs, 16x512 crops of the image and top-K lists, the first 1000 Gaussians' values and summary statistics.
 
-Usage (on a GPU machine with oracle/_ref built): python tests/golden/make_golden_ref.py OUT_DIR
+Usage (on a GPU machine with oracle/_ref built): python tests/golden/make_golden_ref.py [OUT_DIR, default tests/golden]
 """
 import math
 import os
@@ -92,4 +92,4 @@ def main(out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden"))
+    main(sys.argv[1] if len(sys.argv) > 1 else HERE)
