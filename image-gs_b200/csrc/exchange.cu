@@ -5,9 +5,10 @@
 // all-reduce followed by every rank repeating the projection backward on all N Gaussians, each rank takes one share of the Gaussians:
 //   band_reduce_kernel: announce "my partials are complete" to every rank, wait for every rank's announcement, then for each Gaussian of
 //                       this rank's share read its partials from every rank's memory (plain peer loads), add them in rank order, run the
-//                       projection backward and store the results into every rank's results buffer (plain peer stores);
-//   band_done_kernel:   announce "my share is written" to every rank, wait for every rank's announcement; the results buffer is then
-//                       complete on this rank.
+//                       projection backward and store the results into every rank's results buffer (plain peer stores); the last of
+//                       its blocks to finish (a ticket in the rank's own words) announces "my share is written" to every rank and waits
+//                       for every rank's announcement: the results buffer is then complete on this rank. One kernel per step; no block
+//                       waits for another block of its own launch.
 // Per rank and step this moves (world - 1) / world of the partials in and of the results out over NVLink, with two rank-wide waits. The
 // sums are formed by one rank each in a fixed order, so every rank holds bit-identical gradients.
 //
@@ -36,7 +37,8 @@ struct SyncWords {
     unsigned done[kMaxRanks];
     unsigned step;
     unsigned error;
-    unsigned pad[IGS_BAND_SYNC_WORDS - 2 * kMaxRanks - 2];
+    unsigned ticket;  // blocks of this rank's band_reduce_kernel that have finished this step (this rank's own; zero between steps)
+    unsigned pad[IGS_BAND_SYNC_WORDS - 2 * kMaxRanks - 3];
 };
 static_assert(sizeof(SyncWords) == IGS_BAND_SYNC_WORDS * sizeof(unsigned), "sync word layout");
 static_assert(offsetof(SyncWords, step) == IGS_BAND_SYNC_STEP * sizeof(unsigned), "sync word layout");
@@ -92,8 +94,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // words reaches `value`. One thread. Returns false (and records `code` in the error word) past the deadline.
 __device__ bool announce_and_wait(const Peers &peers, const int world, const int rank, const bool done_words, const unsigned value,
                                   const unsigned long long timeout_ns, const unsigned code) {
-    // No fence before the flags: what they announce was written by kernels that have completed (the band's raster step before
-    // band_reduce_kernel; band_reduce_kernel, whose blocks each end with a release fence, before band_done_kernel)
+    // No fence here: what the ready flags announce was written by kernels that have completed (the band's raster step), and the
+    // done flags are announced by band_reduce_kernel's last block after the fences that order every block's stores before them
     for (int q = 0; q < world; ++q) {
         SyncWords *w = peers.sync[q];
         store_relaxed_sys(done_words ? &w->done[rank] : &w->ready[rank], value);
@@ -168,12 +170,11 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
         s_go = go ? 1 : 0;
     }
     __syncthreads();
-    if (!s_go) return;
 
     const size_t nn = (size_t)n;
     const ResultsLayout out(nn, channels);
     const int g = share_begin + blockIdx.x * kThreads + threadIdx.x;
-    if (g < share_end) {
+    if (s_go && g < share_end) {
         // the sums in rank order (the same on every rank: each Gaussian is summed by one rank only)
         float vxy[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[kMaxC];
 #pragma unroll
@@ -202,26 +203,29 @@ __global__ void __launch_bounds__(kThreads) band_reduce_kernel(const Peers peers
                 if (c < channels) r[out.colors + (size_t)g * channels + c] = vcol[c];
         }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (s_go && blockIdx.x == 0 && threadIdx.x == 0) {
         // the loss: every rank adds the partial losses in rank order into its own results
         float loss = 0.f;
         for (int q = 0; q < world; ++q) loss += load_peer(peers.partials[q] + (5 + (size_t)channels) * nn);
         peers.results[rank][out.loss] = loss;
     }
-    // the block's peer stores are performed at system scope before it ends, so before the done announcement (band_done_kernel, next):
-    // the barrier orders every thread's stores before thread 0's fence, which is cumulative over them
+    // The block's peer stores are performed at system scope before its ticket: the barrier orders every thread's stores before thread
+    // 0's fence, which is cumulative over them. Every block takes a ticket (also one that did nothing after a failed wait), and the
+    // last one, after a fence that orders the others' fenced stores before its own operations, announces "share written" to every
+    // rank and waits for every rank's announcement, then counts the step.
     __syncthreads();
-    if (threadIdx.x == 0) fence_acq_rel_sys();
-}
-
-__global__ void __launch_bounds__(32) band_done_kernel(const Peers peers, const int world, const int rank,
-                                                       const unsigned long long timeout_ns) {
-    igs::wait_for_predecessor_only();  // band_reduce_kernel has completed: this rank's share is stored everywhere
-    if (threadIdx.x != 0) return;
-    SyncWords *me = peers.sync[rank];
-    if (atomicOr(&me->error, 0u) != 0u) return;
-    const unsigned value = *(volatile unsigned *)&me->step + 1u;
-    if (announce_and_wait(peers, world, rank, true, value, timeout_ns, IGS_BAND_TIMEOUT_DONE)) *(volatile unsigned *)&me->step = value;
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        if (atomicAdd(&me->ticket, 1u) == gridDim.x - 1) {
+            fence_acq_rel_sys();
+            me->ticket = 0u;  // every block of this step has taken its ticket
+            if (atomicOr(&me->error, 0u) == 0u) {
+                const unsigned value = *(volatile unsigned *)&me->step + 1u;
+                if (announce_and_wait(peers, world, rank, true, value, timeout_ns, IGS_BAND_TIMEOUT_DONE))
+                    *(volatile unsigned *)&me->step = value;
+            }
+        }
+    }
 }
 
 using GetAddressRange = int (*)(unsigned long long *base, size_t *size, unsigned long long dptr);
@@ -311,7 +315,6 @@ int igs_band_reduce(int world, int rank, int num_points, int channels, const flo
     const auto kernel = channels <= 4 ? band_reduce_kernel<4> : band_reduce_kernel<igs::kMaxChannels>;
     igs::launch(kernel, blocks, kThreads, 0, s, peers, world, rank, num_points, channels, share_begin, share_end,
                 reinterpret_cast<const float2 *>(scales2d), rotation, (float)img_width, (float)img_height, radii, conics, timeout_ns);
-    igs::launch(band_done_kernel, 1, 32, 0, s, peers, world, rank, timeout_ns);
     return igs::check_launch(who);
 }
 

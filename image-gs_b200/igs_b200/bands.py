@@ -312,7 +312,7 @@ class BandStep:
         self.peer.reduce(self.scales, self.rotations, self.h, self.w, self.radii, self.conics, self._stream())
 
     KERNELS = {"_project": 2, "_cumsum": 2, "_bin": 4, "_raster": 2, "_forward": 2, "_backward": 1, "_project_backward": 1,
-               "_exchange": 2, "_train_step": 8}
+               "_exchange": 1, "_train_step": 8}
 
     @property
     def LOCAL(self):
