@@ -4,7 +4,7 @@ Gaussians, bins and renders only its rows, takes the L1 loss and its gradient on
 and runs the backward pass for its band. The partial gradients with respect to the projected Gaussians (v_xy, v_conic, v_colors:
 N (5 + C) floats, 2.6 MB at 80,000 Gaussians) and the partial loss are then combined in one of two ways:
   * exchange="peer" (PeerExchange, igs_band_reduce): over peer memory, each rank sums one share of the Gaussians' partials from every
-    rank, runs the projection backward on that share and stores the parameter gradients into every rank's results; two kernels, no
+    rank, runs the projection backward on that share and stores the parameter gradients into every rank's results; one kernel, no
     collective library, and the whole step is one CUDA graph;
   * exchange="nccl": one NCCL all-reduce of the partials, after which every rank runs the projection backward on all Gaussians.
 Either way all ranks hold the same parameter gradients.
