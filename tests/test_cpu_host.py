@@ -107,3 +107,18 @@ def test_rate_model_install_replaces_and_restores(monkeypatch):
     rate_model.restore(again)
     rate_model.restore(replaced)
     assert (fake.rate_model, fake.bitstream_neighbors) == originals
+
+
+@pytest.mark.parametrize("n,c", [(1, 1), (20000, 3), (50000, 9), (63, 12)])
+def test_packed_parameter_layout(n, c):
+    """RasterStep.packed_layout: means, scales, rotations, features back to back, each on a 256-byte boundary, in a buffer that holds
+    them all and no more than the alignment padding."""
+    from igs_b200 import pipeline
+
+    offsets, length = pipeline.RasterStep.packed_layout(n, c)
+    sizes = (2 * n, 2 * n, n, c * n)
+    align = pipeline.RasterStep.PACK_ALIGN
+    assert offsets[0] == 0 and all(o % align == 0 for o in offsets) and align * 4 % 256 == 0
+    for k in range(3):
+        assert offsets[k] + sizes[k] <= offsets[k + 1] < offsets[k] + sizes[k] + align
+    assert offsets[3] + sizes[3] <= length < offsets[3] + sizes[3] + align
