@@ -156,7 +156,19 @@ __global__ void __launch_bounds__(256) project_bwd_kernel(const int n, const flo
         // the training step's loss from the raster kernel's per-tile partial sums, in a fixed order: ratio * (sum) / numel
         __shared__ float warp_sums[8];
         float sum = 0.f;
-        for (int t = threadIdx.x; t < finish.count; t += 256) sum += __ldg(&finish.partials[t]);
+        int t0 = 0;
+        if ((reinterpret_cast<uintptr_t>(finish.partials) & 15) == 0) {
+            // four partials per load, several loads in flight per thread (the sum's order stays fixed)
+            const float4 *p4 = reinterpret_cast<const float4 *>(finish.partials);
+            const int n4 = finish.count / 4;
+#pragma unroll 4
+            for (int t = threadIdx.x; t < n4; t += 256) {
+                const float4 v = __ldg(&p4[t]);
+                sum += (v.x + v.y) + (v.z + v.w);
+            }
+            t0 = 4 * n4;
+        }
+        for (int t = t0 + threadIdx.x; t < finish.count; t += 256) sum += __ldg(&finish.partials[t]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = sum;
