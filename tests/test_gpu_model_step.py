@@ -3,7 +3,7 @@ Image-GS's CUDA-graph training step (the protocol of model.py's _capture_step, m
 the model optimises positions in [0, 1), inverse scales, rotations and features with Adam; one eager step runs on a side stream, then the
 next step is captured into a CUDA graph with its own memory pool (torch.cuda.graph_pool_handle): forward as model.forward calls it
 (project_gaussians_2d_scale_rot, then rasterize_gaussians_sum with topk_norm=True and a fixed intersection capacity of twice the current
-count, model.py:966-975), F.l1_loss, backward and the optimizer step. The graph is replayed; at every replay the gradients it computed
+count, model.py:966-975), F.l1_loss (ATen's, or the library's as install_l1() routes it), backward and the optimizer step. The graph is replayed; at every replay the gradients it computed
 must equal those of an eager forward and backward at the same parameters (float atomics reorder sums: the gradient tolerance), and the
 optimizer step inside the graph must move the parameters. The first eager step's gradients are checked against the oracle's step.
 """
@@ -18,25 +18,28 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-def loss_of(params, h, w, target, capacity):
+def loss_of(params, h, w, target, capacity, routed=False):
     import gsplat
+    from igs_b200 import autograd as ag
     from igs_b200 import ops
 
     xy, inv_scale, rot, feat = params
     xys, radii, conics, hits = gsplat.project_gaussians_2d_scale_rot(xy, 1.0 / inv_scale, rot, h, w, ops.tile_grid(h, w))
     img = gsplat.rasterize_gaussians_sum(xys, radii, conics, hits, feat, h, w, 16, 16, topk_norm=True, capacity=capacity)
     img = img.view(-1, h, w, feat.shape[1]).permute(0, 3, 1, 2).contiguous().squeeze(0)
-    return F.l1_loss(img, target), hits
+    l1_loss = ag._routed_l1_loss if routed else F.l1_loss  # routed: model.py's F.l1_loss after igs_b200.autograd.install_l1()
+    return l1_loss(img, target), hits
 
 
-def eager_grads(values, h, w, target):
+def eager_grads(values, h, w, target, routed=False):
     params = [v.clone().requires_grad_(True) for v in values]
-    loss, _ = loss_of(params, h, w, target, None)
+    loss, _ = loss_of(params, h, w, target, None, routed)
     loss.backward()
     return [p.grad for p in params], float(loss)
 
 
-def test_graph_captured_training_step_through_dropin():
+@pytest.mark.parametrize("routed", [False, True])
+def test_graph_captured_training_step_through_dropin(routed):
     from oracle import cpu as orc
 
     wl, inp = make_case(112, 144, 600, seed=29)
@@ -51,7 +54,7 @@ def test_graph_captured_training_step_through_dropin():
     side.wait_stream(torch.cuda.current_stream(DEV))
     with torch.cuda.stream(side):
         opt.zero_grad()
-        loss, hits = loss_of(params, h, w, target, None)
+        loss, hits = loss_of(params, h, w, target, None, routed)
         loss.backward()
         first = [p.grad.clone() for p in params]
         opt.step()
@@ -75,7 +78,7 @@ def test_graph_captured_training_step_through_dropin():
     torch.cuda.synchronize()
     with torch.cuda.stream(side):
         graph.capture_begin(pool=pool)
-        g_loss, _ = loss_of(params, h, w, target, capacity)
+        g_loss, _ = loss_of(params, h, w, target, capacity, routed)
         g_loss.backward()
         opt.step()
         graph.capture_end()
@@ -85,7 +88,7 @@ def test_graph_captured_training_step_through_dropin():
         before = [p.detach().clone() for p in params]
         graph.replay()
         torch.cuda.synchronize()
-        want, want_loss = eager_grads(before, h, w, target)
+        want, want_loss = eager_grads(before, h, w, target, routed)
         assert abs(float(g_loss) - want_loss) <= 2e-6 * want_loss
         for p, g, name in zip(params, want, ("xy", "inv_scale", "rot", "feat")):
             assert_close_grad(p.grad, g, what=f"graph-replayed {name} gradient")
